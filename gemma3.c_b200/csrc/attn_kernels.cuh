@@ -1,0 +1,848 @@
+// attn_kernels.cuh - the device side of the gemma3.c attention hot path.
+//
+//   prologue_*        per-head QK-RMSNorm (gemma3_kernels.c:289-304), RoPE
+//                     from the uploaded table (gemma3_kernels.c:470-484) and
+//                     the KV-cache append (gemma3_transformer.c:236-251),
+//                     fused into one pass over the token's q/k/v rows;
+//   decode_splitkv    GQA decode over the cache (gemma3_kernels.c:527-597):
+//                     one CTA per (sequence, kv head, key range), both query
+//                     heads of the group share every K/V row, 16-byte
+//                     coalesced bulk-copied rows, warp-shuffle reductions,
+//                     online softmax in the log2 domain;
+//   merge_partials    log-sum-exp merge of the (m, l, O) partials;
+//   prefill_fa_sm100  causal / sliding-window flash attention for prefill on
+//                     the 5th-generation tensor core: TMA-staged K/V tiles,
+//                     tcgen05.mma (bf16 x bf16 -> fp32) into TMEM, online
+//                     softmax by four warps, P staged through shared memory.
+//
+// Device KV-cache layout (per layer): [seq][K|V][kv_head][row][256] in the
+// cache dtype (fp32 or bf16), rows = max_context (global layer, or this
+// rank's shard of it) or 1024 (local ring).  Each (seq, K|V, head) plane is
+// contiguous, so a run of rows is one linear bulk copy and one TMA box.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <climits>
+#include <cstdint>
+
+#include "sm100_ptx.cuh"
+
+namespace g3 {
+
+constexpr int kHeads = 8;
+constexpr int kKvHeads = 4;
+constexpr int kHeadDim = 256;
+constexpr int kWindow = 1024;
+constexpr int kMaxDecodeBatch = 256;
+// softmax(x/16) evaluated as 2^(x * log2(e)/16)
+constexpr float kScaleLog2 = 0.0901684400555602f;
+
+template <typename T>
+struct KvType;
+template <>
+struct KvType<float> {
+    __device__ static __forceinline__ float to_f(float x) { return x; }
+    __device__ static __forceinline__ float from_f(float x) { return x; }
+};
+template <>
+struct KvType<__nv_bfloat16> {
+    __device__ static __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+    __device__ static __forceinline__ __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
+};
+
+__device__ __forceinline__ float bf16_bits_to_f(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }
+
+// Block-wide sum over the 128 threads of a prologue block.
+__device__ __forceinline__ float block128_sum(float v, float *red) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    float s = red[0] + red[1] + red[2] + red[3];
+    __syncthreads();
+    return s;
+}
+
+// One 256-wide head row: thread i (of 128) holds the rotate-half pair
+// (x[i], x[i+128]).  Applies RMSNorm with the (1+w) gain when w != null,
+// then RoPE at the given table row.
+__device__ __forceinline__ void norm_rope_pair(float &a, float &b, const uint16_t *w, float eps,
+                                               const float *rope_row, float *red) {
+    const int i = threadIdx.x;
+    if (w) {
+        float ss = block128_sum(a * a + b * b, red);
+        float r = 1.0f / sqrtf(ss / (float)kHeadDim + eps);
+        a = a * r * (1.0f + bf16_bits_to_f(w[i]));
+        b = b * r * (1.0f + bf16_bits_to_f(w[i + 128]));
+    }
+    const float c = rope_row[2 * i], s = rope_row[2 * i + 1];
+    const float x0 = a, x1 = b;
+    a = x0 * c - x1 * s;
+    b = x0 * s + x1 * c;
+}
+
+struct LayerDev {
+    void *kv;          // cache base of the layer
+    int rows;          // rows per (seq, head) plane
+    int is_global;
+    int shard_lo;      // first position held (global layers; 0 otherwise)
+    int shard_hi;      // one past the last position held
+    const uint16_t *qn;  // QK-norm gains or null
+    const uint16_t *kn;
+    const float *rope;   // [max_pos][128][2]
+};
+
+template <typename KVT>
+__device__ __forceinline__ KVT *plane(const LayerDev &L, int seq, int kv_sel, int head) {
+    return reinterpret_cast<KVT *>(L.kv) + (((size_t)seq * 2 + kv_sel) * kKvHeads + head) * (size_t)L.rows * kHeadDim;
+}
+
+// Cache row of position pos, or -1 if this context does not hold it
+// (gemma3_transformer.c:240-248: global append at pos, local ring pos%1024).
+__device__ __forceinline__ int cache_row(const LayerDev &L, int pos) {
+    if (!L.is_global) return pos % kWindow;
+    if (pos < L.shard_lo || pos >= L.shard_hi) return -1;
+    return pos - L.shard_lo;
+}
+
+// ------------------------------------------------------------------------
+// Decode prologue: grid (B, 16); y<8 query head, 8..11 key head, 12..15
+// value head.  q goes to qout [B][8][256] fp32 (already scaled by
+// log2(e)/16 for the exp2 softmax); k and v are appended to the cache.
+// ------------------------------------------------------------------------
+struct DecodeBatch {
+    int B;
+    int seq[kMaxDecodeBatch];
+    int pos[kMaxDecodeBatch];
+};
+
+template <typename KVT>
+__global__ void __launch_bounds__(128) prologue_decode(const float *__restrict__ Q, const float *__restrict__ K,
+                                                       const float *__restrict__ V, LayerDev L, float eps,
+                                                       const __grid_constant__ DecodeBatch batch,
+                                                       float *__restrict__ qout) {
+    __shared__ float red[4];
+    const int b = blockIdx.x, y = blockIdx.y, i = threadIdx.x;
+    const int pos = batch.pos[b], seq = batch.seq[b];
+    const float *rope_row = L.rope + (size_t)pos * kHeadDim;
+    if (y < kHeads) {
+        const float *x = Q + (size_t)b * kHeads * kHeadDim + y * kHeadDim;
+        float a = x[i], c = x[i + 128];
+        norm_rope_pair(a, c, L.qn && L.kn ? L.qn : nullptr, eps, rope_row, red);
+        float *o = qout + ((size_t)b * kHeads + y) * kHeadDim;
+        o[i] = a * kScaleLog2;
+        o[i + 128] = c * kScaleLog2;
+        return;
+    }
+    const int row = cache_row(L, pos);
+    if (y < kHeads + kKvHeads) {
+        const int h = y - kHeads;
+        const float *x = K + (size_t)b * kKvHeads * kHeadDim + h * kHeadDim;
+        float a = x[i], c = x[i + 128];
+        norm_rope_pair(a, c, L.qn && L.kn ? L.kn : nullptr, eps, rope_row, red);
+        if (row >= 0) {
+            KVT *dst = plane<KVT>(L, seq, 0, h) + (size_t)row * kHeadDim;
+            dst[i] = KvType<KVT>::from_f(a);
+            dst[i + 128] = KvType<KVT>::from_f(c);
+        }
+    } else {
+        const int h = y - kHeads - kKvHeads;
+        const float *x = V + (size_t)b * kKvHeads * kHeadDim + h * kHeadDim;
+        if (row >= 0) {
+            KVT *dst = plane<KVT>(L, seq, 1, h) + (size_t)row * kHeadDim;
+            dst[i] = KvType<KVT>::from_f(x[i]);
+            dst[i + 128] = KvType<KVT>::from_f(x[i + 128]);
+        }
+    }
+}
+
+// ------------------------------------------------------------------------
+// Prefill prologue: grid (T, 16).  q -> qst bf16 [8][T][256]; k, v ->
+// cache (cache dtype) and, when `kst` is set, the bf16 linear staging
+// [4][st_rows][256] at row pos - kv_pos0.  On a local layer only the last
+// 1024 tokens are written into the ring (earlier ones would be overwritten
+// by later tokens of the same call anyway).
+// ------------------------------------------------------------------------
+template <typename KVT>
+__global__ void __launch_bounds__(128) prologue_prefill(const float *__restrict__ Q, const float *__restrict__ K,
+                                                        const float *__restrict__ V, LayerDev L, float eps, int seq,
+                                                        int T, int start_pos, int kv_pos0,
+                                                        __nv_bfloat16 *__restrict__ qst,
+                                                        __nv_bfloat16 *__restrict__ kst,
+                                                        __nv_bfloat16 *__restrict__ vst, int st_rows) {
+    __shared__ float red[4];
+    const int t = blockIdx.x, y = blockIdx.y, i = threadIdx.x;
+    const int pos = start_pos + t;
+    const float *rope_row = L.rope + (size_t)pos * kHeadDim;
+    if (y < kHeads) {
+        const float *x = Q + (size_t)t * kHeads * kHeadDim + y * kHeadDim;
+        float a = x[i], c = x[i + 128];
+        norm_rope_pair(a, c, L.qn && L.kn ? L.qn : nullptr, eps, rope_row, red);
+        __nv_bfloat16 *o = qst + ((size_t)y * T + t) * kHeadDim;
+        o[i] = __float2bfloat16_rn(a);
+        o[i + 128] = __float2bfloat16_rn(c);
+        return;
+    }
+    const bool ring_ok = L.is_global || (pos >= start_pos + T - kWindow);
+    const int row = ring_ok ? cache_row(L, pos) : -1;
+    const int srow = pos - kv_pos0;
+    float a, c;
+    int h, sel;
+    if (y < kHeads + kKvHeads) {
+        h = y - kHeads;
+        sel = 0;
+        const float *x = K + (size_t)t * kKvHeads * kHeadDim + h * kHeadDim;
+        a = x[i];
+        c = x[i + 128];
+        norm_rope_pair(a, c, L.qn && L.kn ? L.kn : nullptr, eps, rope_row, red);
+    } else {
+        h = y - kHeads - kKvHeads;
+        sel = 1;
+        const float *x = V + (size_t)t * kKvHeads * kHeadDim + h * kHeadDim;
+        a = x[i];
+        c = x[i + 128];
+    }
+    if (row >= 0) {
+        KVT *dst = plane<KVT>(L, seq, sel, h) + (size_t)row * kHeadDim;
+        dst[i] = KvType<KVT>::from_f(a);
+        dst[i + 128] = KvType<KVT>::from_f(c);
+    }
+    if (kst) {
+        __nv_bfloat16 *s = (sel ? vst : kst) + ((size_t)h * st_rows + srow) * kHeadDim;
+        s[i] = __float2bfloat16_rn(a);
+        s[i + 128] = __float2bfloat16_rn(c);
+    }
+}
+
+// Copies the cached rows of positions [kv_pos0, start_pos) into the bf16
+// staging buffer (rows 0..).  grid (n_rows, 2*4), block 32: each thread moves
+// 8 elements.
+template <typename KVT>
+__global__ void __launch_bounds__(32) stage_prefix(LayerDev L, int seq, int kv_pos0, __nv_bfloat16 *__restrict__ kst,
+                                                   __nv_bfloat16 *__restrict__ vst, int st_rows) {
+    const int r = blockIdx.x, sel = blockIdx.y >> 2, h = blockIdx.y & 3;
+    const int pos = kv_pos0 + r;
+    const int row = cache_row(L, pos);
+    const KVT *src = plane<KVT>(L, seq, sel, h) + (size_t)row * kHeadDim;
+    __nv_bfloat16 *dst = (sel ? vst : kst) + ((size_t)h * st_rows + r) * kHeadDim;
+    const int d = threadIdx.x * 8;
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+        w[j] = pack_bf16x2(KvType<KVT>::to_f(src[d + 2 * j]), KvType<KVT>::to_f(src[d + 2 * j + 1]));
+    *reinterpret_cast<uint4 *>(dst + d) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// ------------------------------------------------------------------------
+// Split-KV decode.
+// grid (nsplit, 4 kv heads, B), block 256 (8 warps).  The CTA streams rows
+// [split*chunk, min(nrows, (split+1)*chunk)) of its (seq, kv head) K and V
+// planes through an NS-stage shared-memory ring filled by 1-D bulk copies
+// (one per plane per tile: the rows are contiguous).  Warp w takes rows
+// w, w+8, ... of each tile; each lane owns 8 of the 256 dims (16 bytes of a
+// bf16 row: fully coalesced, conflict-free shared loads).  Both query heads
+// of the GQA group are scored against every row.
+// ------------------------------------------------------------------------
+struct DecodeParams {
+    const float *q;        // [B][8][256], pre-scaled by log2(e)/16
+    LayerDev L;
+    int chunk;             // rows per split (multiple of the tile)
+    int nsplit;
+    float *partial;        // [B][8][nsplit][258] when write_partial
+    float *out;            // [B][2048] when !write_partial
+    int write_partial;
+    unsigned *err;
+};
+struct DecodeRows {
+    int B;
+    int seq[kMaxDecodeBatch];
+    int nrows[kMaxDecodeBatch];  // rows attended in this context's planes
+};
+
+template <typename KVT>
+struct DecodeCfg;
+template <>
+struct DecodeCfg<__nv_bfloat16> {
+    static constexpr int TK = 32;  // rows per tile (16 KB per plane)
+    static constexpr int NS = 3;
+};
+template <>
+struct DecodeCfg<float> {
+    static constexpr int TK = 16;  // rows per tile (16 KB per plane)
+    static constexpr int NS = 3;
+};
+
+// Lane `lane` owns 8 dims of a row.  bf16: dims 8*lane..8*lane+7 (one 16-B
+// chunk).  fp32: dims 4*lane..+3 and 128+4*lane..+3 (two 16-B chunks, each
+// warp-contiguous).
+template <typename KVT>
+__device__ __forceinline__ int lane_dim(int lane, int j);
+template <>
+__device__ __forceinline__ int lane_dim<__nv_bfloat16>(int lane, int j) { return 8 * lane + j; }
+template <>
+__device__ __forceinline__ int lane_dim<float>(int lane, int j) { return (j < 4 ? 4 * lane + j : 128 + 4 * lane + j - 4); }
+
+template <typename KVT>
+__device__ __forceinline__ void load_row8(const KVT *row, int lane, float (&x)[8]);
+template <>
+__device__ __forceinline__ void load_row8<__nv_bfloat16>(const __nv_bfloat16 *row, int lane, float (&x)[8]) {
+    uint4 u = *reinterpret_cast<const uint4 *>(row + 8 * lane);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        x[2 * j] = __uint_as_float(w[j] << 16);
+        x[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+    }
+}
+template <>
+__device__ __forceinline__ void load_row8<float>(const float *row, int lane, float (&x)[8]) {
+    float4 a = *reinterpret_cast<const float4 *>(row + 4 * lane);
+    float4 b = *reinterpret_cast<const float4 *>(row + 128 + 4 * lane);
+    x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+    x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+}
+
+template <typename KVT>
+__global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, const __grid_constant__ DecodeRows rows) {
+    constexpr int TK = DecodeCfg<KVT>::TK;
+    constexpr int NS = DecodeCfg<KVT>::NS;
+    constexpr int RW = TK / 8;  // rows per warp per tile
+    constexpr uint32_t kPlaneTile = TK * kHeadDim * sizeof(KVT);
+    extern __shared__ __align__(128) unsigned char smem[];
+    KVT *kbuf = reinterpret_cast<KVT *>(smem);
+    KVT *vbuf = reinterpret_cast<KVT *>(smem + NS * kPlaneTile);
+    __shared__ uint64_t full[NS], empty[NS];
+    __shared__ float wm[8][2], wl[8][2];
+    __shared__ int s_abort;
+
+    const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int seq = rows.seq[b];
+    const int n = rows.nrows[b];
+    const int r0 = split * p.chunk;
+    const int r1 = min(n, r0 + p.chunk);
+    const int ntiles = r1 > r0 ? (r1 - r0 + TK - 1) / TK : 0;
+
+    const KVT *Kp = plane<KVT>(p.L, seq, 0, g) + (size_t)r0 * kHeadDim;
+    const KVT *Vp = plane<KVT>(p.L, seq, 1, g) + (size_t)r0 * kHeadDim;
+
+    if (threadIdx.x == 0) {
+        s_abort = 0;
+        for (int s = 0; s < NS; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 8);
+        }
+        fence_mbar_init();
+    }
+    __syncthreads();
+
+    auto issue = [&](int i) {
+        const int s = i % NS;
+        const int nr = min(TK, r1 - (r0 + i * TK));
+        const uint32_t bytes = (uint32_t)nr * kHeadDim * sizeof(KVT);
+        mbar_expect_tx(&full[s], 2 * bytes);
+        bulk_g2s(kbuf + (size_t)s * TK * kHeadDim, Kp + (size_t)i * TK * kHeadDim, bytes, &full[s]);
+        bulk_g2s(vbuf + (size_t)s * TK * kHeadDim, Vp + (size_t)i * TK * kHeadDim, bytes, &full[s]);
+    };
+    if (threadIdx.x == 0)
+        for (int i = 0; i < NS && i < ntiles; ++i) issue(i);
+
+    // Query rows of the two heads sharing kv head g, the lane's 8 dims.
+    float q0[8], q1[8];
+    {
+        const float *qa = p.q + ((size_t)b * kHeads + 2 * g) * kHeadDim;
+        const float *qb = qa + kHeadDim;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            q0[j] = qa[lane_dim<KVT>(lane, j)];
+            q1[j] = qb[lane_dim<KVT>(lane, j)];
+        }
+    }
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
+    float o0[8], o1[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o0[j] = o1[j] = 0.f;
+
+    for (int i = 0; i < ntiles; ++i) {
+        const int s = i % NS;
+        if (!mbar_wait(&full[s], (i / NS) & 1, p.err)) {
+            s_abort = 1;
+            break;
+        }
+        if (s_abort) break;
+        const int nr = min(TK, r1 - (r0 + i * TK));
+        const KVT *kt = kbuf + (size_t)s * TK * kHeadDim;
+        const KVT *vt = vbuf + (size_t)s * TK * kHeadDim;
+        float sc0[RW], sc1[RW];
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            const int row = warp + 8 * r;
+            float k[8];
+            if (row < nr) {
+                load_row8<KVT>(kt + (size_t)row * kHeadDim, lane, k);
+            } else {
+#pragma unroll
+                for (int j = 0; j < 8; ++j) k[j] = 0.f;
+            }
+            float a = 0.f, c = 0.f;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                a = fmaf(q0[j], k[j], a);
+                c = fmaf(q1[j], k[j], c);
+            }
+            sc0[r] = a;
+            sc1[r] = c;
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+            for (int r = 0; r < RW; ++r) {
+                sc0[r] += __shfl_xor_sync(0xffffffffu, sc0[r], o);
+                sc1[r] += __shfl_xor_sync(0xffffffffu, sc1[r], o);
+            }
+        }
+        float mx0 = m0, mx1 = m1;
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            if (warp + 8 * r < nr) {
+                mx0 = fmaxf(mx0, sc0[r]);
+                mx1 = fmaxf(mx1, sc1[r]);
+            }
+        }
+        const float al0 = ex2_approx(m0 - mx0), al1 = ex2_approx(m1 - mx1);
+        m0 = mx0;
+        m1 = mx1;
+        l0 *= al0;
+        l1 *= al1;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            o0[j] *= al0;
+            o1[j] *= al1;
+        }
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            const int row = warp + 8 * r;
+            if (row < nr) {
+                const float p0 = ex2_approx(sc0[r] - m0), p1 = ex2_approx(sc1[r] - m1);
+                l0 += p0;
+                l1 += p1;
+                float v[8];
+                load_row8<KVT>(vt + (size_t)row * kHeadDim, lane, v);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    o0[j] = fmaf(p0, v[j], o0[j]);
+                    o1[j] = fmaf(p1, v[j], o1[j]);
+                }
+            }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        if (threadIdx.x == 0 && i + NS < ntiles) {
+            if (!mbar_wait(&empty[s], (i / NS) & 1, p.err)) {
+                s_abort = 1;
+                break;
+            }
+            issue(i + NS);
+        }
+    }
+    // Wait out any copies still in flight before the ring is reused
+    // (only reachable after an aborted wait).
+    if (threadIdx.x == 0 && s_abort) {
+        for (int i = 0; i < ntiles && i < NS; ++i) mbar_wait(&full[i % NS], 0, nullptr);
+    }
+    __syncthreads();
+
+    // Combine the 8 warps' (m, l, o) through shared memory (the K ring is
+    // free now): acc[warp][head][256].
+    float *acc = reinterpret_cast<float *>(smem);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        acc[(warp * 2 + 0) * kHeadDim + lane_dim<KVT>(lane, j)] = o0[j];
+        acc[(warp * 2 + 1) * kHeadDim + lane_dim<KVT>(lane, j)] = o1[j];
+    }
+    if (lane == 0) {
+        wm[warp][0] = m0;
+        wm[warp][1] = m1;
+        wl[warp][0] = l0;
+        wl[warp][1] = l1;
+    }
+    __syncthreads();
+    const int hh = threadIdx.x >> 7;         // head within the group
+    const int d = (threadIdx.x & 127) * 2;   // two dims per thread
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) M = fmaxf(M, wm[w][hh]);
+    float Ls = 0.f, A = 0.f, Bv = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+            const float f = ex2_approx(wm[w][hh] - M);
+            Ls += wl[w][hh] * f;
+            A += acc[(w * 2 + hh) * kHeadDim + d] * f;
+            Bv += acc[(w * 2 + hh) * kHeadDim + d + 1] * f;
+        }
+    }
+    const int h = 2 * g + hh;
+    if (p.write_partial) {
+        float *dst = p.partial + (((size_t)b * kHeads + h) * p.nsplit + split) * (kHeadDim + 2);
+        if (threadIdx.x == 0 || threadIdx.x == 128) {
+            dst[0] = M;
+            dst[1] = Ls;
+        }
+        dst[2 + d] = A;
+        dst[3 + d] = Bv;
+    } else {
+        const float inv = Ls > 0.f ? 1.0f / Ls : 0.f;
+        float2 *dst = reinterpret_cast<float2 *>(p.out + (size_t)b * kHeads * kHeadDim + h * kHeadDim + d);
+        *dst = make_float2(A * inv, Bv * inv);
+    }
+}
+
+// ------------------------------------------------------------------------
+// Log-sum-exp merge of n partials per (seq, head).  grid (B*8), block 256
+// (one thread per dim).  Partial (b, h, part) lives at
+// partials + b*bstride + h*hstride + part*pstride: [m, l, O[256]].
+// Writes out [B][2048] (normalised) or, with emit_partial, one merged
+// partial per (b, h) at emit [B][8][258].
+// ------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) merge_partials(const float *__restrict__ partials, int nparts, size_t bstride,
+                                                      size_t hstride, size_t pstride, float *__restrict__ out,
+                                                      float *__restrict__ emit) {
+    const int b = blockIdx.x / kHeads, h = blockIdx.x % kHeads, d = threadIdx.x;
+    const float *base = partials + (size_t)b * bstride + (size_t)h * hstride;
+    float M = -INFINITY;
+    for (int i = 0; i < nparts; ++i) M = fmaxf(M, base[(size_t)i * pstride]);
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+        for (int i = 0; i < nparts; ++i) {
+            const float *pp = base + (size_t)i * pstride;
+            const float f = ex2_approx(pp[0] - M);
+            L += pp[1] * f;
+            O += pp[2 + d] * f;
+        }
+    }
+    if (emit) {
+        float *e = emit + ((size_t)b * kHeads + h) * (kHeadDim + 2);
+        if (d == 0) {
+            e[0] = M;
+            e[1] = L;
+        }
+        e[2 + d] = O;
+    } else {
+        out[(size_t)b * kHeads * kHeadDim + h * kHeadDim + d] = L > 0.f ? O / L : 0.f;
+    }
+}
+
+// ------------------------------------------------------------------------
+// Prefill flash attention on tcgen05 / TMEM.
+//
+// CTA = (block of 64 query tokens, kv head g); the MMA M dimension stacks
+// the two query heads of the group (rows 0-63 head 2g, 64-127 head 2g+1),
+// so each K/V tile feeds both.  Per key tile of 64 rows:
+//     S[128x64]  = Q[128x256] . K^T     (16 MMAs of K=16, TMEM cols 0-127, x2 buffers)
+//     softmax    warps 0-3, thread = row, reads S from TMEM, writes P bf16
+//     O[128x256] += P[128x64] . V       (4 MMAs of K=16, TMEM cols 128-383)
+// Warp 4 issues TMA loads, warp 5 issues MMAs (one elected lane each).
+// Shared memory (1024-aligned, 128-B swizzle everywhere):
+//     Q  64 KB: 4 dim-chunks x [128 rows x 128 B]
+//     K  2 stages x 32 KB: 4 dim-chunks x [64 keys x 128 B]   (K-major B)
+//     V  2 stages x 32 KB: 4 dim-chunks x [64 keys x 128 B]   (MN-major B)
+//     P  16 KB: [128 rows x 64 keys] bf16                      (K-major A)
+// ------------------------------------------------------------------------
+struct PrefillParams {
+    float *out;       // [T][8][256]
+    int T;
+    int start_pos;
+    int kv_pos0;      // position of K/V row 0
+    int is_global;
+    unsigned *err;
+};
+
+constexpr int kPfThreads = 192;
+constexpr uint32_t kPfQBytes = 128 * 256 * 2;
+constexpr uint32_t kPfKVStage = 64 * 256 * 2;
+constexpr uint32_t kPfPBytes = 128 * 64 * 2;
+constexpr uint32_t kPfOffK = kPfQBytes;
+constexpr uint32_t kPfOffV = kPfOffK + 2 * kPfKVStage;
+constexpr uint32_t kPfOffP = kPfOffV + 2 * kPfKVStage;
+constexpr uint32_t kPfOffBar = kPfOffP + kPfPBytes;
+constexpr uint32_t kPfSmem = kPfOffBar + 256 + 1024;  // + alignment slack
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemS = 0;    // two 64-column S buffers
+constexpr uint32_t kTmemO = 128;  // 256 columns
+
+__global__ void __launch_bounds__(kPfThreads, 1)
+    prefill_fa_sm100(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const PrefillParams p) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char *sm = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char *sQ = sm;
+    unsigned char *sK = sm + kPfOffK;
+    unsigned char *sV = sm + kPfOffV;
+    unsigned char *sP = sm + kPfOffP;
+    uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kPfOffBar);
+    uint64_t *bar_q = bars + 0;
+    uint64_t *k_full = bars + 1;   // [2]
+    uint64_t *k_empty = bars + 3;  // [2]
+    uint64_t *v_full = bars + 5;   // [2]
+    uint64_t *v_empty = bars + 7;  // [2]
+    uint64_t *s_full = bars + 9;   // [2]
+    uint64_t *s_free = bars + 11;  // [2]
+    uint64_t *p_full = bars + 13;
+    uint64_t *p_empty = bars + 14;
+    uint64_t *mma_done = bars + 15;
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 16);
+    volatile int *s_abort = reinterpret_cast<volatile int *>(bars + 17);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nqb = gridDim.x;
+    const int qb = nqb - 1 - blockIdx.x;  // longest causal rows first
+    const int g = blockIdx.y;
+    const int t0 = qb * 64;
+    const int qlo = p.start_pos + t0;
+    const int qhi = p.start_pos + min(t0 + 64, p.T) - 1;
+    const int kmin = p.is_global ? 0 : max(0, qlo - (kWindow - 1));
+    const int j0 = (kmin - p.kv_pos0) / 64;
+    const int j1 = (qhi - p.kv_pos0) / 64 + 1;
+    const int ntiles = j1 - j0;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 16; ++i) mbar_init(&bars[i], 1);
+        mbar_init(&s_free[0], 128);
+        mbar_init(&s_free[1], 128);
+        mbar_init(p_full, 128);
+        *s_abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 5) tmem_alloc(tmem_slot, kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 4) {
+        // ------------------------------------------------ TMA producer
+        if (lane == 0) {
+            prefetch_tmap(&tmQ);
+            prefetch_tmap(&tmK);
+            prefetch_tmap(&tmV);
+            mbar_expect_tx(bar_q, kPfQBytes);
+            for (int c = 0; c < 4; ++c)
+                for (int hh = 0; hh < 2; ++hh)
+                    tma_load_3d(sQ + c * 16384 + hh * 8192, &tmQ, 64 * c, t0, 2 * g + hh, bar_q);
+            for (int i = 0; i < ntiles && !*s_abort; ++i) {
+                const int s = i & 1;
+                const int krow = (j0 + i) * 64;
+                if (i >= 2 && !mbar_wait(&k_empty[s], ((i - 2) >> 1) & 1, p.err)) { *s_abort = 1; break; }
+                mbar_expect_tx(&k_full[s], kPfKVStage);
+                for (int c = 0; c < 4; ++c)
+                    tma_load_3d(sK + s * kPfKVStage + c * 8192, &tmK, 64 * c, krow, g, &k_full[s]);
+                if (i >= 2 && !mbar_wait(&v_empty[s], ((i - 2) >> 1) & 1, p.err)) { *s_abort = 1; break; }
+                mbar_expect_tx(&v_full[s], kPfKVStage);
+                for (int c = 0; c < 4; ++c)
+                    tma_load_3d(sV + s * kPfKVStage + c * 8192, &tmV, 64 * c, krow, g, &v_full[s]);
+            }
+        }
+    } else if (warp == 5) {
+        // ------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idS = idesc_bf16_f32(128, 64, 0, 0);
+            constexpr uint32_t idO = idesc_bf16_f32(128, 256, 0, 1);
+            const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP);
+            bool ok = mbar_wait(bar_q, 0, p.err);
+            tc_fence_after();
+            for (int i = 0; ok && i <= ntiles; ++i) {
+                if (*s_abort) { ok = false; break; }
+                if (i < ntiles) {
+                    const int s = i & 1;
+                    if (!mbar_wait(&k_full[s], (i >> 1) & 1, p.err)) { ok = false; break; }
+                    if (i >= 2 && !mbar_wait(&s_free[s], ((i - 2) >> 1) & 1, p.err)) { ok = false; break; }
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < 16; ++kk) {
+                        const uint64_t a = smem_desc_sw128(aQ + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+                        const uint64_t bd = smem_desc_sw128(aK + s * kPfKVStage + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024);
+                        tc_mma_f16(tmem + kTmemS + s * 64, a, bd, idS, kk > 0 ? 1u : 0u);
+                    }
+                    tc_commit(&k_empty[s]);
+                    tc_commit(&s_full[s]);
+                }
+                if (i >= 1) {
+                    const int u = i - 1, su = u & 1;
+                    if (!mbar_wait(p_full, u & 1, p.err)) { ok = false; break; }
+                    if (!mbar_wait(&v_full[su], (u >> 1) & 1, p.err)) { ok = false; break; }
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const uint64_t a = smem_desc_sw128(aP + kk * 32, 16, 1024);
+                        const uint64_t bd = smem_desc_sw128(aV + su * kPfKVStage + kk * 2048, 8192, 1024);
+                        tc_mma_f16(tmem + kTmemO, a, bd, idO, (u > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    tc_commit(&v_empty[su]);
+                    tc_commit(p_empty);
+                }
+            }
+            if (!ok) *s_abort = 1;
+            // Drain: every MMA issued above has completed once this fires.
+            tc_commit(mma_done);
+            mbar_wait(mma_done, 0, nullptr);
+        }
+    } else {
+        // ------------------------------------------------ softmax warps 0-3
+        const int row = threadIdx.x;  // TMEM lane == S/O row
+        const int tr = row & 63, hh = row >> 6;
+        const int qpos = p.start_pos + t0 + tr;
+        const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int i = 0; i < ntiles; ++i) {
+            const int s = i & 1;
+            if (*s_abort || !mbar_wait(&s_full[s], (i >> 1) & 1, p.err)) { ok = false; break; }
+            tc_fence_after();
+            float x[64];
+            {
+                float a[32], c[32];
+                tmem_ld32(lane_base + kTmemS + s * 64, a);
+                tmem_ld32(lane_base + kTmemS + s * 64 + 32, c);
+                tc_wait_ld();
+#pragma unroll
+                for (int k = 0; k < 32; ++k) {
+                    x[k] = a[k];
+                    x[32 + k] = c[k];
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(&s_free[s]);
+            const int kbase = p.kv_pos0 + (j0 + i) * 64;
+            const int lo_ok = p.is_global ? INT_MIN : qpos - (kWindow - 1);
+            float mx = -INFINITY;
+#pragma unroll
+            for (int k = 0; k < 64; ++k) {
+                const int kp = kbase + k;
+                const bool valid = (kp <= qpos) && (kp >= lo_ok);
+                x[k] = valid ? x[k] * kScaleLog2 : -INFINITY;
+                mx = fmaxf(mx, x[k]);
+            }
+            const float m_new = fmaxf(m, mx);
+            const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
+            const float alpha = ex2_approx(m - m_use);
+            float rs = 0.f;
+            uint32_t pk[32];
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+                const float e0 = ex2_approx(x[2 * k] - m_use);
+                const float e1 = ex2_approx(x[2 * k + 1] - m_use);
+                rs += e0 + e1;
+                pk[k] = pack_bf16x2(e0, e1);
+            }
+            // P buffer and O are owned by the tensor core until PV(i-1) is done.
+            if (i >= 1 && !mbar_wait(p_empty, (i - 1) & 1, p.err)) { ok = false; break; }
+            tc_fence_after();
+            if (i >= 1 && m_new > m) {
+#pragma unroll 1
+                for (int c = 0; c < 8; ++c) {
+                    float o[32];
+                    tmem_ld32(lane_base + kTmemO + c * 32, o);
+                    tc_wait_ld();
+#pragma unroll
+                    for (int k = 0; k < 32; ++k) o[k] *= alpha;
+                    tmem_st32(lane_base + kTmemO + c * 32, o);
+                }
+                tc_wait_st();
+            }
+            l = l * alpha + rs;
+            m = m_new;
+            unsigned char *prow = sP + row * 128;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                *reinterpret_cast<uint4 *>(prow + ((j ^ (row & 7)) * 16)) =
+                    make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+            }
+            fence_proxy_async_smem();
+            tc_fence_before();
+            mbar_arrive(p_full);
+        }
+        if (!ok) *s_abort = 1;
+        // Epilogue: O / l -> out[t][2g+hh][:]
+        if (ok && ntiles > 0 && mbar_wait(p_empty, (ntiles - 1) & 1, p.err)) {
+            tc_fence_after();
+            const float inv = l > 0.f ? 1.0f / l : 0.f;
+            const bool store = (t0 + tr) < p.T;
+            float *dst = p.out + ((size_t)(t0 + tr) * kHeads + 2 * g + hh) * kHeadDim;
+#pragma unroll 1
+            for (int c = 0; c < 8; ++c) {
+                float o[32];
+                tmem_ld32(lane_base + kTmemO + c * 32, o);
+                tc_wait_ld();
+                if (store) {
+#pragma unroll
+                    for (int k = 0; k < 32; k += 4)
+                        *reinterpret_cast<float4 *>(dst + c * 32 + k) =
+                            make_float4(o[k] * inv, o[k + 1] * inv, o[k + 2] * inv, o[k + 3] * inv);
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 4 && lane == 0 && *s_abort) {
+        // Let in-flight TMA copies land before the CTA's shared memory goes.
+        for (int s = 0; s < 2; ++s) {
+            mbar_wait(&k_full[s], 0, nullptr);
+            mbar_wait(&v_full[s], 0, nullptr);
+        }
+    }
+    __syncthreads();
+    if (warp == 5) {
+        tc_fence_after();
+        tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// ------------------------------------------------------------------------
+// Utility kernels: seeded N(0,1) fill, host-layout import/export.
+// ------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t splitmix64(uint64_t x) {
+    x += 0x9E3779B97F4A7C15ull;
+    x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+    x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+    return x ^ (x >> 31);
+}
+
+template <typename KVT>
+__global__ void fill_normal(KVT *dst, size_t n, uint64_t seed) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n / 2; i += (size_t)gridDim.x * blockDim.x) {
+        const uint64_t r = splitmix64(seed ^ (i * 0xD1B54A32D192ED03ull));
+        const float u1 = ((uint32_t)(r >> 40) + 0.5f) * (1.0f / 16777216.0f);
+        const float u2 = ((uint32_t)(r & 0xFFFFFF)) * (1.0f / 16777216.0f);
+        const float rad = sqrtf(-2.0f * logf(u1));
+        float sn, cs;
+        sincospif(2.0f * u2, &sn, &cs);
+        dst[2 * i] = KvType<KVT>::from_f(rad * cs);
+        dst[2 * i + 1] = KvType<KVT>::from_f(rad * sn);
+    }
+}
+
+// host-layout [rows][4][256] fp32  <->  device planes [4][rows][256]
+template <typename KVT>
+__global__ void import_rows(const float *__restrict__ src, KVT *__restrict__ dst_plane0, size_t plane_stride, int rows) {
+    const size_t n = (size_t)rows * kKvHeads * kHeadDim;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int d = i % kHeadDim;
+        const int h = (i / kHeadDim) % kKvHeads;
+        const size_t r = i / (kHeadDim * kKvHeads);
+        dst_plane0[h * plane_stride + r * kHeadDim + d] = KvType<KVT>::from_f(src[i]);
+    }
+}
+template <typename KVT>
+__global__ void export_rows(const KVT *__restrict__ src_plane0, size_t plane_stride, int rows, float *__restrict__ dst) {
+    const size_t n = (size_t)rows * kKvHeads * kHeadDim;
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int d = i % kHeadDim;
+        const int h = (i / kHeadDim) % kKvHeads;
+        const size_t r = i / (kHeadDim * kKvHeads);
+        dst[i] = KvType<KVT>::to_f(src_plane0[h * plane_stride + r * kHeadDim + d]);
+    }
+}
+
+}  // namespace g3

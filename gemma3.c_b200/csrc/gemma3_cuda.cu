@@ -1,0 +1,723 @@
+// gemma3_cuda.cu - host side of the C-ABI declared in include/gemma3_cuda.h.
+//
+// One context = one GPU = one CUDA stream.  The context owns the device KV
+// cache of all 34 layers for max_batch sequence slots, the uploaded RoPE
+// tables, the per-layer QK-norm gains and the scratch the kernels need
+// (bf16 Q/K/V staging for prefill, split-KV partials for decode, device
+// copies of host arguments).  Nothing on the compute path falls back to the
+// CPU: a failure is reported through the return code.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <dlfcn.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <vector>
+
+#include "../../include/gemma3_cuda.h"
+#include "attn_kernels.cuh"
+
+using g3::kHeadDim;
+using g3::kHeads;
+using g3::kKvHeads;
+using g3::kWindow;
+
+// ------------------------------------------------------------------ errors
+static thread_local char g_err[512] = "";
+
+static int fail(int code, const char *fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof g_err, fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+#define CU_TRY(expr)                                                                                    \
+    do {                                                                                                \
+        cudaError_t e_ = (expr);                                                                        \
+        if (e_ != cudaSuccess)                                                                          \
+            return fail(e_ == cudaErrorMemoryAllocation ? GEMMA3_CUDA_ERR_OUT_OF_MEMORY                 \
+                                                        : GEMMA3_CUDA_ERR_GENERATION_FAILED,            \
+                        "%s: %s (%s:%d)", #expr, cudaGetErrorString(e_), __FILE__, __LINE__);           \
+    } while (0)
+
+extern "C" const char *gemma3_cuda_last_error(void) { return g_err; }
+
+// ------------------------------------------------------------------ NCCL (loaded lazily)
+// The library does not link NCCL: a process that already holds one (torch's)
+// must not get a second copy.  The few entry points are resolved with dlopen
+// the first time a communicator is requested.
+typedef struct {
+    char internal[128];
+} g3NcclUniqueId;
+typedef void *g3NcclComm;
+struct NcclApi {
+    int (*getUniqueId)(g3NcclUniqueId *);
+    int (*commInitRank)(g3NcclComm *, int, g3NcclUniqueId, int);
+    int (*allGather)(const void *, void *, size_t, int, g3NcclComm, cudaStream_t);
+    int (*commDestroy)(g3NcclComm);
+    const char *(*getErrorString)(int);
+    bool ok = false;
+};
+static NcclApi g_nccl;
+static int nccl_load() {
+    if (g_nccl.ok) return 0;
+    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "NCCL not loadable: %s", dlerror());
+    g_nccl.getUniqueId = (int (*)(g3NcclUniqueId *))dlsym(h, "ncclGetUniqueId");
+    g_nccl.commInitRank = (int (*)(g3NcclComm *, int, g3NcclUniqueId, int))dlsym(h, "ncclCommInitRank");
+    g_nccl.allGather = (int (*)(const void *, void *, size_t, int, g3NcclComm, cudaStream_t))dlsym(h, "ncclAllGather");
+    g_nccl.commDestroy = (int (*)(g3NcclComm))dlsym(h, "ncclCommDestroy");
+    g_nccl.getErrorString = (const char *(*)(int))dlsym(h, "ncclGetErrorString");
+    if (!g_nccl.getUniqueId || !g_nccl.commInitRank || !g_nccl.allGather || !g_nccl.commDestroy)
+        return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "NCCL symbols missing");
+    g_nccl.ok = true;
+    return 0;
+}
+static const int kNcclFloat32 = 7;  // ncclFloat32 in nccl.h
+
+// ------------------------------------------------------------------ TMA encode (driver entry point)
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static EncodeTiledFn g_encode = nullptr;
+static int load_encode() {
+    if (g_encode) return 0;
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    CU_TRY(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q));
+    if (!fn || q != cudaDriverEntryPointSuccess)
+        return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "cuTensorMapEncodeTiled unavailable");
+    g_encode = (EncodeTiledFn)fn;
+    return 0;
+}
+// bf16 tensor [planes][rows][256] (planes stride given), box 64 x 64 x 1,
+// 128-byte swizzle.
+static int make_map(CUtensorMap *m, const void *base, int rows, size_t plane_stride_elems, int planes) {
+    cuuint64_t dims[3] = {(cuuint64_t)kHeadDim, (cuuint64_t)rows, (cuuint64_t)planes};
+    cuuint64_t strides[2] = {(cuuint64_t)kHeadDim * 2, (cuuint64_t)plane_stride_elems * 2};
+    cuuint32_t box[3] = {64, 64, 1};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return 0;
+}
+
+// ------------------------------------------------------------------ context
+struct LayerState {
+    void *kv = nullptr;
+    int rows = 0;
+    int is_global = 0;
+    uint16_t *qn = nullptr, *kn = nullptr;
+    int use_norm = 0;
+};
+
+struct gemma3_cuda_ctx {
+    gemma3_cuda_config cfg;
+    cudaStream_t stream = nullptr;
+    size_t esz = 4;
+    int shard_lo = 0, shard_hi = 0;
+    std::vector<LayerState> layers;
+    float *rope_local = nullptr, *rope_global = nullptr;
+    int rope_rows = 0;
+    // prefill scratch
+    __nv_bfloat16 *qst = nullptr;             // [8][max_prefill][256]
+    __nv_bfloat16 *kst = nullptr, *vst = nullptr;  // [4][st_rows][256]
+    int st_rows = 0;
+    // decode scratch
+    float *qdec = nullptr;     // [max_batch][8][256]
+    float *partial = nullptr;  // [max_batch][8][kMaxSplit][258]
+    float *emit = nullptr;     // [max_batch][8][258]
+    float *gather = nullptr;   // [kv_ranks][max_batch][8][258]
+    // device copies for the host-pointer entry points
+    float *io = nullptr;
+    size_t io_rows = 0;
+    unsigned *err = nullptr;
+    long long launches = 0;
+    g3NcclComm comm = nullptr;
+};
+
+static constexpr int kMaxSplit = 128;
+static constexpr int kPartialStride = kHeadDim + 2;
+
+static bool is_global_layer(int l) { return (l + 1) % 6 == 0; }
+
+extern "C" void gemma3_cuda_config_default(gemma3_cuda_config *c) {
+    if (!c) return;
+    c->num_layers = 34;
+    c->num_heads = kHeads;
+    c->num_kv_heads = kKvHeads;
+    c->head_dim = kHeadDim;
+    c->sliding_window = kWindow;
+    c->rmsnorm_eps = 1e-6f;
+    c->max_context = 8192;
+    c->max_batch = 1;
+    c->kv_dtype = GEMMA3_CUDA_KV_F32;
+    c->device = 0;
+    c->max_prefill = 8192;
+    c->kv_rank = 0;
+    c->kv_ranks = 1;
+}
+
+static void ctx_release(gemma3_cuda_ctx *c) {
+    if (!c) return;
+    cudaSetDevice(c->cfg.device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    if (c->comm && g_nccl.ok) g_nccl.commDestroy(c->comm);
+    for (auto &L : c->layers) {
+        cudaFree(L.kv);
+        cudaFree(L.qn);
+        cudaFree(L.kn);
+    }
+    cudaFree(c->rope_local);
+    cudaFree(c->rope_global);
+    cudaFree(c->qst);
+    cudaFree(c->kst);
+    cudaFree(c->vst);
+    cudaFree(c->qdec);
+    cudaFree(c->partial);
+    cudaFree(c->emit);
+    cudaFree(c->gather);
+    cudaFree(c->io);
+    cudaFree(c->err);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+static int ctx_alloc(gemma3_cuda_ctx *c) {
+    const gemma3_cuda_config &k = c->cfg;
+    CU_TRY(cudaSetDevice(k.device));
+    int major = 0, minor = 0;
+    CU_TRY(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, k.device));
+    CU_TRY(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, k.device));
+    if (major != 10 || minor != 0)
+        return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "device %d is sm_%d%d; this library is built for sm_100a only",
+                    k.device, major, minor);
+    CU_TRY(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+    c->esz = k.kv_dtype == GEMMA3_CUDA_KV_BF16 ? 2 : 4;
+    const int S = (k.max_context + k.kv_ranks - 1) / k.kv_ranks;
+    c->shard_lo = std::min(k.max_context, k.kv_rank * S);
+    c->shard_hi = std::min(k.max_context, c->shard_lo + S);
+    c->layers.resize(k.num_layers);
+    for (int l = 0; l < k.num_layers; ++l) {
+        LayerState &L = c->layers[l];
+        L.is_global = is_global_layer(l);
+        L.rows = L.is_global ? std::max(1, c->shard_hi - c->shard_lo) : kWindow;
+        const size_t bytes = (size_t)k.max_batch * 2 * kKvHeads * L.rows * kHeadDim * c->esz;
+        CU_TRY(cudaMalloc(&L.kv, bytes));
+        CU_TRY(cudaMemsetAsync(L.kv, 0, bytes, c->stream));
+        CU_TRY(cudaMalloc(&L.qn, kHeadDim * 2));
+        CU_TRY(cudaMalloc(&L.kn, kHeadDim * 2));
+    }
+    CU_TRY(cudaMalloc(&c->qst, (size_t)kHeads * k.max_prefill * kHeadDim * 2));
+    CU_TRY(cudaMalloc(&c->qdec, (size_t)k.max_batch * kHeads * kHeadDim * 4));
+    CU_TRY(cudaMalloc(&c->partial, (size_t)k.max_batch * kHeads * kMaxSplit * kPartialStride * 4));
+    CU_TRY(cudaMalloc(&c->emit, (size_t)k.max_batch * kHeads * kPartialStride * 4));
+    CU_TRY(cudaMalloc(&c->gather, (size_t)k.kv_ranks * k.max_batch * kHeads * kPartialStride * 4));
+    c->io_rows = std::max(k.max_prefill, k.max_batch);
+    CU_TRY(cudaMalloc(&c->io, c->io_rows * (2048 + 1024 + 1024 + 2048) * sizeof(float)));
+    CU_TRY(cudaMalloc(&c->err, sizeof(unsigned)));
+    CU_TRY(cudaMemsetAsync(c->err, 0, sizeof(unsigned), c->stream));
+    CU_TRY(cudaFuncSetAttribute(g3::prefill_fa_sm100, cudaFuncAttributeMaxDynamicSharedMemorySize, g3::kPfSmem));
+    const int dsm_bf = g3::DecodeCfg<__nv_bfloat16>::NS * 2 * g3::DecodeCfg<__nv_bfloat16>::TK * kHeadDim * 2;
+    const int dsm_f = g3::DecodeCfg<float>::NS * 2 * g3::DecodeCfg<float>::TK * kHeadDim * 4;
+    CU_TRY(cudaFuncSetAttribute(g3::decode_splitkv<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, dsm_bf));
+    CU_TRY(cudaFuncSetAttribute(g3::decode_splitkv<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, dsm_f));
+    if (int r = load_encode()) return r;
+    CU_TRY(cudaStreamSynchronize(c->stream));
+    return 0;
+}
+
+extern "C" gemma3_cuda_ctx *gemma3_cuda_init(const gemma3_cuda_config *cfg) {
+    g_err[0] = 0;
+    if (!cfg) {
+        fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null config");
+        return nullptr;
+    }
+    const gemma3_cuda_config &k = *cfg;
+    if (k.num_heads != kHeads || k.num_kv_heads != kKvHeads || k.head_dim != kHeadDim ||
+        k.sliding_window != kWindow || k.num_layers <= 0 || k.num_layers > 256 || k.max_context <= 0 ||
+        k.max_batch <= 0 || k.max_batch > g3::kMaxDecodeBatch || k.max_prefill <= 0 ||
+        (k.kv_dtype != GEMMA3_CUDA_KV_F32 && k.kv_dtype != GEMMA3_CUDA_KV_BF16) || k.kv_ranks < 1 ||
+        k.kv_rank < 0 || k.kv_rank >= k.kv_ranks) {
+        fail(GEMMA3_CUDA_ERR_INVALID_ARG,
+             "unsupported configuration (needs 8 q heads, 4 kv heads, head_dim 256, window 1024, "
+             "1 <= max_batch <= %d, valid kv_rank/kv_ranks)",
+             g3::kMaxDecodeBatch);
+        return nullptr;
+    }
+    gemma3_cuda_ctx *c = new gemma3_cuda_ctx();
+    c->cfg = k;
+    if (ctx_alloc(c) != 0) {
+        char keep[512];
+        memcpy(keep, g_err, sizeof keep);
+        ctx_release(c);
+        memcpy(g_err, keep, sizeof keep);
+        return nullptr;
+    }
+    return c;
+}
+
+extern "C" void gemma3_cuda_free(gemma3_cuda_ctx *ctx) { ctx_release(ctx); }
+
+extern "C" void *gemma3_cuda_stream(gemma3_cuda_ctx *ctx) { return ctx ? (void *)ctx->stream : nullptr; }
+extern "C" long long gemma3_cuda_launch_count(gemma3_cuda_ctx *ctx) { return ctx ? ctx->launches : 0; }
+
+extern "C" int gemma3_cuda_synchronize(gemma3_cuda_ctx *ctx) {
+    if (!ctx) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null context");
+    CU_TRY(cudaSetDevice(ctx->cfg.device));
+    CU_TRY(cudaStreamSynchronize(ctx->stream));
+    unsigned e = 0;
+    CU_TRY(cudaMemcpy(&e, ctx->err, sizeof e, cudaMemcpyDeviceToHost));
+    if (e) {
+        cudaMemsetAsync(ctx->err, 0, sizeof(unsigned), ctx->stream);
+        cudaStreamSynchronize(ctx->stream);
+        return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "device status 0x%x (%s)", e,
+                    (e & g3::kErrWaitTimeout) ? "bounded wait timed out" : "bad index");
+    }
+    return 0;
+}
+
+// Host RoPE table, the formula of gemma3_rope_precompute
+// (gemma3_kernels.c:455-468): freq = 1/theta^(2i/d), angle = (float)pos*freq.
+extern "C" void gemma3_cuda_rope_precompute(float *freqs, int max_pos, int head_dim, float theta) {
+    if (!freqs || max_pos <= 0 || head_dim <= 0) return;
+    const int half = head_dim / 2;
+    std::vector<float> inv(half);
+    for (int i = 0; i < half; ++i) inv[i] = 1.0f / powf(theta, (float)(2 * i) / (float)head_dim);
+    for (int p = 0; p < max_pos; ++p)
+        for (int i = 0; i < half; ++i) {
+            const float a = (float)p * inv[i];
+            freqs[((size_t)p * half + i) * 2] = cosf(a);
+            freqs[((size_t)p * half + i) * 2 + 1] = sinf(a);
+        }
+}
+
+extern "C" int gemma3_cuda_upload_rope(gemma3_cuda_ctx *ctx, const float *rope_local, const float *rope_global,
+                                       int max_context, int head_dim) {
+    if (!ctx || !rope_local || !rope_global) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null argument");
+    if (head_dim != kHeadDim || max_context < ctx->cfg.max_context)
+        return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "rope table must cover max_context=%d rows of head_dim 256",
+                    ctx->cfg.max_context);
+    CU_TRY(cudaSetDevice(ctx->cfg.device));
+    const size_t n = (size_t)ctx->cfg.max_context * kHeadDim;
+    if (!ctx->rope_local) {
+        CU_TRY(cudaMalloc(&ctx->rope_local, n * 4));
+        CU_TRY(cudaMalloc(&ctx->rope_global, n * 4));
+    }
+    CU_TRY(cudaMemcpyAsync(ctx->rope_local, rope_local, n * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CU_TRY(cudaMemcpyAsync(ctx->rope_global, rope_global, n * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CU_TRY(cudaStreamSynchronize(ctx->stream));
+    ctx->rope_rows = ctx->cfg.max_context;
+    return 0;
+}
+
+extern "C" int gemma3_cuda_set_qk_norm(gemma3_cuda_ctx *ctx, int layer, const uint16_t *q_norm,
+                                       const uint16_t *k_norm) {
+    if (!ctx || layer < 0 || layer >= ctx->cfg.num_layers) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad layer");
+    CU_TRY(cudaSetDevice(ctx->cfg.device));
+    LayerState &L = ctx->layers[layer];
+    L.use_norm = (q_norm && k_norm) ? 1 : 0;
+    if (L.use_norm) {
+        CU_TRY(cudaMemcpyAsync(L.qn, q_norm, kHeadDim * 2, cudaMemcpyHostToDevice, ctx->stream));
+        CU_TRY(cudaMemcpyAsync(L.kn, k_norm, kHeadDim * 2, cudaMemcpyHostToDevice, ctx->stream));
+        CU_TRY(cudaStreamSynchronize(ctx->stream));
+    }
+    return 0;
+}
+
+static g3::LayerDev layer_dev(gemma3_cuda_ctx *ctx, int layer) {
+    const LayerState &L = ctx->layers[layer];
+    g3::LayerDev d;
+    d.kv = L.kv;
+    d.rows = L.rows;
+    d.is_global = L.is_global;
+    d.shard_lo = L.is_global ? ctx->shard_lo : 0;
+    d.shard_hi = L.is_global ? ctx->shard_hi : kWindow;
+    d.qn = L.use_norm ? L.qn : nullptr;
+    d.kn = L.use_norm ? L.kn : nullptr;
+    d.rope = L.is_global ? ctx->rope_global : ctx->rope_local;
+    return d;
+}
+
+static int check_launch(gemma3_cuda_ctx *ctx, int n) {
+    ctx->launches += n;
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess)
+        return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "kernel launch failed: %s", cudaGetErrorString(e));
+    return 0;
+}
+
+// ------------------------------------------------------------------ prefill
+template <typename KVT>
+static int prefill_impl(gemma3_cuda_ctx *ctx, int layer, int seq, const float *Q, const float *K, const float *V,
+                        int T, int start_pos, float *out) {
+    const LayerState &LS = ctx->layers[layer];
+    g3::LayerDev L = layer_dev(ctx, layer);
+    const bool global = LS.is_global;
+    const int kv_pos0 = global ? 0 : std::max(0, start_pos - (kWindow - 1));
+    const int lrows = start_pos + T - kv_pos0;  // key rows the attention sees
+    const bool direct = global && sizeof(KVT) == 2;  // bf16 global cache is already linear
+    if (!direct && ctx->st_rows < lrows) {
+        cudaFree(ctx->kst);
+        cudaFree(ctx->vst);
+        ctx->kst = ctx->vst = nullptr;
+        ctx->st_rows = 0;
+        const int want = std::max(lrows, std::min(ctx->cfg.max_context, kWindow - 1 + ctx->cfg.max_prefill));
+        CU_TRY(cudaMalloc(&ctx->kst, (size_t)kKvHeads * want * kHeadDim * 2));
+        CU_TRY(cudaMalloc(&ctx->vst, (size_t)kKvHeads * want * kHeadDim * 2));
+        ctx->st_rows = want;
+    }
+    const int nprefix = start_pos - kv_pos0;
+    if (!direct && nprefix > 0) {
+        g3::stage_prefix<KVT><<<dim3(nprefix, 8), 32, 0, ctx->stream>>>(L, seq, kv_pos0, ctx->kst, ctx->vst,
+                                                                          ctx->st_rows);
+        if (int r = check_launch(ctx, 1)) return r;
+    }
+    g3::prologue_prefill<KVT><<<dim3(T, 16), 128, 0, ctx->stream>>>(
+        Q, K, V, L, ctx->cfg.rmsnorm_eps, seq, T, start_pos, kv_pos0, ctx->qst, direct ? nullptr : ctx->kst,
+        direct ? nullptr : ctx->vst, ctx->st_rows);
+    if (int r = check_launch(ctx, 1)) return r;
+
+    CUtensorMap tq, tk, tv;
+    if (int r = make_map(&tq, ctx->qst, T, (size_t)T * kHeadDim, kHeads)) return r;
+    if (direct) {
+        const size_t plane = (size_t)LS.rows * kHeadDim;
+        const __nv_bfloat16 *kbase = reinterpret_cast<const __nv_bfloat16 *>(LS.kv) + (size_t)seq * 2 * kKvHeads * plane;
+        if (int r = make_map(&tk, kbase, lrows, plane, kKvHeads)) return r;
+        if (int r = make_map(&tv, kbase + kKvHeads * plane, lrows, plane, kKvHeads)) return r;
+    } else {
+        const size_t plane = (size_t)ctx->st_rows * kHeadDim;
+        if (int r = make_map(&tk, ctx->kst, lrows, plane, kKvHeads)) return r;
+        if (int r = make_map(&tv, ctx->vst, lrows, plane, kKvHeads)) return r;
+    }
+    g3::PrefillParams p;
+    p.out = out;
+    p.T = T;
+    p.start_pos = start_pos;
+    p.kv_pos0 = kv_pos0;
+    p.is_global = global;
+    p.err = ctx->err;
+    const int nqb = (T + 63) / 64;
+    g3::prefill_fa_sm100<<<dim3(nqb, kKvHeads), g3::kPfThreads, g3::kPfSmem, ctx->stream>>>(tq, tk, tv, p);
+    return check_launch(ctx, 1);
+}
+
+static int prefill_check(gemma3_cuda_ctx *ctx, int layer, int seq, int T, int start_pos) {
+    if (!ctx) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null context");
+    if (layer < 0 || layer >= ctx->cfg.num_layers) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad layer %d", layer);
+    if (seq < 0 || seq >= ctx->cfg.max_batch) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad sequence slot %d", seq);
+    if (T <= 0 || T > ctx->cfg.max_prefill || start_pos < 0)
+        return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad token range T=%d start_pos=%d (max_prefill %d)", T, start_pos,
+                    ctx->cfg.max_prefill);
+    if ((long long)start_pos + T > ctx->cfg.max_context)
+        return fail(GEMMA3_CUDA_ERR_CONTEXT_OVERFLOW, "positions up to %d exceed max_context %d", start_pos + T - 1,
+                    ctx->cfg.max_context);
+    if (!ctx->rope_local) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "RoPE tables not uploaded");
+    if (ctx->layers[layer].is_global && ctx->cfg.kv_ranks > 1)
+        return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "prefill into a context-parallel global layer is not supported");
+    return 0;
+}
+
+extern "C" int gemma3_cuda_attn_prefill_dev(gemma3_cuda_ctx *ctx, int layer, int seq, const float *Q,
+                                            const float *K, const float *V, int T, int start_pos, float *out) {
+    if (int r = prefill_check(ctx, layer, seq, T, start_pos)) return r;
+    if (!Q || !K || !V || !out) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null buffer");
+    CU_TRY(cudaSetDevice(ctx->cfg.device));
+    if (ctx->cfg.kv_dtype == GEMMA3_CUDA_KV_BF16)
+        return prefill_impl<__nv_bfloat16>(ctx, layer, seq, Q, K, V, T, start_pos, out);
+    return prefill_impl<float>(ctx, layer, seq, Q, K, V, T, start_pos, out);
+}
+
+extern "C" int gemma3_cuda_attn_prefill(gemma3_cuda_ctx *ctx, int layer, int seq, const float *Q, const float *K,
+                                        const float *V, int T, int start_pos, float *out) {
+    if (int r = prefill_check(ctx, layer, seq, T, start_pos)) return r;
+    if (!Q || !K || !V || !out) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null buffer");
+    CU_TRY(cudaSetDevice(ctx->cfg.device));
+    float *dq = ctx->io, *dk = dq + (size_t)T * 2048, *dv = dk + (size_t)T * 1024, *dout = dv + (size_t)T * 1024;
+    CU_TRY(cudaMemcpyAsync(dq, Q, (size_t)T * 2048 * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CU_TRY(cudaMemcpyAsync(dk, K, (size_t)T * 1024 * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CU_TRY(cudaMemcpyAsync(dv, V, (size_t)T * 1024 * 4, cudaMemcpyHostToDevice, ctx->stream));
+    if (int r = gemma3_cuda_attn_prefill_dev(ctx, layer, seq, dq, dk, dv, T, start_pos, dout)) return r;
+    CU_TRY(cudaMemcpyAsync(out, dout, (size_t)T * 2048 * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return gemma3_cuda_synchronize(ctx);
+}
+
+// ------------------------------------------------------------------ decode
+struct DecodePlan {
+    g3::DecodeBatch batch;
+    g3::DecodeRows rows;
+    int chunk = 0, nsplit = 0;
+};
+
+static int decode_check(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_ids, const int *pos) {
+    if (!ctx) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null context");
+    if (layer < 0 || layer >= ctx->cfg.num_layers) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad layer %d", layer);
+    if (B <= 0 || B > ctx->cfg.max_batch || !seq_ids || !pos)
+        return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad batch B=%d (max_batch %d)", B, ctx->cfg.max_batch);
+    if (!ctx->rope_local) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "RoPE tables not uploaded");
+    std::vector<char> seen(ctx->cfg.max_batch, 0);
+    for (int b = 0; b < B; ++b) {
+        if (seq_ids[b] < 0 || seq_ids[b] >= ctx->cfg.max_batch || seen[seq_ids[b]])
+            return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad or repeated sequence slot %d", seq_ids[b]);
+        seen[seq_ids[b]] = 1;
+        if (pos[b] < 0) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "negative position");
+        if (pos[b] >= ctx->cfg.max_context)
+            return fail(GEMMA3_CUDA_ERR_CONTEXT_OVERFLOW, "position %d >= max_context %d", pos[b], ctx->cfg.max_context);
+    }
+    return 0;
+}
+
+template <typename KVT>
+static void plan_decode(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_ids, const int *pos, DecodePlan &pl) {
+    const LayerState &L = ctx->layers[layer];
+    constexpr int TK = g3::DecodeCfg<KVT>::TK;
+    pl.batch.B = pl.rows.B = B;
+    long long total = 0;
+    int maxrows = 0;
+    for (int b = 0; b < B; ++b) {
+        pl.batch.seq[b] = pl.rows.seq[b] = seq_ids[b];
+        pl.batch.pos[b] = pos[b];
+        int n;
+        if (L.is_global) {
+            n = std::min(pos[b] + 1, ctx->shard_hi) - ctx->shard_lo;
+            n = std::max(0, std::min(n, L.rows));
+        } else {
+            n = std::min(pos[b] + 1, kWindow);
+        }
+        pl.rows.nrows[b] = n;
+        total += (long long)n * kKvHeads;
+        maxrows = std::max(maxrows, n);
+    }
+    // Aim for ~8 CTAs per SM over the call (2 resident x 4 waves) and at
+    // least 4 tiles per CTA; never more than kMaxSplit splits.
+    const long long target = 148LL * 8;
+    long long chunk = std::max<long long>(4 * TK, (total + target - 1) / target);
+    chunk = std::max<long long>(chunk, (maxrows + kMaxSplit - 1) / kMaxSplit);
+    chunk = (chunk + TK - 1) / TK * TK;
+    pl.chunk = (int)chunk;
+    pl.nsplit = std::max(1, (int)((maxrows + chunk - 1) / chunk));
+}
+
+// Runs the prologue and the split-KV kernel.  mode 0: final output into out
+// (merging splits if needed); mode 1: one merged (m, l, O) partial per
+// (seq, head) into `partial_out` [B][8][258].
+template <typename KVT>
+static int decode_impl(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_ids, const int *pos, const float *Q,
+                       const float *K, const float *V, float *out, float *partial_out) {
+    DecodePlan pl;
+    plan_decode<KVT>(ctx, layer, B, seq_ids, pos, pl);
+    g3::LayerDev L = layer_dev(ctx, layer);
+    g3::prologue_decode<KVT><<<dim3(B, 16), 128, 0, ctx->stream>>>(Q, K, V, L, ctx->cfg.rmsnorm_eps, pl.batch,
+                                                                    ctx->qdec);
+    if (int r = check_launch(ctx, 1)) return r;
+    g3::DecodeParams p;
+    p.q = ctx->qdec;
+    p.L = L;
+    p.chunk = pl.chunk;
+    p.nsplit = pl.nsplit;
+    p.partial = ctx->partial;
+    p.out = out;
+    p.write_partial = (pl.nsplit > 1 || partial_out) ? 1 : 0;
+    p.err = ctx->err;
+    constexpr int smem = g3::DecodeCfg<KVT>::NS * 2 * g3::DecodeCfg<KVT>::TK * kHeadDim * sizeof(KVT);
+    g3::decode_splitkv<KVT><<<dim3(pl.nsplit, kKvHeads, B), 256, smem, ctx->stream>>>(p, pl.rows);
+    if (int r = check_launch(ctx, 1)) return r;
+    if (p.write_partial) {
+        const size_t hs = (size_t)pl.nsplit * kPartialStride;
+        g3::merge_partials<<<B * kHeads, 256, 0, ctx->stream>>>(ctx->partial, pl.nsplit, kHeads * hs, hs,
+                                                                 kPartialStride, out, partial_out);
+        if (int r = check_launch(ctx, 1)) return r;
+    }
+    return 0;
+}
+
+static int decode_dispatch(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_ids, const int *pos,
+                           const float *Q, const float *K, const float *V, float *out, float *partial_out) {
+    if (ctx->cfg.kv_dtype == GEMMA3_CUDA_KV_BF16)
+        return decode_impl<__nv_bfloat16>(ctx, layer, B, seq_ids, pos, Q, K, V, out, partial_out);
+    return decode_impl<float>(ctx, layer, B, seq_ids, pos, Q, K, V, out, partial_out);
+}
+
+extern "C" int gemma3_cuda_merge_partials_dev(gemma3_cuda_ctx *ctx, int n_parts, int B, const float *partials,
+                                              float *out) {
+    if (!ctx || n_parts <= 0 || B <= 0 || !partials || !out) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad argument");
+    CU_TRY(cudaSetDevice(ctx->cfg.device));
+    // partials [n_parts][B][8][258]
+    g3::merge_partials<<<B * kHeads, 256, 0, ctx->stream>>>(partials, n_parts, (size_t)kHeads * kPartialStride,
+                                                             kPartialStride, (size_t)B * kHeads * kPartialStride,
+                                                             out, nullptr);
+    return check_launch(ctx, 1);
+}
+
+extern "C" int gemma3_cuda_attn_decode_partial_dev(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_ids,
+                                                   const int *pos, const float *Q, const float *K, const float *V,
+                                                   float *partial) {
+    if (int r = decode_check(ctx, layer, B, seq_ids, pos)) return r;
+    if (!Q || !K || !V || !partial) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null buffer");
+    CU_TRY(cudaSetDevice(ctx->cfg.device));
+    return decode_dispatch(ctx, layer, B, seq_ids, pos, Q, K, V, nullptr, partial);
+}
+
+extern "C" int gemma3_cuda_attn_decode_dev(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_ids,
+                                           const int *pos, const float *Q, const float *K, const float *V,
+                                           float *out) {
+    if (int r = decode_check(ctx, layer, B, seq_ids, pos)) return r;
+    if (!Q || !K || !V || !out) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null buffer");
+    CU_TRY(cudaSetDevice(ctx->cfg.device));
+    const bool split = ctx->layers[layer].is_global && ctx->cfg.kv_ranks > 1;
+    if (!split) return decode_dispatch(ctx, layer, B, seq_ids, pos, Q, K, V, out, nullptr);
+    if (!ctx->comm)
+        return fail(GEMMA3_CUDA_ERR_INVALID_ARG,
+                    "global layer of a context-parallel context needs gemma3_cuda_comm_init (or the partial API)");
+    if (int r = decode_dispatch(ctx, layer, B, seq_ids, pos, Q, K, V, nullptr, ctx->emit)) return r;
+    const size_t n = (size_t)B * kHeads * kPartialStride;
+    int nr = g_nccl.allGather(ctx->emit, ctx->gather, n, kNcclFloat32, ctx->comm, ctx->stream);
+    if (nr != 0)
+        return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "ncclAllGather failed: %s",
+                    g_nccl.getErrorString ? g_nccl.getErrorString(nr) : "?");
+    return gemma3_cuda_merge_partials_dev(ctx, ctx->cfg.kv_ranks, B, ctx->gather, out);
+}
+
+extern "C" int gemma3_cuda_attn_decode(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_ids, const int *pos,
+                                       const float *Q, const float *K, const float *V, float *out) {
+    if (int r = decode_check(ctx, layer, B, seq_ids, pos)) return r;
+    if (!Q || !K || !V || !out) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null buffer");
+    CU_TRY(cudaSetDevice(ctx->cfg.device));
+    float *dq = ctx->io, *dk = dq + (size_t)B * 2048, *dv = dk + (size_t)B * 1024, *dout = dv + (size_t)B * 1024;
+    CU_TRY(cudaMemcpyAsync(dq, Q, (size_t)B * 2048 * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CU_TRY(cudaMemcpyAsync(dk, K, (size_t)B * 1024 * 4, cudaMemcpyHostToDevice, ctx->stream));
+    CU_TRY(cudaMemcpyAsync(dv, V, (size_t)B * 1024 * 4, cudaMemcpyHostToDevice, ctx->stream));
+    if (int r = gemma3_cuda_attn_decode_dev(ctx, layer, B, seq_ids, pos, dq, dk, dv, dout)) return r;
+    CU_TRY(cudaMemcpyAsync(out, dout, (size_t)B * 2048 * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return gemma3_cuda_synchronize(ctx);
+}
+
+// ------------------------------------------------------------------ NCCL
+extern "C" int gemma3_cuda_comm_unique_id(void *id_128_bytes) {
+    if (!id_128_bytes) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null id buffer");
+    if (int r = nccl_load()) return r;
+    g3NcclUniqueId id;
+    int nr = g_nccl.getUniqueId(&id);
+    if (nr != 0) return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "ncclGetUniqueId failed (%d)", nr);
+    memcpy(id_128_bytes, id.internal, 128);
+    return 0;
+}
+
+extern "C" int gemma3_cuda_comm_init(gemma3_cuda_ctx *ctx, const void *id_128_bytes) {
+    if (!ctx || !id_128_bytes) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null argument");
+    if (int r = nccl_load()) return r;
+    CU_TRY(cudaSetDevice(ctx->cfg.device));
+    g3NcclUniqueId id;
+    memcpy(id.internal, id_128_bytes, 128);
+    int nr = g_nccl.commInitRank(&ctx->comm, ctx->cfg.kv_ranks, id, ctx->cfg.kv_rank);
+    if (nr != 0) {
+        ctx->comm = nullptr;
+        return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "ncclCommInitRank failed: %s",
+                    g_nccl.getErrorString ? g_nccl.getErrorString(nr) : "?");
+    }
+    return 0;
+}
+
+// ------------------------------------------------------------------ cache utilities
+extern "C" int gemma3_cuda_reset(gemma3_cuda_ctx *ctx) {
+    if (!ctx) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null context");
+    CU_TRY(cudaSetDevice(ctx->cfg.device));
+    for (auto &L : ctx->layers)
+        CU_TRY(cudaMemsetAsync(L.kv, 0, (size_t)ctx->cfg.max_batch * 2 * kKvHeads * L.rows * kHeadDim * ctx->esz,
+                               ctx->stream));
+    return gemma3_cuda_synchronize(ctx);
+}
+
+static int cache_args(gemma3_cuda_ctx *ctx, int layer, int seq) {
+    if (!ctx) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null context");
+    if (layer < 0 || layer >= ctx->cfg.num_layers) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad layer %d", layer);
+    if (seq < 0 || seq >= ctx->cfg.max_batch) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad sequence slot %d", seq);
+    return 0;
+}
+
+extern "C" int gemma3_cuda_export_cache(gemma3_cuda_ctx *ctx, int layer, int seq, float *k, float *v) {
+    if (int r = cache_args(ctx, layer, seq)) return r;
+    if (!k || !v) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null buffer");
+    CU_TRY(cudaSetDevice(ctx->cfg.device));
+    const LayerState &L = ctx->layers[layer];
+    const size_t plane = (size_t)L.rows * kHeadDim, n = (size_t)L.rows * kKvHeads * kHeadDim;
+    float *tmp = nullptr;
+    CU_TRY(cudaMalloc(&tmp, n * 4));
+    for (int sel = 0; sel < 2; ++sel) {
+        const size_t off = ((size_t)seq * 2 + sel) * kKvHeads * plane;
+        if (ctx->esz == 2)
+            g3::export_rows<__nv_bfloat16><<<592, 256, 0, ctx->stream>>>(
+                reinterpret_cast<const __nv_bfloat16 *>(L.kv) + off, plane, L.rows, tmp);
+        else
+            g3::export_rows<float><<<592, 256, 0, ctx->stream>>>(reinterpret_cast<const float *>(L.kv) + off, plane,
+                                                                  L.rows, tmp);
+        if (int r = check_launch(ctx, 1)) { cudaFree(tmp); return r; }
+        cudaError_t e = cudaMemcpyAsync(sel ? v : k, tmp, n * 4, cudaMemcpyDeviceToHost, ctx->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+        if (e != cudaSuccess) {
+            cudaFree(tmp);
+            return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "export: %s", cudaGetErrorString(e));
+        }
+    }
+    cudaFree(tmp);
+    return 0;
+}
+
+extern "C" int gemma3_cuda_import_cache(gemma3_cuda_ctx *ctx, int layer, int seq, const float *k, const float *v,
+                                        int rows) {
+    if (int r = cache_args(ctx, layer, seq)) return r;
+    const LayerState &L = ctx->layers[layer];
+    if (!k || !v || rows < 0 || rows > L.rows) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad import rows %d", rows);
+    if (rows == 0) return 0;
+    CU_TRY(cudaSetDevice(ctx->cfg.device));
+    const size_t plane = (size_t)L.rows * kHeadDim, n = (size_t)rows * kKvHeads * kHeadDim;
+    float *tmp = nullptr;
+    CU_TRY(cudaMalloc(&tmp, n * 4));
+    for (int sel = 0; sel < 2; ++sel) {
+        cudaError_t e = cudaMemcpyAsync(tmp, sel ? v : k, n * 4, cudaMemcpyHostToDevice, ctx->stream);
+        if (e != cudaSuccess) { cudaFree(tmp); return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "import copy"); }
+        const size_t off = ((size_t)seq * 2 + sel) * kKvHeads * plane;
+        if (ctx->esz == 2)
+            g3::import_rows<__nv_bfloat16><<<592, 256, 0, ctx->stream>>>(
+                tmp, reinterpret_cast<__nv_bfloat16 *>(L.kv) + off, plane, rows);
+        else
+            g3::import_rows<float><<<592, 256, 0, ctx->stream>>>(tmp, reinterpret_cast<float *>(L.kv) + off, plane,
+                                                                  rows);
+        if (int r = check_launch(ctx, 1)) { cudaFree(tmp); return r; }
+    }
+    cudaError_t e = cudaStreamSynchronize(ctx->stream);
+    cudaFree(tmp);
+    if (e != cudaSuccess) return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "import: %s", cudaGetErrorString(e));
+    return 0;
+}
+
+extern "C" int gemma3_cuda_fill_cache_random(gemma3_cuda_ctx *ctx, int layer, int seq, int rows, uint64_t seed) {
+    if (int r = cache_args(ctx, layer, seq)) return r;
+    const LayerState &L = ctx->layers[layer];
+    if (rows < 0 || rows > L.rows) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad fill rows %d", rows);
+    CU_TRY(cudaSetDevice(ctx->cfg.device));
+    const size_t plane = (size_t)L.rows * kHeadDim;
+    for (int sel = 0; sel < 2; ++sel)
+        for (int h = 0; h < kKvHeads; ++h) {
+            const size_t off = (((size_t)seq * 2 + sel) * kKvHeads + h) * plane;
+            const uint64_t s = seed * 0x9E3779B97F4A7C15ull + (uint64_t)((layer * 2 + sel) * kKvHeads + h) * 0x632BE59BD9B4E019ull;
+            if (ctx->esz == 2)
+                g3::fill_normal<__nv_bfloat16><<<296, 256, 0, ctx->stream>>>(
+                    reinterpret_cast<__nv_bfloat16 *>(L.kv) + off, (size_t)rows * kHeadDim, s);
+            else
+                g3::fill_normal<float><<<296, 256, 0, ctx->stream>>>(reinterpret_cast<float *>(L.kv) + off,
+                                                                      (size_t)rows * kHeadDim, s);
+            if (int r = check_launch(ctx, 1)) return r;
+        }
+    return 0;
+}

@@ -1,0 +1,200 @@
+/*
+ * gemma3_cuda.h - C-ABI of the B200 (sm_100a) attention hot path for gemma3.c.
+ *
+ * This is the drop-in boundary for the attention core of gemma3.c: per-head
+ * QK-RMSNorm, RoPE from the host's precomputed table, KV-cache append and GQA
+ * softmax(QK^T/16)V over the cache, with the 1024-row sliding window on local
+ * layers and full causal attention on every 6th (global) layer.
+ *
+ * Shape of the API follows the reference's GPU-backend header
+ * (gemma3_metal.h:20-50): an opaque context created once at model set-up,
+ * a RoPE upload, per-call entry points and a cache reset.  The context owns
+ * the device-resident KV cache that replaces the host cache of
+ * gemma3_transformer.c:76-88 / :180-233.
+ *
+ * Conventions
+ *  - plain C11, no CUDA or torch types in any signature;
+ *  - every call returns GEMMA3_CUDA_OK (0) or a negative code whose values
+ *    equal the reference's gemma3_error enum (gemma3.h:57-67); the text of the
+ *    last failure on the calling thread is gemma3_cuda_last_error();
+ *  - there is NO CPU fallback: if the device or the kernels are unusable the
+ *    calls fail;
+ *  - one host thread drives a context; all work is ordered on the context's
+ *    own CUDA stream.  Host-pointer entry points synchronise that stream
+ *    before returning; `_dev` entry points only enqueue.
+ *
+ * Layouts at the boundary are the reference's: Q [T][8*256], K/V [T][4*256]
+ * fp32 (gemma3_transformer.c:614-639 Q_all/K_all/V_all), attention output
+ * [T][8*256] fp32 (attn_out_all, the o_proj input), QK-norm gains BF16 [256]
+ * (gemma3_transformer.c:65-66), RoPE table fp32 [max_pos][128][cos,sin]
+ * (gemma3_kernels.c:455-468).
+ */
+#ifndef GEMMA3_CUDA_H
+#define GEMMA3_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Return codes: same values as gemma3_error (gemma3.h:57-67). */
+#define GEMMA3_CUDA_OK 0
+#define GEMMA3_CUDA_ERR_INVALID_ARG (-1)
+#define GEMMA3_CUDA_ERR_OUT_OF_MEMORY (-4)
+#define GEMMA3_CUDA_ERR_GENERATION_FAILED (-7) /* device fault, timeout, launch failure */
+#define GEMMA3_CUDA_ERR_CONTEXT_OVERFLOW (-8)  /* pos >= max_context */
+
+/* Element type of the device KV cache. */
+#define GEMMA3_CUDA_KV_F32 0  /* the reference's cache dtype (bit-exact rows) */
+#define GEMMA3_CUDA_KV_BF16 1 /* half the bytes; round-to-nearest-even */
+
+/* Model dimensions + device options.  The dimension fields mirror the
+ * reference's gemma3_config (gemma3.h:82-95); only Gemma-3-4B's attention
+ * geometry (8 q heads, 4 kv heads, head_dim 256, window 1024) is supported
+ * and anything else is rejected with GEMMA3_CUDA_ERR_INVALID_ARG. */
+typedef struct {
+    int num_layers;      /* 34 */
+    int num_heads;       /* 8 */
+    int num_kv_heads;    /* 4 */
+    int head_dim;        /* 256 */
+    int sliding_window;  /* 1024 */
+    float rmsnorm_eps;   /* 1e-6 */
+    int max_context;     /* rows of a global-layer cache per sequence */
+    int max_batch;       /* number of sequence slots held in the cache */
+    int kv_dtype;        /* GEMMA3_CUDA_KV_F32 or GEMMA3_CUDA_KV_BF16 */
+    int device;          /* CUDA device ordinal */
+    int max_prefill;     /* largest T accepted by gemma3_cuda_attn_prefill */
+    /* Context-parallel split of the GLOBAL layers' KV range: this context
+     * holds positions [kv_rank*S, (kv_rank+1)*S), S = ceil(max_context /
+     * kv_ranks).  kv_ranks == 1 holds everything.  Local layers are never
+     * split. */
+    int kv_rank;
+    int kv_ranks;
+} gemma3_cuda_config;
+
+typedef struct gemma3_cuda_ctx gemma3_cuda_ctx;
+
+/* Fills *cfg with Gemma-3-4B's dimensions and single-GPU defaults
+ * (max_context 8192, max_batch 1, fp32 cache, device 0, max_prefill 8192). */
+void gemma3_cuda_config_default(gemma3_cuda_config *cfg);
+
+/* Creates a context and allocates its device KV cache.  Replaces
+ * gemma3_metal_init (gemma3_metal.h:26) and the cache allocation of
+ * gemma3_kv_cache_alloc (gemma3_transformer.c:180-214).  NULL on failure
+ * (reason in gemma3_cuda_last_error()). */
+gemma3_cuda_ctx *gemma3_cuda_init(const gemma3_cuda_config *cfg);
+
+/* Frees every device resource of the context.  Replaces gemma3_metal_free
+ * (gemma3_metal.h:29) / gemma3_kv_cache_free (gemma3_transformer.c:216). */
+void gemma3_cuda_free(gemma3_cuda_ctx *ctx);
+
+/* Uploads the host RoPE tables bit-for-bit (fp32 [max_context][head_dim/2][2]
+ * as built by gemma3_rope_precompute, gemma3_kernels.c:455-468).  Replaces
+ * gemma3_metal_upload_rope (gemma3_metal.h:36-38). */
+int gemma3_cuda_upload_rope(gemma3_cuda_ctx *ctx, const float *rope_local,
+                            const float *rope_global, int max_context,
+                            int head_dim);
+
+/* Host helper that builds a RoPE table exactly as gemma3_rope_precompute
+ * does (gemma3_kernels.c:455-468), for callers that have no table. */
+void gemma3_cuda_rope_precompute(float *freqs, int max_pos, int head_dim,
+                                 float theta);
+
+/* Sets the QK-norm gains of one layer (BF16 [head_dim] each, the stored
+ * weights w; the kernels apply 1+w as gemma3_kernels.c:301 does).  Passing
+ * NULL for either disables QK-norm for that layer, as the reference's
+ * `if (q_norm && k_norm)` does (gemma3_transformer.c:295). */
+int gemma3_cuda_set_qk_norm(gemma3_cuda_ctx *ctx, int layer,
+                            const uint16_t *q_norm, const uint16_t *k_norm);
+
+/* Prefill attention core for T consecutive tokens of sequence slot `seq` at
+ * positions start_pos..start_pos+T-1 of layer `layer`: QK-norm, RoPE,
+ * cache append and causal / sliding-window GQA.  Replaces the per-token loop
+ * of gemma3_transformer_prefill_batched (gemma3_transformer.c:641-692) with
+ * one call per layer.  Q [T][2048], K/V [T][1024] are the raw projections,
+ * out [T][2048] receives the attention output.  Host pointers. */
+int gemma3_cuda_attn_prefill(gemma3_cuda_ctx *ctx, int layer, int seq,
+                             const float *Q, const float *K, const float *V,
+                             int T, int start_pos, float *out);
+/* Same, all four arrays in device memory; enqueues only. */
+int gemma3_cuda_attn_prefill_dev(gemma3_cuda_ctx *ctx, int layer, int seq,
+                                 const float *Q, const float *K, const float *V,
+                                 int T, int start_pos, float *out);
+
+/* Decode attention core for B sequences, one new token each: sequence slot
+ * seq_ids[b] at position pos[b].  Replaces gemma3_transformer.c:294-352 of
+ * layer_attention (QK-norm, RoPE, cache_kv, seq_len/mask, gemma3_gqa) for a
+ * batch.  Q [B][2048], K/V [B][1024] raw projections, out [B][2048].
+ * seq_ids / pos are host arrays (B <= max_batch, distinct slots).  Host
+ * pointers for Q/K/V/out. */
+int gemma3_cuda_attn_decode(gemma3_cuda_ctx *ctx, int layer, int B,
+                            const int *seq_ids, const int *pos, const float *Q,
+                            const float *K, const float *V, float *out);
+/* Same with Q/K/V/out in device memory; enqueues only. */
+int gemma3_cuda_attn_decode_dev(gemma3_cuda_ctx *ctx, int layer, int B,
+                                const int *seq_ids, const int *pos,
+                                const float *Q, const float *K, const float *V,
+                                float *out);
+
+/* Context-parallel decode on a global layer whose KV range is split across
+ * kv_ranks contexts (one per GPU).  Step 1 runs on every rank and writes this
+ * rank's log-sum-exp partial for each (sequence, q head) into `partial`
+ * (device, fp32 [B][8][2+256]: running max m and sum l in the log2 domain,
+ * then the unnormalised output).  Step 2 merges n_parts such partials
+ * ([n_parts][B][8][258], device) into out [B][2048] (device).  The exchange
+ * between the steps (an all-gather over NVLink) is done by the caller, or by
+ * gemma3_cuda_attn_decode_dev when a communicator is attached. */
+int gemma3_cuda_attn_decode_partial_dev(gemma3_cuda_ctx *ctx, int layer, int B,
+                                        const int *seq_ids, const int *pos,
+                                        const float *Q, const float *K,
+                                        const float *V, float *partial);
+int gemma3_cuda_merge_partials_dev(gemma3_cuda_ctx *ctx, int n_parts, int B,
+                                   const float *partials, float *out);
+
+/* NCCL communicator for the context-parallel split (optional).  Rank 0 calls
+ * gemma3_cuda_comm_unique_id and ships the 128 opaque bytes to every rank
+ * (any host channel); each rank then calls gemma3_cuda_comm_init with its
+ * kv_rank / kv_ranks.  With a communicator attached, decode on a global layer
+ * of a split context performs partial -> all-gather -> merge internally. */
+int gemma3_cuda_comm_unique_id(void *id_128_bytes);
+int gemma3_cuda_comm_init(gemma3_cuda_ctx *ctx, const void *id_128_bytes);
+
+/* Marks every cache empty (counters only in the reference,
+ * gemma3_transformer.c:226-233; here the device cache is also zeroed, as the
+ * Metal backend does at gemma3_metal.m:989-997). */
+int gemma3_cuda_reset(gemma3_cuda_ctx *ctx);
+
+/* Debug/test: copies one sequence's cache of one layer to the host in the
+ * reference layout fp32 [rows][4][256] (rows = max_context for a global
+ * layer -- this rank's shard rows when split -- and 1024 for a local one). */
+int gemma3_cuda_export_cache(gemma3_cuda_ctx *ctx, int layer, int seq,
+                             float *k, float *v);
+/* Test/bench: fills rows [0, rows) of one sequence's cache from host fp32
+ * [rows][4][256] arrays (converted to the cache dtype). */
+int gemma3_cuda_import_cache(gemma3_cuda_ctx *ctx, int layer, int seq,
+                             const float *k, const float *v, int rows);
+/* Bench: fills rows [0, rows) of one sequence's cache on the device with
+ * seeded pseudo-random N(0,1) values (no host traffic). */
+int gemma3_cuda_fill_cache_random(gemma3_cuda_ctx *ctx, int layer, int seq,
+                                  int rows, uint64_t seed);
+
+/* The context's CUDA stream (a cudaStream_t) for callers that time or order
+ * work against it; and a blocking synchronise that reports device errors,
+ * including the bounded-wait timeout flag raised by the kernels. */
+void *gemma3_cuda_stream(gemma3_cuda_ctx *ctx);
+int gemma3_cuda_synchronize(gemma3_cuda_ctx *ctx);
+
+/* Number of kernels this context has launched since creation (instrumentation
+ * for the bench's launch count). */
+long long gemma3_cuda_launch_count(gemma3_cuda_ctx *ctx);
+
+/* Text of the last failure on this thread ("" if none). */
+const char *gemma3_cuda_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GEMMA3_CUDA_H */

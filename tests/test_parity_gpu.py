@@ -1,0 +1,208 @@
+"""Parity of the CUDA path (through the C-ABI) against the reference's own CPU
+attention (oracle/_ref, falling back to the C restatement) on seeded inputs.
+
+Tolerance (from the task statement): max |err| <= 1e-2 x RMS(reference
+output), fp32 accumulation.  Cache indexing is checked bit-exactly: the V
+rows (stored without transformation) of an fp32 cache must equal the
+reference's cache row for row, ring slots included.
+"""
+import numpy as np
+import pytest
+
+import gemma3_cuda as gc
+import synth
+from oracles import best_oracle, rel_err
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-2
+
+
+@pytest.fixture(scope="module")
+def oracle():
+    return best_oracle()
+
+
+@pytest.fixture(scope="module")
+def ropes(oracle):
+    # the integration uploads the host's own tables (gemma3_transformer.c:870-883)
+    return oracle.rope_table(8192, 10000.0), oracle.rope_table(8192, 1000000.0)
+
+
+def make_ctx(ropes, kv_dtype=gc.KV_F32, max_batch=1, max_context=8192, max_prefill=4096):
+    ctx = gc.Context(max_context=max_context, max_batch=max_batch, kv_dtype=kv_dtype, max_prefill=max_prefill)
+    ctx.upload_rope(ropes[0][:max_context], ropes[1][:max_context])
+    return ctx
+
+
+def qkv(seed, T):
+    return (synth.normal(seed, (T, gc.Q_SIZE)), synth.normal(seed + 1, (T, gc.KV_SIZE)),
+            synth.normal(seed + 2, (T, gc.KV_SIZE)))
+
+
+@pytest.mark.parametrize("layer,T,kv", [(0, 200, gc.KV_F32), (5, 300, gc.KV_F32), (0, 200, gc.KV_BF16),
+                                        (5, 300, gc.KV_BF16), (1, 1, gc.KV_F32), (11, 65, gc.KV_BF16)])
+def test_prefill_from_zero(oracle, ropes, layer, T, kv):
+    glob = gc.is_global_layer(layer)
+    rope = ropes[1] if glob else ropes[0]
+    qn, kn = synth.qk_norm_gains(100 + layer)
+    Q, K, V = qkv(7 * layer + T, T)
+    c = oracle.new_cache(glob, 8192)
+    want = oracle.attn_core_tokens(c, Q, K, V, qn, kn, rope, 0)
+    ctx = make_ctx(ropes, kv)
+    ctx.set_qk_norm(layer, qn, kn)
+    got = ctx.attn_prefill(layer, 0, Q, K, V, 0)
+    assert np.isfinite(got).all()
+    assert rel_err(got, want) <= TOL, rel_err(got, want)
+    # cache contents
+    kr, vr = oracle.cache_arrays(c)
+    kd, vd = ctx.export_cache(layer, 0)
+    rows = min(T, kd.shape[0])
+    if kv == gc.KV_F32:
+        assert np.array_equal(vd[:rows], vr[:rows])
+        assert rel_err(kd[:rows], kr[:rows]) < 1e-5
+    else:
+        assert rel_err(vd[:rows], vr[:rows]) < 1e-2
+        assert rel_err(kd[:rows], kr[:rows]) < 1e-2
+    oracle.free_cache(c)
+    ctx.close()
+
+
+def test_prefill_local_window_wrap(oracle, ropes):
+    """T=1500 on a local layer: the window slides past 1024 and the ring wraps."""
+    layer, T = 2, 1500
+    qn, kn = synth.qk_norm_gains(5)
+    Q, K, V = qkv(11, T)
+    c = oracle.new_cache(False, 8192)
+    want = oracle.attn_core_tokens(c, Q, K, V, qn, kn, ropes[0], 0)
+    ctx = make_ctx(ropes)
+    ctx.set_qk_norm(layer, qn, kn)
+    got = ctx.attn_prefill(layer, 0, Q, K, V, 0)
+    assert rel_err(got, want) <= TOL
+    # ring slots bit-exact: slot s holds the last position p with p % 1024 == s
+    kr, vr = oracle.cache_arrays(c)
+    kd, vd = ctx.export_cache(layer, 0)
+    assert np.array_equal(vd, vr)
+    oracle.free_cache(c)
+
+
+@pytest.mark.parametrize("layer,kv", [(3, gc.KV_F32), (5, gc.KV_F32), (3, gc.KV_BF16), (17, gc.KV_BF16)])
+def test_prefill_chunked(oracle, ropes, layer, kv):
+    """Two prefill calls (start_pos > 0) crossing the 1024 window edge."""
+    glob = gc.is_global_layer(layer)
+    rope = ropes[1] if glob else ropes[0]
+    qn, kn = synth.qk_norm_gains(9)
+    Q, K, V = qkv(21, 1300)
+    c = oracle.new_cache(glob, 8192)
+    want = oracle.attn_core_tokens(c, Q, K, V, qn, kn, rope, 0)
+    ctx = make_ctx(ropes, kv)
+    ctx.set_qk_norm(layer, qn, kn)
+    a = ctx.attn_prefill(layer, 0, Q[:700], K[:700], V[:700], 0)
+    b = ctx.attn_prefill(layer, 0, Q[700:], K[700:], V[700:], 700)
+    got = np.concatenate([a, b])
+    assert rel_err(got, want) <= TOL
+    oracle.free_cache(c)
+
+
+@pytest.mark.parametrize("kv", [gc.KV_F32, gc.KV_BF16])
+def test_decode_global_8192(oracle, ropes, kv):
+    """Config 1: one token at position 8191 over an 8192-row global cache."""
+    layer, pos = 5, 8191
+    c = oracle.new_cache(True, 8192)
+    kr, vr = oracle.cache_arrays(c)
+    kr[:pos] = synth.normal(31, (pos, 4, 256))
+    vr[:pos] = synth.normal(32, (pos, 4, 256))
+    if kv == gc.KV_BF16:  # the reference sees the same (rounded) cache contents
+        import torch
+        kr[:pos] = torch.from_numpy(kr[:pos]).bfloat16().float().numpy()
+        vr[:pos] = torch.from_numpy(vr[:pos]).bfloat16().float().numpy()
+    qn, kn = synth.qk_norm_gains(33)
+    Q, K, V = qkv(34, 1)
+    ctx = make_ctx(ropes, kv)
+    ctx.set_qk_norm(layer, qn, kn)
+    ctx.import_cache(layer, 0, kr[:pos].copy(), vr[:pos].copy())
+    want = oracle.attn_core_tokens(c, Q, K, V, qn, kn, ropes[1], pos)
+    got = ctx.attn_decode(layer, [0], [pos], Q, K, V)
+    assert rel_err(got, want) <= TOL
+    kd, vd = ctx.export_cache(layer, 0)
+    if kv == gc.KV_F32:
+        assert np.array_equal(vd[pos], vr[pos])
+    oracle.free_cache(c)
+
+
+def test_decode_batch_mixed(oracle, ropes):
+    """B=4 sequences at different positions on local and global layers; the
+    decode path follows a prefill, the way generation does."""
+    rng = [(0, 40), (1, 1030), (2, 2100), (3, 5)]
+    for layer in (4, 5):
+        glob = gc.is_global_layer(layer)
+        rope = ropes[1] if glob else ropes[0]
+        qn, kn = synth.qk_norm_gains(40 + layer)
+        ctx = make_ctx(ropes, gc.KV_F32, max_batch=4)
+        ctx.set_qk_norm(layer, qn, kn)
+        caches, Qd, Kd, Vd, wants = [], [], [], [], []
+        for s, n in rng:
+            Q, K, V = qkv(1000 + 10 * s + layer, n + 1)
+            c = oracle.new_cache(glob, 8192)
+            full = oracle.attn_core_tokens(c, Q, K, V, qn, kn, rope, 0)
+            ctx.attn_prefill(layer, s, Q[:n], K[:n], V[:n], 0)
+            Qd.append(Q[n]); Kd.append(K[n]); Vd.append(V[n]); wants.append(full[n])
+            caches.append(c)
+        got = ctx.attn_decode(layer, [s for s, _ in rng], [n for _, n in rng], np.stack(Qd), np.stack(Kd),
+                              np.stack(Vd))
+        for b in range(len(rng)):
+            assert rel_err(got[b], wants[b]) <= TOL, (layer, b, rel_err(got[b], wants[b]))
+        for c in caches:
+            oracle.free_cache(c)
+        ctx.close()
+
+
+def test_decode_steps_local_ring(oracle, ropes):
+    """Token-by-token decode across the ring wrap on a local layer."""
+    layer = 0
+    qn, kn = synth.qk_norm_gains(77)
+    n0, steps = 1018, 12
+    Q, K, V = qkv(55, n0 + steps)
+    c = oracle.new_cache(False, 8192)
+    want = oracle.attn_core_tokens(c, Q, K, V, qn, kn, ropes[0], 0)
+    ctx = make_ctx(ropes)
+    ctx.set_qk_norm(layer, qn, kn)
+    ctx.attn_prefill(layer, 0, Q[:n0], K[:n0], V[:n0], 0)
+    for i in range(n0, n0 + steps):
+        got = ctx.attn_decode(layer, [0], [i], Q[i:i + 1], K[i:i + 1], V[i:i + 1])
+        assert rel_err(got[0], want[i]) <= TOL, i
+    kr, vr = oracle.cache_arrays(c)
+    kd, vd = ctx.export_cache(layer, 0)
+    assert np.array_equal(vd, vr)
+    oracle.free_cache(c)
+
+
+def test_no_qk_norm(oracle, ropes):
+    """Null gains disable QK-norm, as `if (q_norm && k_norm)` does."""
+    layer, T = 0, 70
+    Q, K, V = qkv(88, T)
+    c = oracle.new_cache(False, 8192)
+    want = oracle.attn_core_tokens(c, Q, K, V, None, None, ropes[0], 0)
+    ctx = make_ctx(ropes)
+    ctx.set_qk_norm(layer, None, None)
+    got = ctx.attn_prefill(layer, 0, Q, K, V, 0)
+    assert rel_err(got, want) <= TOL
+    oracle.free_cache(c)
+
+
+def test_errors_are_reported(ropes):
+    ctx = make_ctx(ropes, max_context=2048, max_prefill=512)
+    Q, K, V = qkv(1, 1)
+    with pytest.raises(gc.Gemma3CudaError) as e:
+        ctx.attn_decode(0, [0], [2048], Q, K, V)
+    assert e.value.code == gc.ERR_CONTEXT_OVERFLOW
+    with pytest.raises(gc.Gemma3CudaError) as e:
+        ctx.attn_decode(0, [1], [3], Q, K, V)
+    assert e.value.code == gc.ERR_INVALID_ARG
+    with pytest.raises(gc.Gemma3CudaError) as e:
+        ctx.attn_decode(40, [0], [3], Q, K, V)
+    assert e.value.code == gc.ERR_INVALID_ARG
+    Q, K, V = qkv(1, 600)
+    with pytest.raises(gc.Gemma3CudaError) as e:
+        ctx.attn_prefill(0, 0, Q, K, V, 0)
+    assert e.value.code == gc.ERR_INVALID_ARG
+    ctx.synchronize()
