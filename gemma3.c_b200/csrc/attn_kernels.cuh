@@ -738,7 +738,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             // P buffer and O are owned by the tensor core until PV(i-1) is done.
             if (i >= 1 && !mbar_wait(p_empty, (i - 1) & 1, p.err)) { ok = false; break; }
             tc_fence_after();
-            if (i >= 1 && m_new > m) {
+            // tcgen05.ld/st are warp-collective: rescale when any row of the
+            // warp needs it (alpha == 1 exactly for rows whose max held).
+            if (i >= 1 && __any_sync(0xffffffffu, m_new > m)) {
 #pragma unroll 1
                 for (int c = 0; c < 8; ++c) {
                     float o[32];

@@ -17,9 +17,14 @@ enum : unsigned {
     kErrBadIndex = 2u,
 };
 
-// Polls of an mbarrier before a wait is declared dead (each try_wait itself
-// suspends for a hardware-chosen interval, so this is well over a second).
-constexpr uint32_t kMaxPolls = 1u << 24;
+// A bounded wait gives up after this much wall-clock time (globaltimer ns).
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    return t;
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -53,11 +58,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait: returns false (and raises kErrWaitTimeout in *err) if the
-// phase never completes.
+// Bounded wait: returns false if the phase does not complete within
+// kWaitLimitNs, or at once if another wait of the same launch context has
+// already failed (*err != 0), so one failure does not cascade into many
+// serial timeouts.  A failure raises kErrWaitTimeout in *err.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsigned *err) {
-    for (uint32_t i = 0; i < kMaxPolls; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t i = 1;; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 255u) == 0) {
+            if (err && *(volatile unsigned *)err) return false;
+            if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+        }
+    }
     if (err) atomicOr(err, kErrWaitTimeout);
     return false;
 }
