@@ -409,7 +409,10 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
                 mx1 = fmaxf(mx1, sc1[r]);
             }
         }
-        const float al0 = ex2_approx(m0 - mx0), al1 = ex2_approx(m1 - mx1);
+        // A warp with no valid row in this tile keeps mx == m == -inf; its
+        // rescale factor must then be 1, not 2^(-inf - -inf) = NaN.
+        const float al0 = mx0 == -INFINITY ? 1.f : ex2_approx(m0 - mx0);
+        const float al1 = mx1 == -INFINITY ? 1.f : ex2_approx(m1 - mx1);
         m0 = mx0;
         m1 = mx1;
         l0 *= al0;
@@ -476,6 +479,7 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
     if (M != -INFINITY) {
 #pragma unroll
         for (int w = 0; w < 8; ++w) {
+            if (wm[w][hh] == -INFINITY) continue;  // warp saw no row
             const float f = ex2_approx(wm[w][hh] - M);
             Ls += wl[w][hh] * f;
             A += acc[(w * 2 + hh) * kHeadDim + d] * f;
@@ -516,6 +520,7 @@ __global__ void __launch_bounds__(256) merge_partials(const float *__restrict__ 
     if (M != -INFINITY) {
         for (int i = 0; i < nparts; ++i) {
             const float *pp = base + (size_t)i * pstride;
+            if (pp[0] == -INFINITY) continue;  // empty key range
             const float f = ex2_approx(pp[0] - M);
             L += pp[1] * f;
             O += pp[2 + d] * f;

@@ -103,6 +103,7 @@ class RefOracle:
         out = np.zeros((T, NH * HD), dtype=np.float32)
         self.lib.ref_attn_core_tokens(c.h, _fp(Q), _fp(K), _fp(V), _u16(q_norm), _u16(k_norm), _fp(rope),
                                       int(c.is_global), T, start_pos, c.max_seq, _fp(out))
+        self.last_qk = (Q, K)  # the reference normalises/rotates Q and K in place
         return out
 
     def gqa(self, q, kc, vc, seq_len):
@@ -165,6 +166,7 @@ class PortOracle:
         out = np.zeros((T, NH * HD), dtype=np.float32)
         self.lib.oracle_attn_core_tokens(_fp(c.k), _fp(c.v), _fp(Q), _fp(K), _fp(V), _u16(q_norm), _u16(k_norm),
                                          _fp(rope), int(c.is_global), T, start_pos, c.max_seq, _fp(out))
+        self.last_qk = (Q, K)
         return out
 
     def gqa(self, q, kc, vc, seq_len):
@@ -184,8 +186,54 @@ def best_oracle():
 
 
 def rel_err(got, want):
-    """max |err| / RMS(want): the tolerance metric the parity tests use."""
+    """max over tokens of  max|err| / RMS(reference output of that token).
+
+    The unit is one row of [T][2048]: what one gemma3_gqa call of the
+    reference returns (gemma3_transformer.c:689-691).  A 1-D input is one
+    token.  Tolerance in the tests: 1e-2."""
     got = np.asarray(got, dtype=np.float64)
     want = np.asarray(want, dtype=np.float64)
-    rms = np.sqrt(np.mean(want * want))
-    return float(np.max(np.abs(got - want)) / max(rms, 1e-30))
+    if want.ndim == 1:
+        got, want = got[None], want[None]
+    got = got.reshape(want.shape[0], -1)
+    want = want.reshape(want.shape[0], -1)
+    rms = np.sqrt(np.mean(want * want, axis=1))
+    err = np.max(np.abs(got - want), axis=1)
+    return float(np.max(err / np.maximum(rms, 1e-30)))
+
+
+def bf16_round(x):
+    """fp32 -> nearest-even bf16 -> fp32 (what the device stores)."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    u = x.view(np.uint32).astype(np.uint64)
+    u = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16
+    return u.astype(np.uint32).view(np.float32)
+
+
+def emulated_prefill(Qn, Kn, V, start_pos, is_global, kv_prefix=None):
+    """fp32 (torch, float64 accumulate) attention on bf16-rounded operands:
+    the arithmetic the tensor-core prefill performs, used as a tight check of
+    the kernel itself.  Qn/Kn are the normalised+rotated rows [T][...];
+    kv_prefix = (K, V) rows for positions [0, start_pos) or None."""
+    import torch
+    T = Qn.shape[0]
+    Kall, Vall = Kn, V
+    if kv_prefix is not None:
+        Kall = np.concatenate([kv_prefix[0], Kn])
+        Vall = np.concatenate([kv_prefix[1], V])
+    q = torch.from_numpy(bf16_round(Qn).reshape(T, NH, HD)).double()
+    k = torch.from_numpy(bf16_round(Kall).reshape(-1, NKV, HD)).double()
+    v = torch.from_numpy(bf16_round(Vall).reshape(-1, NKV, HD)).double()
+    L = k.shape[0]
+    qpos = torch.arange(start_pos, start_pos + T)[:, None]
+    kpos = torch.arange(0, L)[None, :]
+    ok = kpos <= qpos
+    if not is_global:
+        ok &= kpos > qpos - WINDOW
+    out = torch.empty(T, NH, HD, dtype=torch.float64)
+    for h in range(NH):
+        s = (q[:, h] @ k[:, h // 2].T) / 16.0
+        s = s.masked_fill(~ok, float("-inf"))
+        p = torch.softmax(s, dim=1)
+        out[:, h] = p @ v[:, h // 2]
+    return out.reshape(T, NH * HD).float().numpy()

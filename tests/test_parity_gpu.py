@@ -11,7 +11,7 @@ import pytest
 
 import gemma3_cuda as gc
 import synth
-from oracles import best_oracle, rel_err
+from oracles import best_oracle, emulated_prefill, rel_err
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-2
@@ -48,11 +48,15 @@ def test_prefill_from_zero(oracle, ropes, layer, T, kv):
     Q, K, V = qkv(7 * layer + T, T)
     c = oracle.new_cache(glob, 8192)
     want = oracle.attn_core_tokens(c, Q, K, V, qn, kn, rope, 0)
+    Qn, Kn = oracle.last_qk
     ctx = make_ctx(ropes, kv)
     ctx.set_qk_norm(layer, qn, kn)
     got = ctx.attn_prefill(layer, 0, Q, K, V, 0)
     assert np.isfinite(got).all()
     assert rel_err(got, want) <= TOL, rel_err(got, want)
+    # the kernel itself: same result as exact attention on bf16 operands
+    emu = emulated_prefill(Qn, Kn, V, 0, glob)
+    assert rel_err(got, emu) <= 4e-3, rel_err(got, emu)
     # cache contents
     kr, vr = oracle.cache_arrays(c)
     kd, vd = ctx.export_cache(layer, 0)
@@ -74,10 +78,12 @@ def test_prefill_local_window_wrap(oracle, ropes):
     Q, K, V = qkv(11, T)
     c = oracle.new_cache(False, 8192)
     want = oracle.attn_core_tokens(c, Q, K, V, qn, kn, ropes[0], 0)
+    Qn, Kn = oracle.last_qk
     ctx = make_ctx(ropes)
     ctx.set_qk_norm(layer, qn, kn)
     got = ctx.attn_prefill(layer, 0, Q, K, V, 0)
     assert rel_err(got, want) <= TOL
+    assert rel_err(got, emulated_prefill(Qn, Kn, V, 0, False)) <= 4e-3
     # ring slots bit-exact: slot s holds the last position p with p % 1024 == s
     kr, vr = oracle.cache_arrays(c)
     kd, vd = ctx.export_cache(layer, 0)
