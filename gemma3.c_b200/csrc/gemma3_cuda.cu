@@ -3,11 +3,12 @@
 // One context = one GPU = one CUDA stream.  The context owns the device KV
 // cache of all 34 layers for max_batch sequence slots, the uploaded RoPE
 // tables, the per-layer QK-norm gains and the scratch the kernels need
-// (bf16 Q/K/V staging for prefill, split-KV partials for decode, device
+// (fp16 Q/K/V staging for prefill, split-KV partials for decode, device
 // copies of host arguments).  Nothing on the compute path falls back to the
 // CPU: a failure is reported through the return code.
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <dlfcn.h>
 
@@ -98,14 +99,14 @@ static int load_encode() {
     g_encode = (EncodeTiledFn)fn;
     return 0;
 }
-// bf16 tensor [planes][rows][256] (planes stride given), box 64 x 64 x 1,
+// fp16 tensor [planes][rows][256] (planes stride given), box 64 x 64 x 1,
 // 128-byte swizzle.
 static int make_map(CUtensorMap *m, const void *base, int rows, size_t plane_stride_elems, int planes) {
     cuuint64_t dims[3] = {(cuuint64_t)kHeadDim, (cuuint64_t)rows, (cuuint64_t)planes};
     cuuint64_t strides[2] = {(cuuint64_t)kHeadDim * 2, (cuuint64_t)plane_stride_elems * 2};
     cuuint32_t box[3] = {64, 64, 1};
     cuuint32_t estr[3] = {1, 1, 1};
-    CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, estr,
+    CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void *>(base), dims, strides, box, estr,
                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "cuTensorMapEncodeTiled failed (%d)", (int)r);
@@ -130,8 +131,8 @@ struct gemma3_cuda_ctx {
     float *rope_local = nullptr, *rope_global = nullptr;
     int rope_rows = 0;
     // prefill scratch
-    __nv_bfloat16 *qst = nullptr;             // [8][max_prefill][256]
-    __nv_bfloat16 *kst = nullptr, *vst = nullptr;  // [4][st_rows][256]
+    __half *qst = nullptr;                 // [8][max_prefill][256] fp16
+    __half *kst = nullptr, *vst = nullptr;  // [4][st_rows][256] fp16
     int st_rows = 0;
     // decode scratch
     float *qdec = nullptr;     // [max_batch][8][256]
@@ -282,7 +283,9 @@ extern "C" int gemma3_cuda_synchronize(gemma3_cuda_ctx *ctx) {
         cudaMemsetAsync(ctx->err, 0, sizeof(unsigned), ctx->stream);
         cudaStreamSynchronize(ctx->stream);
         return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "device status 0x%x (%s)", e,
-                    (e & g3::kErrWaitTimeout) ? "bounded wait timed out" : "bad index");
+                    (e & g3::kErrWaitTimeout) ? "bounded wait timed out"
+                    : (e & g3::kErrRange)     ? "prefill operand outside the fp16 range"
+                                              : "bad index");
     }
     return 0;
 }
@@ -361,13 +364,11 @@ static int check_launch(gemma3_cuda_ctx *ctx, int n) {
 template <typename KVT>
 static int prefill_impl(gemma3_cuda_ctx *ctx, int layer, int seq, const float *Q, const float *K, const float *V,
                         int T, int start_pos, float *out) {
-    const LayerState &LS = ctx->layers[layer];
     g3::LayerDev L = layer_dev(ctx, layer);
-    const bool global = LS.is_global;
+    const bool global = ctx->layers[layer].is_global;
     const int kv_pos0 = global ? 0 : std::max(0, start_pos - (kWindow - 1));
     const int lrows = start_pos + T - kv_pos0;  // key rows the attention sees
-    const bool direct = global && sizeof(KVT) == 2;  // bf16 global cache is already linear
-    if (!direct && ctx->st_rows < lrows) {
+    if (ctx->st_rows < lrows) {
         cudaFree(ctx->kst);
         cudaFree(ctx->vst);
         ctx->kst = ctx->vst = nullptr;
@@ -378,28 +379,21 @@ static int prefill_impl(gemma3_cuda_ctx *ctx, int layer, int seq, const float *Q
         ctx->st_rows = want;
     }
     const int nprefix = start_pos - kv_pos0;
-    if (!direct && nprefix > 0) {
+    if (nprefix > 0) {
         g3::stage_prefix<KVT><<<dim3(nprefix, 8), 32, 0, ctx->stream>>>(L, seq, kv_pos0, ctx->kst, ctx->vst,
-                                                                          ctx->st_rows);
+                                                                          ctx->st_rows, ctx->err);
         if (int r = check_launch(ctx, 1)) return r;
     }
-    g3::prologue_prefill<KVT><<<dim3(T, 16), 128, 0, ctx->stream>>>(
-        Q, K, V, L, ctx->cfg.rmsnorm_eps, seq, T, start_pos, kv_pos0, ctx->qst, direct ? nullptr : ctx->kst,
-        direct ? nullptr : ctx->vst, ctx->st_rows);
+    g3::prologue_prefill<KVT><<<dim3(T, 16), 128, 0, ctx->stream>>>(Q, K, V, L, ctx->cfg.rmsnorm_eps, seq, T,
+                                                                     start_pos, kv_pos0, ctx->qst, ctx->kst,
+                                                                     ctx->vst, ctx->st_rows, ctx->err);
     if (int r = check_launch(ctx, 1)) return r;
 
     CUtensorMap tq, tk, tv;
+    const size_t plane = (size_t)ctx->st_rows * kHeadDim;
     if (int r = make_map(&tq, ctx->qst, T, (size_t)T * kHeadDim, kHeads)) return r;
-    if (direct) {
-        const size_t plane = (size_t)LS.rows * kHeadDim;
-        const __nv_bfloat16 *kbase = reinterpret_cast<const __nv_bfloat16 *>(LS.kv) + (size_t)seq * 2 * kKvHeads * plane;
-        if (int r = make_map(&tk, kbase, lrows, plane, kKvHeads)) return r;
-        if (int r = make_map(&tv, kbase + kKvHeads * plane, lrows, plane, kKvHeads)) return r;
-    } else {
-        const size_t plane = (size_t)ctx->st_rows * kHeadDim;
-        if (int r = make_map(&tk, ctx->kst, lrows, plane, kKvHeads)) return r;
-        if (int r = make_map(&tv, ctx->vst, lrows, plane, kKvHeads)) return r;
-    }
+    if (int r = make_map(&tk, ctx->kst, lrows, plane, kKvHeads)) return r;
+    if (int r = make_map(&tv, ctx->vst, lrows, plane, kKvHeads)) return r;
     g3::PrefillParams p;
     p.out = out;
     p.T = T;

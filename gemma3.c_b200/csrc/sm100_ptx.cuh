@@ -15,6 +15,7 @@ namespace g3 {
 enum : unsigned {
     kErrWaitTimeout = 1u,
     kErrBadIndex = 2u,
+    kErrRange = 4u,  // a prefill operand exceeded the fp16 range
 };
 
 // A bounded wait gives up after this much wall-clock time (globaltimer ns).
@@ -187,18 +188,24 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
     return d;
 }
 
-// Instruction descriptor for kind::f16 with bf16 A/B and fp32 D.
-// a_mn / b_mn select MN-major operands (bits 15/16); N>>3 in bits 17-22,
-// M>>4 in bits 24-28.
-__host__ __device__ constexpr uint32_t idesc_bf16_f32(int M, int N, int a_mn, int b_mn) {
-    return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) |
-           ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+// Instruction descriptor for kind::f16 with fp16 A/B (format 0 in bits
+// 7-9 and 10-12) and fp32 D (1 in bits 4-5).  a_mn / b_mn select MN-major
+// operands (bits 15/16); N>>3 in bits 17-22, M>>4 in bits 24-28.
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, int a_mn, int b_mn) {
+    return (1u << 4) | ((uint32_t)a_mn << 15) | ((uint32_t)b_mn << 16) | ((uint32_t)(N >> 3) << 17) |
+           ((uint32_t)(M >> 4) << 24);
 }
 
 __device__ __forceinline__ float ex2_approx(float x) {
     float y;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
     return y;
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {

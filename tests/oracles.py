@@ -210,20 +210,23 @@ def bf16_round(x):
     return u.astype(np.uint32).view(np.float32)
 
 
-def emulated_prefill(Qn, Kn, V, start_pos, is_global, kv_prefix=None):
-    """fp32 (torch, float64 accumulate) attention on bf16-rounded operands:
-    the arithmetic the tensor-core prefill performs, used as a tight check of
-    the kernel itself.  Qn/Kn are the normalised+rotated rows [T][...];
-    kv_prefix = (K, V) rows for positions [0, start_pos) or None."""
+def exact_attention(Qn, Kn, V, start_pos, is_global, kv_round=None, kv_prefix=None):
+    """float64 torch attention of the reference's semantics (causal, 1024
+    window on local layers, scale 1/16) over the normalised+rotated Qn/Kn
+    the reference produced.  kv_round='bf16' stores K/V rows as a bf16 cache
+    holds them (round-to-nearest-even): the reference's semantics on a BF16
+    cache.  kv_prefix = (K, V) rows for positions [0, start_pos) or None."""
     import torch
     T = Qn.shape[0]
     Kall, Vall = Kn, V
     if kv_prefix is not None:
         Kall = np.concatenate([kv_prefix[0], Kn])
         Vall = np.concatenate([kv_prefix[1], V])
-    q = torch.from_numpy(bf16_round(Qn).reshape(T, NH, HD)).double()
-    k = torch.from_numpy(bf16_round(Kall).reshape(-1, NKV, HD)).double()
-    v = torch.from_numpy(bf16_round(Vall).reshape(-1, NKV, HD)).double()
+    if kv_round == "bf16":
+        Kall, Vall = bf16_round(Kall), bf16_round(Vall)
+    q = torch.from_numpy(np.ascontiguousarray(Qn, dtype=np.float32).reshape(T, NH, HD)).double()
+    k = torch.from_numpy(np.ascontiguousarray(Kall, dtype=np.float32).reshape(-1, NKV, HD)).double()
+    v = torch.from_numpy(np.ascontiguousarray(Vall, dtype=np.float32).reshape(-1, NKV, HD)).double()
     L = k.shape[0]
     qpos = torch.arange(start_pos, start_pos + T)[:, None]
     kpos = torch.arange(0, L)[None, :]
@@ -234,6 +237,5 @@ def emulated_prefill(Qn, Kn, V, start_pos, is_global, kv_prefix=None):
     for h in range(NH):
         s = (q[:, h] @ k[:, h // 2].T) / 16.0
         s = s.masked_fill(~ok, float("-inf"))
-        p = torch.softmax(s, dim=1)
-        out[:, h] = p @ v[:, h // 2]
+        out[:, h] = torch.softmax(s, dim=1) @ v[:, h // 2]
     return out.reshape(T, NH * HD).float().numpy()
