@@ -145,7 +145,31 @@ struct gemma3_cuda_ctx {
     unsigned *err = nullptr;
     long long launches = 0;
     g3NcclComm comm = nullptr;
+    // profiling of the dominant kernels (decode_splitkv = 0, prefill_fa = 1)
+    bool prof = false;
+    std::vector<cudaEvent_t> ev_pool;
+    size_t ev_used = 0;
+    struct Span { int kind; size_t e0, e1; double work; };
+    std::vector<Span> spans;
 };
+
+// Events bracketing one launch of a profiled kernel, with its algorithmic
+// work (bytes for decode, FLOPs for prefill).
+static size_t prof_event(gemma3_cuda_ctx *c) {
+    if (c->ev_used == c->ev_pool.size()) {
+        cudaEvent_t e;
+        if (cudaEventCreate(&e) != cudaSuccess) return (size_t)-1;
+        c->ev_pool.push_back(e);
+    }
+    cudaEventRecord(c->ev_pool[c->ev_used], c->stream);
+    return c->ev_used++;
+}
+static void prof_begin(gemma3_cuda_ctx *c, size_t *e0) { *e0 = c->prof ? prof_event(c) : (size_t)-1; }
+static void prof_end(gemma3_cuda_ctx *c, int kind, size_t e0, double work) {
+    if (!c->prof || e0 == (size_t)-1) return;
+    size_t e1 = prof_event(c);
+    if (e1 != (size_t)-1) c->spans.push_back({kind, e0, e1, work});
+}
 
 static constexpr int kMaxSplit = 128;
 static constexpr int kPartialStride = kHeadDim + 2;
@@ -190,6 +214,7 @@ static void ctx_release(gemma3_cuda_ctx *c) {
     cudaFree(c->gather);
     cudaFree(c->io);
     cudaFree(c->err);
+    for (auto e : c->ev_pool) cudaEventDestroy(e);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
 }
@@ -402,7 +427,18 @@ static int prefill_impl(gemma3_cuda_ctx *ctx, int layer, int seq, const float *Q
     p.is_global = global;
     p.err = ctx->err;
     const int nqb = (T + 63) / 64;
+    size_t e0;
+    prof_begin(ctx, &e0);
     g3::prefill_fa_sm100<<<dim3(nqb, kKvHeads), g3::kPfThreads, g3::kPfSmem, ctx->stream>>>(tq, tk, tv, p);
+    if (ctx->prof) {
+        // algorithmic FLOPs: 2 (QK) + 2 (PV) x 256 x 8 heads per attended key
+        double keys = 0;
+        for (int t = 0; t < T; ++t) {
+            const int pos = start_pos + t;
+            keys += global ? pos + 1 : std::min(pos + 1, kWindow);
+        }
+        prof_end(ctx, 1, e0, keys * 4.0 * kHeadDim * kHeads);
+    }
     return check_launch(ctx, 1);
 }
 
@@ -524,7 +560,15 @@ static int decode_impl(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_id
     p.write_partial = (pl.nsplit > 1 || partial_out) ? 1 : 0;
     p.err = ctx->err;
     constexpr int smem = g3::DecodeCfg<KVT>::NS * 2 * g3::DecodeCfg<KVT>::TK * kHeadDim * sizeof(KVT);
+    size_t e0;
+    prof_begin(ctx, &e0);
     g3::decode_splitkv<KVT><<<dim3(pl.nsplit, kKvHeads, B), 256, smem, ctx->stream>>>(p, pl.rows);
+    if (ctx->prof) {
+        // algorithmic bytes: every attended K and V row once
+        double rows = 0;
+        for (int b = 0; b < B; ++b) rows += pl.rows.nrows[b];
+        prof_end(ctx, 0, e0, rows * kKvHeads * 2.0 * kHeadDim * sizeof(KVT));
+    }
     if (int r = check_launch(ctx, 1)) return r;
     if (p.write_partial) {
         const size_t hs = (size_t)pl.nsplit * kPartialStride;
@@ -713,5 +757,37 @@ extern "C" int gemma3_cuda_fill_cache_random(gemma3_cuda_ctx *ctx, int layer, in
                                                                       (size_t)rows * kHeadDim, s);
             if (int r = check_launch(ctx, 1)) return r;
         }
+    return 0;
+}
+
+// ------------------------------------------------------------------ profiling
+extern "C" int gemma3_cuda_profile(gemma3_cuda_ctx *ctx, int enable) {
+    if (!ctx) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null context");
+    CU_TRY(cudaSetDevice(ctx->cfg.device));
+    CU_TRY(cudaStreamSynchronize(ctx->stream));
+    ctx->prof = enable != 0;
+    ctx->spans.clear();
+    ctx->ev_used = 0;
+    return 0;
+}
+
+extern "C" int gemma3_cuda_profile_read(gemma3_cuda_ctx *ctx, int kernel, long long *launches, double *ms,
+                                        double *work) {
+    if (!ctx || !launches || !ms || !work) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null argument");
+    CU_TRY(cudaSetDevice(ctx->cfg.device));
+    CU_TRY(cudaStreamSynchronize(ctx->stream));
+    long long n = 0;
+    double t = 0, w = 0;
+    for (const auto &sp : ctx->spans) {
+        if (sp.kind != kernel) continue;
+        float f = 0;
+        CU_TRY(cudaEventElapsedTime(&f, ctx->ev_pool[sp.e0], ctx->ev_pool[sp.e1]));
+        ++n;
+        t += f;
+        w += sp.work;
+    }
+    *launches = n;
+    *ms = t;
+    *work = w;
     return 0;
 }

@@ -97,6 +97,9 @@ SIGNATURES = {
     "gemma3_cuda_stream": (_P, [_P]),
     "gemma3_cuda_synchronize": (_I, [_P]),
     "gemma3_cuda_launch_count": (ctypes.c_longlong, [_P]),
+    "gemma3_cuda_profile": (_I, [_P, _I]),
+    "gemma3_cuda_profile_read": (_I, [_P, _I, ctypes.POINTER(ctypes.c_longlong), ctypes.POINTER(ctypes.c_double),
+                                      ctypes.POINTER(ctypes.c_double)]),
     "gemma3_cuda_last_error": (ctypes.c_char_p, []),
 }
 
@@ -195,6 +198,15 @@ class Context:
 
     def launch_count(self) -> int:
         return int(self.lib.gemma3_cuda_launch_count(self.h))
+
+    def profile(self, enable: bool):
+        self._chk(self.lib.gemma3_cuda_profile(self.h, int(enable)))
+
+    def profile_read(self, kernel: int):
+        """(launches, device ms, algorithmic work) of kernel 0 (decode) / 1 (prefill)."""
+        n, ms, w = ctypes.c_longlong(), ctypes.c_double(), ctypes.c_double()
+        self._chk(self.lib.gemma3_cuda_profile_read(self.h, kernel, ctypes.byref(n), ctypes.byref(ms), ctypes.byref(w)))
+        return n.value, ms.value, w.value
 
     # -- model set-up -----------------------------------------------------
     def upload_rope(self, rope_local: np.ndarray, rope_global: np.ndarray):

@@ -190,6 +190,16 @@ int gemma3_cuda_synchronize(gemma3_cuda_ctx *ctx);
  * for the bench's launch count). */
 long long gemma3_cuda_launch_count(gemma3_cuda_ctx *ctx);
 
+/* Instrumentation (no counterpart in the reference, which has no timers).
+ * gemma3_cuda_profile(ctx, 1) starts recording a CUDA event pair around
+ * every launch of the two dominant kernels (and clears earlier records);
+ * gemma3_cuda_profile_read sums, for kernel 0 = split-KV decode or
+ * 1 = tensor-core prefill, the launches, their device time in ms and their
+ * algorithmic work: K/V bytes read (decode) or FLOPs (prefill). */
+int gemma3_cuda_profile(gemma3_cuda_ctx *ctx, int enable);
+int gemma3_cuda_profile_read(gemma3_cuda_ctx *ctx, int kernel, long long *launches,
+                             double *ms, double *work);
+
 /* Text of the last failure on this thread ("" if none). */
 const char *gemma3_cuda_last_error(void);
 

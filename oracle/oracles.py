@@ -1,4 +1,7 @@
-"""ctypes front-ends of the CPU checkers (test infrastructure only).
+"""ctypes front-ends of the CPU checkers.
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and
+bench.py's CPU-baseline / reference legs, never by the shipped library.
 
   RefOracle  - the reference's own code (gemma3_kernels.c +
                gemma3_transformer.c statics), compiled by oracle/Makefile into
@@ -15,8 +18,7 @@ import subprocess
 
 import numpy as np
 
-ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-ORACLE = os.path.join(ROOT, "oracle")
+ORACLE = os.path.dirname(os.path.abspath(__file__))
 REF_SO = os.path.join(ORACLE, "_ref", "libgemma3_ref.so")
 PORT_SO = os.path.join(ORACLE, "libattn_oracle.so")
 
