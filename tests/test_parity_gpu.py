@@ -67,7 +67,9 @@ def test_prefill_from_zero(oracle, ropes, layer, T, kv):
         assert rel_err(kd[:rows], kr[:rows]) < 1e-5
     else:  # a bf16 cache holds the round-to-nearest-even value of each row
         assert np.array_equal(vd[:rows], bf16_round(vr[:rows]))
-        assert np.all(np.abs(kd[:rows] - kr[:rows]) <= 2.0 ** -8 * np.abs(kr[:rows]) + 1e-30)
+        # K is recomputed in fp32 on both sides, so the rounding may land one
+        # bf16 ulp (<= 2^-7 relative) apart
+        assert np.all(np.abs(kd[:rows] - kr[:rows]) <= 2.0 ** -7 * np.abs(kr[:rows]) + 1e-6)
     oracle.free_cache(c)
     ctx.close()
 
