@@ -12,6 +12,8 @@
 #include <cuda_runtime.h>
 #include <dlfcn.h>
 
+#include <mutex>
+
 #include <algorithm>
 #include <cmath>
 #include <cstdarg>
@@ -789,5 +791,122 @@ extern "C" int gemma3_cuda_profile_read(gemma3_cuda_ctx *ctx, int kernel, long l
     *launches = n;
     *ms = t;
     *work = w;
+    return 0;
+}
+
+// ------------------------------------------------------------------ decode without allocation
+// For callers that cannot allocate device memory: code that runs while a
+// CUDA graph is being captured, hosts whose memory budget is fixed when the
+// process starts, and embedders that hand every device buffer in themselves.
+// The split-KV decode needs scratch (the scaled queries and the per-split
+// (m, l, O) partials); here it lives in one file-scope device array that
+// every GPU which loads this library holds until the process exits.
+namespace {
+constexpr int kNoAllocMaxBatch = 64;
+constexpr int kNoAllocMaxSlots = 4096;  // (sequence, head, split) partials
+constexpr size_t kNoAllocQ = (size_t)kNoAllocMaxBatch * kHeads * kHeadDim;  // 512 KB
+constexpr size_t kNoAllocPart = (size_t)kNoAllocMaxSlots * kPartialStride;  // 4.03 MB
+constexpr size_t kNoAllocStatus = 64;                                      // status word + pad
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float *g_noalloc_addr[kNoAllocMaxDevices] = {};
+}  // namespace
+
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocQ + kNoAllocPart + kNoAllocStatus];
+
+__global__ void noalloc_scale_q(const float *__restrict__ q, float *__restrict__ dst, int n) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) dst[i] = q[i] * g3::kScaleLog2;
+}
+
+extern "C" int gemma3_cuda_gqa_decode_noalloc(const float *q, const void *kv, int kv_dtype, int rows, int B,
+                                              const int *nrows, float *out, void *stream) {
+    if (!q || !kv || !nrows || !out) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null argument");
+    if (kv_dtype != GEMMA3_CUDA_KV_F32 && kv_dtype != GEMMA3_CUDA_KV_BF16)
+        return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad kv_dtype %d", kv_dtype);
+    if (B < 1 || B > kNoAllocMaxBatch)
+        return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "B=%d outside 1..%d: the no-allocation scratch holds at most %d sequences",
+                    B, kNoAllocMaxBatch, kNoAllocMaxBatch);
+    if (rows < 1) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "rows must be >= 1");
+    int maxrows = 0;
+    long long total = 0;
+    for (int b = 0; b < B; ++b) {
+        if (nrows[b] < 1 || nrows[b] > rows)
+            return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "nrows[%d]=%d outside 1..rows=%d", b, nrows[b], rows);
+        maxrows = std::max(maxrows, nrows[b]);
+        total += (long long)nrows[b] * kKvHeads;
+    }
+    int dev = 0;
+    CU_TRY(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kNoAllocMaxDevices) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "device %d unsupported", dev);
+    float *scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        if (!g_noalloc_addr[dev]) {
+            // One-time set-up on this device (the current one): resolve the
+            // array's device address; the host-side symbol is not it.
+            void *p = nullptr;
+            CU_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+            const int smem_bf = g3::DecodeCfg<__nv_bfloat16>::NS * 2 * g3::DecodeCfg<__nv_bfloat16>::TK * kHeadDim * 2;
+            const int smem_f = g3::DecodeCfg<float>::NS * 2 * g3::DecodeCfg<float>::TK * kHeadDim * 4;
+            CU_TRY(cudaFuncSetAttribute(g3::decode_splitkv<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        smem_bf));
+            CU_TRY(cudaFuncSetAttribute(g3::decode_splitkv<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_f));
+            g_noalloc_addr[dev] = static_cast<float *>(p);
+        }
+        scratch = g_noalloc_addr[dev];
+    }
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    float *qs = scratch;
+    float *part = scratch + kNoAllocQ;
+    unsigned *status = reinterpret_cast<unsigned *>(scratch + kNoAllocQ + kNoAllocPart);
+    CU_TRY(cudaMemsetAsync(status, 0, sizeof(unsigned), st));
+
+    // Split plan as for the context path, capped by the scratch slots.
+    const bool bf = kv_dtype == GEMMA3_CUDA_KV_BF16;
+    const int TK = bf ? g3::DecodeCfg<__nv_bfloat16>::TK : g3::DecodeCfg<float>::TK;
+    const long long target = 148LL * 8;
+    const int max_split = std::max(1, kNoAllocMaxSlots / (B * kHeads));
+    long long chunk = std::max<long long>(4 * TK, (total + target - 1) / target);
+    chunk = std::max<long long>(chunk, (maxrows + max_split - 1) / max_split);
+    chunk = (chunk + TK - 1) / TK * TK;
+    const int nsplit = (int)((maxrows + chunk - 1) / chunk);
+
+    const int nq = B * kHeads * kHeadDim;
+    noalloc_scale_q<<<(nq + 255) / 256, 256, 0, st>>>(q, qs, nq);
+
+    g3::DecodeRows rws;
+    rws.B = B;
+    for (int b = 0; b < B; ++b) {
+        rws.seq[b] = b;
+        rws.nrows[b] = nrows[b];
+    }
+    g3::DecodeParams p;
+    p.q = qs;
+    p.L.kv = const_cast<void *>(kv);
+    p.L.rows = rows;
+    p.L.is_global = 1;
+    p.L.shard_lo = 0;
+    p.L.shard_hi = rows;
+    p.L.qn = p.L.kn = nullptr;
+    p.L.rope = nullptr;
+    p.chunk = (int)chunk;
+    p.nsplit = nsplit;
+    p.partial = part;
+    p.out = nullptr;
+    p.write_partial = 1;
+    p.err = status;
+    if (bf) {
+        constexpr int smem = g3::DecodeCfg<__nv_bfloat16>::NS * 2 * g3::DecodeCfg<__nv_bfloat16>::TK * kHeadDim * 2;
+        g3::decode_splitkv<__nv_bfloat16><<<dim3(nsplit, kKvHeads, B), 256, smem, st>>>(p, rws);
+    } else {
+        constexpr int smem = g3::DecodeCfg<float>::NS * 2 * g3::DecodeCfg<float>::TK * kHeadDim * 4;
+        g3::decode_splitkv<float><<<dim3(nsplit, kKvHeads, B), 256, smem, st>>>(p, rws);
+    }
+    const size_t hs = (size_t)nsplit * kPartialStride;
+    g3::merge_partials<<<B * kHeads, 256, 0, st>>>(part, nsplit, kHeads * hs, hs, kPartialStride, out, nullptr);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess)
+        return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "kernel launch failed: %s", cudaGetErrorString(e));
     return 0;
 }

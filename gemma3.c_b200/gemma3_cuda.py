@@ -100,6 +100,7 @@ SIGNATURES = {
     "gemma3_cuda_profile": (_I, [_P, _I]),
     "gemma3_cuda_profile_read": (_I, [_P, _I, ctypes.POINTER(ctypes.c_longlong), ctypes.POINTER(ctypes.c_double),
                                       ctypes.POINTER(ctypes.c_double)]),
+    "gemma3_cuda_gqa_decode_noalloc": (_I, [_P, _P, _I, _I, _I, _IP, _P, _P]),
     "gemma3_cuda_last_error": (ctypes.c_char_p, []),
 }
 
@@ -145,6 +146,17 @@ def rope_table(max_pos: int, theta: float) -> np.ndarray:
     t = np.empty((max_pos, HEAD_DIM // 2, 2), dtype=np.float32)
     lib.gemma3_cuda_rope_precompute(_fptr(t), max_pos, HEAD_DIM, ctypes.c_float(theta))
     return t
+
+
+def gqa_decode_noalloc(q_ptr: int, kv_ptr: int, kv_dtype: int, rows: int, nrows, out_ptr: int, stream: int = 0):
+    """gemma3_cuda_gqa_decode_noalloc: decode over a caller-owned device cache
+    [B][K,V][4][rows][256] with no device allocation (scratch is a static
+    device array).  Enqueues on `stream`."""
+    lib = load_library()
+    a, ap = _iarr(nrows)
+    rc = lib.gemma3_cuda_gqa_decode_noalloc(q_ptr, kv_ptr, kv_dtype, rows, len(a), ap, out_ptr, stream or None)
+    if rc != 0:
+        raise Gemma3CudaError(rc, (lib.gemma3_cuda_last_error() or b"").decode())
 
 
 class Context:

@@ -200,6 +200,29 @@ int gemma3_cuda_profile(gemma3_cuda_ctx *ctx, int enable);
 int gemma3_cuda_profile_read(gemma3_cuda_ctx *ctx, int kernel, long long *launches,
                              double *ms, double *work);
 
+/* GQA decode that allocates no memory.  No counterpart in the reference: it
+ * exists for callers that cannot allocate device memory -- code running while
+ * a CUDA graph is captured, processes whose device memory budget is fixed up
+ * front, embedders that supply every buffer themselves.  It runs the same
+ * split-KV kernels as gemma3_cuda_attn_decode_dev on a cache the caller owns,
+ * keeping its scratch (scaled queries and split partials) in a static device
+ * array of 4.6 MB that every GPU loading this library holds until exit.
+ *   q      device fp32 [B][8][256], already QK-normed and rotated (the q that
+ *          gemma3_gqa receives, gemma3_kernels.h:188);
+ *   kv     device cache, layout [B][K,V][4][rows][256] in kv_dtype;
+ *   nrows  host int[B], rows 0..nrows[b]-1 of sequence b are attended
+ *          (1 <= nrows[b] <= rows);
+ *   out    device fp32 [B][8*256];
+ *   stream cudaStream_t to enqueue on (NULL = legacy default stream).
+ * Limits: 1 <= B <= 64 (larger B is rejected with GEMMA3_CUDA_ERR_INVALID_ARG).
+ * The first call on a device resolves the array's address on that device
+ * (the current one), so make it before any stream capture.  All calls share
+ * the one array: calls that overlap on the GPU (other streams, other host
+ * threads) race and must be serialised by the caller.  Enqueues only. */
+int gemma3_cuda_gqa_decode_noalloc(const float *q, const void *kv, int kv_dtype,
+                                   int rows, int B, const int *nrows, float *out,
+                                   void *stream);
+
 /* Text of the last failure on this thread ("" if none). */
 const char *gemma3_cuda_last_error(void);
 
