@@ -57,6 +57,8 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true", help="skip the configs[1]/[2] figures")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-case", choices=["decode", "prefill"],
+                    help="tiny workload for ncu captures: 3 launches of the kernel, ~1-2 GB on the device")
     ap.add_argument("--seqs", type=int, default=B_TOTAL,
                     help="override the 64 sequences (small cases for ncu captures only)")
     return ap.parse_args()
@@ -474,10 +476,50 @@ def ncu_traffic(kernel):
     return None
 
 
+def profile_case(args):
+    """Few-launch cases for `ncu --set full` (one GPU, about 1-2 GB resident,
+    inputs still larger than L2): decode = global layer, 8 sequences x 32769
+    rows (1.07 GB of BF16 KV); prefill = one global and one local layer at
+    T=8192."""
+    import torch
+    import gemma3_cuda as gc
+    import synth
+    if args.profile_case == "decode":
+        B = 8
+        ctx = gc.Context(max_context=POS + 1, max_batch=B, kv_dtype=gc.KV_BF16, max_prefill=64, num_layers=6)
+        ctx.upload_rope(gc.rope_table(POS + 1, 1e4), gc.rope_table(POS + 1, 1e6))
+        for s in range(B):
+            ctx.fill_cache_random(5, s, CTX, s)
+        q = torch.randn(B, 2048, device="cuda")
+        k = torch.randn(B, 1024, device="cuda")
+        v = torch.randn(B, 1024, device="cuda")
+        o = torch.empty(B, 2048, device="cuda")
+        for _ in range(3):
+            ctx.attn_decode_dev(5, list(range(B)), [POS] * B, q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr())
+    else:
+        T = 8192
+        ctx = gc.Context(max_context=T, max_batch=1, kv_dtype=gc.KV_BF16, max_prefill=T, num_layers=6)
+        ctx.upload_rope(gc.rope_table(T, 1e4), gc.rope_table(T, 1e6))
+        for l in (0, 5):
+            qn, kn = synth.qk_norm_gains(l)
+            ctx.set_qk_norm(l, qn, kn)
+        q = torch.randn(T, 2048, device="cuda")
+        k = torch.randn(T, 1024, device="cuda")
+        v = torch.randn(T, 1024, device="cuda")
+        o = torch.empty(T, 2048, device="cuda")
+        for l in (5, 0, 5):
+            ctx.attn_prefill_dev(l, 0, q.data_ptr(), k.data_ptr(), v.data_ptr(), T, 0, o.data_ptr())
+    ctx.synchronize()
+    ctx.close()
+    print(json.dumps({"profile_case": args.profile_case, "ok": True}))
+
+
 def main():
     global B_TOTAL
     args = parse_args()
     B_TOTAL = args.seqs
+    if args.profile_case:
+        return profile_case(args)
     dist = Dist()
     if args.impl == "reference":
         dist.init("gloo")
