@@ -556,14 +556,25 @@ __global__ void __launch_bounds__(256) merge_partials(const float *__restrict__ 
 // the two query heads of the group (rows 0-63 head 2g, 64-127 head 2g+1),
 // so each K/V tile feeds both.  Per key tile of 64 rows:
 //     S[128x64]  = Q[128x256] . K^T     (16 MMAs of K=16, TMEM cols 0-127, x2 buffers)
-//     softmax    warps 0-3, thread = row, reads S from TMEM, writes P bf16
+//     softmax    warps 0-7: row r is shared by threads r (keys 0-31, O
+//                cols 0-127) and r+128 (keys 32-63, O cols 128-255)
 //     O[128x256] += P[128x64] . V       (4 MMAs of K=16, TMEM cols 128-383)
-// Warp 4 issues TMA loads, warp 5 issues MMAs (one elected lane each).
+// Warp 8 issues TMA loads, warp 9 issues MMAs (one elected lane each).
+// Operands are fp16 (see prologue_prefill), accumulation fp32.
+//
+// Online softmax with a lazily updated reference max: P = 2^(s*c - m) is
+// computed against the row's current reference m, which is only raised
+// (rescaling l and the TMEM-resident O by 2^(m_old - m_new)) when the tile
+// max exceeds it by more than kRescaleLog2; otherwise P <= 2^kRescaleLog2 =
+// 256, exact in fp16, and the result is mathematically unchanged.  This
+// removes the O rescale from almost every tile.
+//
 // Shared memory (1024-aligned, 128-B swizzle everywhere):
 //     Q  64 KB: 4 dim-chunks x [128 rows x 128 B]
 //     K  2 stages x 32 KB: 4 dim-chunks x [64 keys x 128 B]   (K-major B)
 //     V  2 stages x 32 KB: 4 dim-chunks x [64 keys x 128 B]   (MN-major B)
-//     P  16 KB: [128 rows x 64 keys] bf16                      (K-major A)
+//     P  16 KB: [128 rows x 64 keys] fp16                      (K-major A)
+//     row-max exchange 2 KB, barriers
 // ------------------------------------------------------------------------
 struct PrefillParams {
     float *out;       // [T][8][256]
@@ -574,7 +585,11 @@ struct PrefillParams {
     unsigned *err;
 };
 
-constexpr int kPfThreads = 192;
+constexpr int kPfSoftmaxThreads = 256;
+constexpr int kPfThreads = kPfSoftmaxThreads + 64;  // + producer warp + MMA warp
+constexpr int kPfWarpTma = 8;
+constexpr int kPfWarpMma = 9;
+constexpr float kRescaleLog2 = 8.0f;
 constexpr uint32_t kPfQBytes = 128 * 256 * 2;
 constexpr uint32_t kPfKVStage = 64 * 256 * 2;
 constexpr uint32_t kPfPBytes = 128 * 64 * 2;
@@ -582,10 +597,12 @@ constexpr uint32_t kPfOffK = kPfQBytes;
 constexpr uint32_t kPfOffV = kPfOffK + 2 * kPfKVStage;
 constexpr uint32_t kPfOffP = kPfOffV + 2 * kPfKVStage;
 constexpr uint32_t kPfOffBar = kPfOffP + kPfPBytes;
-constexpr uint32_t kPfSmem = kPfOffBar + 256 + 1024;  // + alignment slack
+constexpr uint32_t kPfOffRed = kPfOffBar + 256;
+constexpr uint32_t kPfSmem = kPfOffRed + 2048 + 1024;  // + alignment slack
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemS = 0;    // two 64-column S buffers
 constexpr uint32_t kTmemO = 128;  // 256 columns
+
 
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_fa_sm100(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -596,6 +613,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     unsigned char *sK = sm + kPfOffK;
     unsigned char *sV = sm + kPfOffV;
     unsigned char *sP = sm + kPfOffP;
+    float *red = reinterpret_cast<float *>(sm + kPfOffRed);  // [2 parity][2 half][128 rows]
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kPfOffBar);
     uint64_t *bar_q = bars + 0;
     uint64_t *k_full = bars + 1;   // [2]
@@ -624,19 +642,22 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < 16; ++i) mbar_init(&bars[i], 1);
-        mbar_init(&s_free[0], 128);
-        mbar_init(&s_free[1], 128);
-        mbar_init(p_full, 128);
+        mbar_init(&s_free[0], kPfSoftmaxThreads);
+        mbar_init(&s_free[1], kPfSoftmaxThreads);
+        mbar_init(p_full, kPfSoftmaxThreads);
+        mbar_init(&bars[18], kPfSoftmaxThreads);  // red_bar[0]
+        mbar_init(&bars[19], kPfSoftmaxThreads);  // red_bar[1]
+        mbar_init(&bars[20], kPfSoftmaxThreads);  // fin_bar
         *s_abort = 0;
         fence_mbar_init();
     }
-    if (warp == 5) tmem_alloc(tmem_slot, kTmemCols);
+    if (warp == kPfWarpMma) tmem_alloc(tmem_slot, kTmemCols);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
-    if (warp == 4) {
+    if (warp == kPfWarpTma) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
             prefetch_tmap(&tmQ);
@@ -659,7 +680,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     tma_load_3d(sV + s * kPfKVStage + c * 8192, &tmV, 64 * c, krow, g, &v_full[s]);
             }
         }
-    } else if (warp == 5) {
+    } else if (warp == kPfWarpMma) {
         // ------------------------------------------------ MMA issuer
         if (lane == 0) {
             constexpr uint32_t idS = idesc_f16_f32(128, 64, 0, 0);
@@ -704,67 +725,89 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             mbar_wait(mma_done, 0, nullptr);
         }
     } else {
-        // ------------------------------------------------ softmax warps 0-3
-        const int row = threadIdx.x;  // TMEM lane == S/O row
+        // ------------------------------------------------ softmax warps 0-7
+        uint64_t *red_bar = bars + 18;  // [2] row-max exchange, by tile parity
+        uint64_t *fin_bar = bars + 20;  // row-sum exchange before the epilogue
+        const int row = threadIdx.x & 127;  // TMEM lane == S/O row
+        const int half = threadIdx.x >> 7;  // keys [32*half, +32), O cols [128*half, +128)
         const int tr = row & 63, hh = row >> 6;
         const int qpos = p.start_pos + t0 + tr;
-        const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
-        float m = -INFINITY, l = 0.f;
+        const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
+        const int lo_ok = p.is_global ? INT_MIN : qpos - (kWindow - 1);
+        float m = -INFINITY;  // reference max of the row, log2 domain
+        float l = 0.f;        // this half's share of the row sum
         bool ok = true;
         for (int i = 0; i < ntiles; ++i) {
             const int s = i & 1;
-            if (*s_abort || !mbar_wait(&s_full[s], (i >> 1) & 1, p.err)) { ok = false; break; }
-            tc_fence_after();
-            float x[64];
-            {
-                float a[32], c[32];
-                tmem_ld32(lane_base + kTmemS + s * 64, a);
-                tmem_ld32(lane_base + kTmemS + s * 64 + 32, c);
-                tc_wait_ld();
-#pragma unroll
-                for (int k = 0; k < 32; ++k) {
-                    x[k] = a[k];
-                    x[32 + k] = c[k];
-                }
+            // every wait's outcome is made warp-uniform so the warp-collective
+            // tcgen05 and vote instructions below never run diverged
+            if (!__all_sync(0xffffffffu, !*s_abort && mbar_wait(&s_full[s], (i >> 1) & 1, p.err))) {
+                ok = false;
+                break;
             }
+            tc_fence_after();
+            float x[32];
+            tmem_ld32(lane_base + kTmemS + s * 64 + half * 32, x);
+            tc_wait_ld();
             tc_fence_before();
             mbar_arrive(&s_free[s]);
-            const int kbase = p.kv_pos0 + (j0 + i) * 64;
-            const int lo_ok = p.is_global ? INT_MIN : qpos - (kWindow - 1);
+            const int tb = p.kv_pos0 + (j0 + i) * 64;  // position of the tile's first key
+            const bool edge = (tb + 63 > qlo) || (!p.is_global && tb < qhi - (kWindow - 1));
             float mx = -INFINITY;
+            if (edge) {
+                const int kb = tb + half * 32;
 #pragma unroll
-            for (int k = 0; k < 64; ++k) {
-                const int kp = kbase + k;
-                const bool valid = (kp <= qpos) && (kp >= lo_ok);
-                x[k] = valid ? x[k] * kScaleLog2 : -INFINITY;
-                mx = fmaxf(mx, x[k]);
+                for (int k = 0; k < 32; ++k) {
+                    const int kp = kb + k;
+                    if (!(kp <= qpos && kp >= lo_ok)) x[k] = -INFINITY;
+                    mx = fmaxf(mx, x[k]);
+                }
+            } else {
+#pragma unroll
+                for (int k = 0; k < 32; ++k) mx = fmaxf(mx, x[k]);
             }
-            const float m_new = fmaxf(m, mx);
-            const float m_use = (m_new == -INFINITY) ? 0.f : m_new;
-            const float alpha = ex2_approx(m - m_use);
+            mx *= kScaleLog2;
+            red[(s * 2 + half) * 128 + row] = mx;
+            mbar_arrive(&red_bar[s]);
+            if (!__all_sync(0xffffffffu, mbar_wait(&red_bar[s], (i >> 1) & 1, p.err))) {
+                ok = false;
+                break;
+            }
+            mx = fmaxf(mx, red[(s * 2 + (half ^ 1)) * 128 + row]);
+            const bool raise = mx > m + kRescaleLog2;  // false while the row has no valid key
+            const float m_new = raise ? mx : m;
+            const float alpha = raise ? ex2_approx(m - m_new) : 1.f;
             float rs = 0.f;
-            uint32_t pk[32];
+            uint32_t pk[16];
+            if (m_new == -INFINITY) {
 #pragma unroll
-            for (int k = 0; k < 32; ++k) {
-                const float e0 = ex2_approx(x[2 * k] - m_use);
-                const float e1 = ex2_approx(x[2 * k + 1] - m_use);
-                rs += e0 + e1;
-                pk[k] = pack_f16x2(e0, e1);
+                for (int k = 0; k < 16; ++k) pk[k] = 0u;
+            } else {
+                const float nm = -m_new;
+#pragma unroll
+                for (int k = 0; k < 16; ++k) {
+                    const float e0 = ex2_approx(fmaf(x[2 * k], kScaleLog2, nm));
+                    const float e1 = ex2_approx(fmaf(x[2 * k + 1], kScaleLog2, nm));
+                    rs += e0 + e1;
+                    pk[k] = pack_f16x2(e0, e1);
+                }
             }
-            // P buffer and O are owned by the tensor core until PV(i-1) is done.
-            if (i >= 1 && !mbar_wait(p_empty, (i - 1) & 1, p.err)) { ok = false; break; }
+            // P buffer and O belong to the tensor core until PV(i-1) is done.
+            if (i >= 1 && !__all_sync(0xffffffffu, mbar_wait(p_empty, (i - 1) & 1, p.err))) {
+                ok = false;
+                break;
+            }
             tc_fence_after();
-            // tcgen05.ld/st are warp-collective: rescale when any row of the
-            // warp needs it (alpha == 1 exactly for rows whose max held).
-            if (i >= 1 && __any_sync(0xffffffffu, m_new > m)) {
+            if (i >= 1 && __any_sync(0xffffffffu, raise)) {
 #pragma unroll 1
-                for (int c = 0; c < 8; ++c) {
+                for (int cc = 0; cc < 4; ++cc) {
                     float o[32];
-                    tmem_ld32(lane_base + kTmemO + c * 32, o);
+                    const uint32_t ta = lane_base + kTmemO + half * 128 + cc * 32;
+                    tmem_ld32(ta, o);
                     tc_wait_ld();
 #pragma unroll
                     for (int k = 0; k < 32; ++k) o[k] *= alpha;
-                    tmem_st32(lane_base + kTmemO + c * 32, o);
+                    tmem_st32(ta, o);
                 }
                 tc_wait_st();
             }
@@ -772,8 +815,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             m = m_new;
             unsigned char *prow = sP + row * 128;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                *reinterpret_cast<uint4 *>(prow + ((j ^ (row & 7)) * 16)) =
+            for (int j = 0; j < 4; ++j) {
+                const int chunk = half * 4 + j;
+                *reinterpret_cast<uint4 *>(prow + ((chunk ^ (row & 7)) * 16)) =
                     make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
             }
             fence_proxy_async_smem();
@@ -781,21 +825,28 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             mbar_arrive(p_full);
         }
         if (!ok) *s_abort = 1;
-        // Epilogue: O / l -> out[t][2g+hh][:]
-        if (ok && ntiles > 0 && mbar_wait(p_empty, (ntiles - 1) & 1, p.err)) {
+        // Epilogue: O / (l_half0 + l_half1) -> out[t][2g+hh][:]
+        if (ok) {
+            red[half * 128 + row] = l;
+            mbar_arrive(fin_bar);
+            ok = __all_sync(0xffffffffu, mbar_wait(fin_bar, 0, p.err) &&
+                                             mbar_wait(p_empty, (ntiles - 1) & 1, p.err));
+        }
+        if (ok) {
             tc_fence_after();
-            const float inv = l > 0.f ? 1.0f / l : 0.f;
+            const float lt = red[row] + red[128 + row];
+            const float inv = lt > 0.f ? 1.0f / lt : 0.f;
             const bool store = (t0 + tr) < p.T;
-            float *dst = p.out + ((size_t)(t0 + tr) * kHeads + 2 * g + hh) * kHeadDim;
+            float *dst = p.out + ((size_t)(t0 + tr) * kHeads + 2 * g + hh) * kHeadDim + half * 128;
 #pragma unroll 1
-            for (int c = 0; c < 8; ++c) {
+            for (int cc = 0; cc < 4; ++cc) {
                 float o[32];
-                tmem_ld32(lane_base + kTmemO + c * 32, o);
+                tmem_ld32(lane_base + kTmemO + half * 128 + cc * 32, o);
                 tc_wait_ld();
                 if (store) {
 #pragma unroll
                     for (int k = 0; k < 32; k += 4)
-                        *reinterpret_cast<float4 *>(dst + c * 32 + k) =
+                        *reinterpret_cast<float4 *>(dst + cc * 32 + k) =
                             make_float4(o[k] * inv, o[k + 1] * inv, o[k + 2] * inv, o[k + 3] * inv);
                 }
             }
@@ -803,7 +854,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 4 && lane == 0 && *s_abort) {
+    if (warp == kPfWarpTma && lane == 0 && *s_abort) {
         // Let in-flight TMA copies land before the CTA's shared memory goes.
         for (int s = 0; s < 2; ++s) {
             mbar_wait(&k_full[s], 0, nullptr);
@@ -811,7 +862,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
     }
     __syncthreads();
-    if (warp == 5) {
+    if (warp == kPfWarpMma) {
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
