@@ -557,8 +557,13 @@ __global__ void __launch_bounds__(256) merge_partials(const float *__restrict__ 
 // so each K/V tile feeds both.  Per key tile of 64 rows:
 //     S[128x64]  = Q[128x256] . K^T     (16 MMAs of K=16, TMEM cols 0-127, x2 buffers)
 //     softmax    warps 0-7: row r is shared by threads r (keys 0-31, O
-//                cols 0-127) and r+128 (keys 32-63, O cols 128-255)
-//     O[128x256] += P[128x64] . V       (4 MMAs of K=16, TMEM cols 128-383)
+//                cols 0-127) and r+128 (keys 32-63, O cols 128-255); P is
+//                written back to TMEM as fp16 (cols 384-447, x2 buffers)
+//     O[128x256] += P[128x64] . V       (4 MMAs of K=16, A = P from TMEM,
+//                                        TMEM cols 128-383)
+// With P double-buffered in TMEM, softmax of tile j overlaps both PV(j-1)
+// and S(j+1) on the tensor core; it only waits for PV(j-1) when it has to
+// rescale O.
 // Warp 8 issues TMA loads, warp 9 issues MMAs (one elected lane each).
 // Operands are fp16 (see prologue_prefill), accumulation fp32.
 //
@@ -573,8 +578,7 @@ __global__ void __launch_bounds__(256) merge_partials(const float *__restrict__ 
 //     Q  64 KB: 4 dim-chunks x [128 rows x 128 B]
 //     K  2 stages x 32 KB: 4 dim-chunks x [64 keys x 128 B]   (K-major B)
 //     V  2 stages x 32 KB: 4 dim-chunks x [64 keys x 128 B]   (MN-major B)
-//     P  16 KB: [128 rows x 64 keys] fp16                      (K-major A)
-//     row-max exchange 2 KB, barriers
+//     row-max / row-sum exchange 3 KB, barriers
 // ------------------------------------------------------------------------
 struct PrefillParams {
     float *out;       // [T][8][256]
@@ -592,16 +596,15 @@ constexpr int kPfWarpMma = 9;
 constexpr float kRescaleLog2 = 8.0f;
 constexpr uint32_t kPfQBytes = 128 * 256 * 2;
 constexpr uint32_t kPfKVStage = 64 * 256 * 2;
-constexpr uint32_t kPfPBytes = 128 * 64 * 2;
 constexpr uint32_t kPfOffK = kPfQBytes;
 constexpr uint32_t kPfOffV = kPfOffK + 2 * kPfKVStage;
-constexpr uint32_t kPfOffP = kPfOffV + 2 * kPfKVStage;
-constexpr uint32_t kPfOffBar = kPfOffP + kPfPBytes;
+constexpr uint32_t kPfOffBar = kPfOffV + 2 * kPfKVStage;
 constexpr uint32_t kPfOffRed = kPfOffBar + 256;
-constexpr uint32_t kPfSmem = kPfOffRed + 2048 + 1024;  // + alignment slack
+constexpr uint32_t kPfSmem = kPfOffRed + 3072 + 1024;  // + alignment slack
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemS = 0;    // two 64-column S buffers
 constexpr uint32_t kTmemO = 128;  // 256 columns
+constexpr uint32_t kTmemP = 384;  // two 32-column fp16 P buffers
 
 
 __global__ void __launch_bounds__(kPfThreads, 1)
@@ -612,8 +615,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     unsigned char *sQ = sm;
     unsigned char *sK = sm + kPfOffK;
     unsigned char *sV = sm + kPfOffV;
-    unsigned char *sP = sm + kPfOffP;
-    float *red = reinterpret_cast<float *>(sm + kPfOffRed);  // [2 parity][2 half][128 rows]
+    float *red = reinterpret_cast<float *>(sm + kPfOffRed);  // [2 parity][2 half][128 rows] maxima, then [2][128] sums
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kPfOffBar);
     uint64_t *bar_q = bars + 0;
     uint64_t *k_full = bars + 1;   // [2]
@@ -622,11 +624,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     uint64_t *v_empty = bars + 7;  // [2]
     uint64_t *s_full = bars + 9;   // [2]
     uint64_t *s_free = bars + 11;  // [2]
-    uint64_t *p_full = bars + 13;
-    uint64_t *p_empty = bars + 14;
-    uint64_t *mma_done = bars + 15;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 16);
-    volatile int *s_abort = reinterpret_cast<volatile int *>(bars + 17);
+    uint64_t *p_full = bars + 13;   // [2]
+    uint64_t *p_empty = bars + 15;  // [2]
+    uint64_t *mma_done = bars + 17;
+    uint64_t *red_bar = bars + 18;  // [2] row-max exchange, by tile parity
+    uint64_t *fin_bar = bars + 20;  // row-sum exchange before the epilogue
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 21);
+    volatile int *s_abort = reinterpret_cast<volatile int *>(bars + 22);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nqb = gridDim.x;
@@ -641,13 +645,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const int ntiles = j1 - j0;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 16; ++i) mbar_init(&bars[i], 1);
-        mbar_init(&s_free[0], kPfSoftmaxThreads);
-        mbar_init(&s_free[1], kPfSoftmaxThreads);
-        mbar_init(p_full, kPfSoftmaxThreads);
-        mbar_init(&bars[18], kPfSoftmaxThreads);  // red_bar[0]
-        mbar_init(&bars[19], kPfSoftmaxThreads);  // red_bar[1]
-        mbar_init(&bars[20], kPfSoftmaxThreads);  // fin_bar
+        for (int i = 0; i < 21; ++i) mbar_init(&bars[i], 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&s_free[b], kPfSoftmaxThreads);
+            mbar_init(&p_full[b], kPfSoftmaxThreads);
+            mbar_init(&red_bar[b], kPfSoftmaxThreads);
+        }
+        mbar_init(fin_bar, kPfSoftmaxThreads);
         *s_abort = 0;
         fence_mbar_init();
     }
@@ -685,7 +689,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         if (lane == 0) {
             constexpr uint32_t idS = idesc_f16_f32(128, 64, 0, 0);
             constexpr uint32_t idO = idesc_f16_f32(128, 256, 0, 1);
-            const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP);
+            const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV);
             bool ok = mbar_wait(bar_q, 0, p.err);
             tc_fence_after();
             for (int i = 0; ok && i <= ntiles; ++i) {
@@ -706,17 +710,17 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 }
                 if (i >= 1) {
                     const int u = i - 1, su = u & 1;
-                    if (!mbar_wait(p_full, u & 1, p.err)) { ok = false; break; }
+                    if (!mbar_wait(&p_full[su], (u >> 1) & 1, p.err)) { ok = false; break; }
                     if (!mbar_wait(&v_full[su], (u >> 1) & 1, p.err)) { ok = false; break; }
                     tc_fence_after();
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk) {
-                        const uint64_t a = smem_desc_sw128(aP + kk * 32, 16, 1024);
                         const uint64_t bd = smem_desc_sw128(aV + su * kPfKVStage + kk * 2048, 8192, 1024);
-                        tc_mma_f16(tmem + kTmemO, a, bd, idO, (u > 0 || kk > 0) ? 1u : 0u);
+                        tc_mma_f16_ts(tmem + kTmemO, tmem + kTmemP + su * 32 + kk * 8, bd, idO,
+                                      (u > 0 || kk > 0) ? 1u : 0u);
                     }
                     tc_commit(&v_empty[su]);
-                    tc_commit(p_empty);
+                    tc_commit(&p_empty[su]);
                 }
             }
             if (!ok) *s_abort = 1;
@@ -726,8 +730,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
     } else {
         // ------------------------------------------------ softmax warps 0-7
-        uint64_t *red_bar = bars + 18;  // [2] row-max exchange, by tile parity
-        uint64_t *fin_bar = bars + 20;  // row-sum exchange before the epilogue
         const int row = threadIdx.x & 127;  // TMEM lane == S/O row
         const int half = threadIdx.x >> 7;  // keys [32*half, +32), O cols [128*half, +128)
         const int tr = row & 63, hh = row >> 6;
@@ -792,13 +794,19 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     pk[k] = pack_f16x2(e0, e1);
                 }
             }
-            // P buffer and O belong to the tensor core until PV(i-1) is done.
-            if (i >= 1 && !__all_sync(0xffffffffu, mbar_wait(p_empty, (i - 1) & 1, p.err))) {
+            // P buffer s was last read by PV(i-2); O is written by PV(i-1),
+            // so an O rescale waits for that one too.
+            if (i >= 2 && !__all_sync(0xffffffffu, mbar_wait(&p_empty[s], ((i - 2) >> 1) & 1, p.err))) {
+                ok = false;
+                break;
+            }
+            const bool rescale = i >= 1 && __any_sync(0xffffffffu, raise);
+            if (rescale && !__all_sync(0xffffffffu, mbar_wait(&p_empty[s ^ 1], ((i - 1) >> 1) & 1, p.err))) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            if (i >= 1 && __any_sync(0xffffffffu, raise)) {
+            if (rescale) {
 #pragma unroll 1
                 for (int cc = 0; cc < 4; ++cc) {
                     float o[32];
@@ -813,28 +821,23 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             }
             l = l * alpha + rs;
             m = m_new;
-            unsigned char *prow = sP + row * 128;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const int chunk = half * 4 + j;
-                *reinterpret_cast<uint4 *>(prow + ((chunk ^ (row & 7)) * 16)) =
-                    make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-            }
-            fence_proxy_async_smem();
+            tmem_st16(lane_base + kTmemP + s * 32 + half * 16, pk);
+            tc_wait_st();
             tc_fence_before();
-            mbar_arrive(p_full);
+            mbar_arrive(&p_full[s]);
         }
         if (!ok) *s_abort = 1;
         // Epilogue: O / (l_half0 + l_half1) -> out[t][2g+hh][:]
         if (ok) {
-            red[half * 128 + row] = l;
+            red[512 + half * 128 + row] = l;
             mbar_arrive(fin_bar);
+            const int u = ntiles - 1;
             ok = __all_sync(0xffffffffu, mbar_wait(fin_bar, 0, p.err) &&
-                                             mbar_wait(p_empty, (ntiles - 1) & 1, p.err));
+                                             mbar_wait(&p_empty[u & 1], (u >> 1) & 1, p.err));
         }
         if (ok) {
             tc_fence_after();
-            const float lt = red[row] + red[128 + row];
+            const float lt = red[512 + row] + red[640 + row];
             const float inv = lt > 0.f ? 1.0f / lt : 0.f;
             const bool store = (t0 + tr) < p.T;
             float *dst = p.out + ((size_t)(t0 + tr) * kHeads + 2 * g + hh) * kHeadDim + half * 128;
