@@ -594,6 +594,25 @@ constexpr int kPfThreads = kPfSoftmaxThreads + 64;  // + producer warp + MMA war
 constexpr int kPfWarpTma = 8;
 constexpr int kPfWarpMma = 9;
 constexpr float kRescaleLog2 = 8.0f;
+#ifndef G3_EXP_EMU_QUARTERS
+#define G3_EXP_EMU_QUARTERS 0
+#endif
+constexpr int kExpEmuQuarters = G3_EXP_EMU_QUARTERS;
+
+// Development-only per-tile timestamps of CTA (0,0) (build with
+// -DG3_PF_TRACE); compiled out of the library.
+#ifdef G3_PF_TRACE
+__device__ long long g3_pf_trace[8][256];
+#define G3_TRACE(slot, i)                                                     \
+    do {                                                                      \
+        if (blockIdx.x == 0 && blockIdx.y == 0 && (i) < 256)                  \
+            g3_pf_trace[slot][i] = clock64();                                 \
+    } while (0)
+#else
+#define G3_TRACE(slot, i) \
+    do {                  \
+    } while (0)
+#endif
 constexpr uint32_t kPfQBytes = 128 * 256 * 2;
 constexpr uint32_t kPfKVStage = 64 * 256 * 2;
 constexpr uint32_t kPfOffK = kPfQBytes;
@@ -707,10 +726,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     }
                     tc_commit(&k_empty[s]);
                     tc_commit(&s_full[s]);
+                    G3_TRACE(0, i);
                 }
                 if (i >= 1) {
                     const int u = i - 1, su = u & 1;
                     if (!mbar_wait(&p_full[su], (u >> 1) & 1, p.err)) { ok = false; break; }
+                    G3_TRACE(1, u);
                     if (!mbar_wait(&v_full[su], (u >> 1) & 1, p.err)) { ok = false; break; }
                     tc_fence_after();
 #pragma unroll
@@ -748,6 +769,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 break;
             }
             tc_fence_after();
+            if (threadIdx.x == 0) G3_TRACE(2, i);
             float x[32];
             tmem_ld32(lane_base + kTmemS + s * 64 + half * 32, x);
             tc_wait_ld();
@@ -775,6 +797,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 ok = false;
                 break;
             }
+            if (threadIdx.x == 0) G3_TRACE(3, i);
             mx = fmaxf(mx, red[(s * 2 + (half ^ 1)) * 128 + row]);
             const bool raise = mx > m + kRescaleLog2;  // false while the row has no valid key
             const float m_new = raise ? mx : m;
@@ -788,8 +811,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 const float nm = -m_new;
 #pragma unroll
                 for (int k = 0; k < 16; ++k) {
-                    const float e0 = ex2_approx(fmaf(x[2 * k], kScaleLog2, nm));
-                    const float e1 = ex2_approx(fmaf(x[2 * k + 1], kScaleLog2, nm));
+                    // kExpEmuQuarters of every four element pairs use the
+                    // FMA-pipe exp2, the rest the transcendental unit.
+                    const bool emu = (k & 3) < kExpEmuQuarters;
+                    const float a0 = fmaf(x[2 * k], kScaleLog2, nm), a1 = fmaf(x[2 * k + 1], kScaleLog2, nm);
+                    const float e0 = emu ? ex2_poly(a0) : ex2_approx(a0);
+                    const float e1 = emu ? ex2_poly(a1) : ex2_approx(a1);
                     rs += e0 + e1;
                     pk[k] = pack_f16x2(e0, e1);
                 }
@@ -824,6 +851,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             tmem_st16(lane_base + kTmemP + s * 32 + half * 16, pk);
             tc_wait_st();
             tc_fence_before();
+            if (threadIdx.x == 0) G3_TRACE(4, i);
             mbar_arrive(&p_full[s]);
         }
         if (!ok) *s_abort = 1;

@@ -910,3 +910,9 @@ extern "C" int gemma3_cuda_gqa_decode_noalloc(const float *q, const void *kv, in
         return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "kernel launch failed: %s", cudaGetErrorString(e));
     return 0;
 }
+
+#ifdef G3_PF_TRACE
+extern "C" int g3_debug_read_trace(long long *host) {
+    return (int)cudaMemcpyFromSymbol(host, g3::g3_pf_trace, sizeof(g3::g3_pf_trace));
+}
+#endif
