@@ -555,32 +555,35 @@ __global__ void __launch_bounds__(256) merge_partials(const float *__restrict__ 
 // CTA = (block of 64 query tokens, kv head g); the MMA M dimension stacks
 // the two query heads of the group (rows 0-63 head 2g, 64-127 head 2g+1),
 // so each K/V tile feeds both.  Per key tile of 64 rows:
-//     S[128x64]  = Q[128x256] . K^T     (16 MMAs of K=16, TMEM cols 0-127, x2 buffers)
-//     softmax    warps 0-7: row r is shared by threads r (keys 0-31, O
-//                cols 0-127) and r+128 (keys 32-63, O cols 128-255); P is
-//                written back to TMEM as fp16 (cols 384-447, x2 buffers)
-//     O[128x256] += P[128x64] . V       (4 MMAs of K=16, A = P from TMEM,
-//                                        TMEM cols 128-383)
-// With P double-buffered in TMEM, softmax of tile j overlaps both PV(j-1)
-// and S(j+1) on the tensor core; it only waits for PV(j-1) when it has to
-// rescale O.
-// Warp 8 issues TMA loads, warp 9 issues MMAs (one elected lane each).
+//     S[128x64]  = Q[128x256] . K^T   16 MMAs (K=16); A = Q resident in TMEM,
+//                                      B = K tile from shared memory
+//     softmax    warps 0-7: row r is shared by threads r (keys 0-31, O cols
+//                0-127) and r+128 (keys 32-63, O cols 128-255); P goes back
+//                to TMEM as fp16 (two buffers)
+//     O[128x256] += P[128x64] . V     4 MMAs (K=16); A = P from TMEM,
+//                                      B = V tile (MN-major) from shared memory
+// Keeping both A operands in TMEM leaves shared memory bandwidth to the K/V
+// tiles only (with Q in shared memory the narrow N=64 S MMAs were limited by
+// reading the 4 KB Q slice per instruction) and frees the space for a third
+// K/V stage.  Warp 8 issues the TMA loads, warp 9 the MMAs (one lane each).
 // Operands are fp16 (see prologue_prefill), accumulation fp32.
+//
+// TMEM columns (512): Q 0-127 (fp16 pairs), S 128-191 (fp32), P 192-255
+// (2 x 32, fp16 pairs), O 256-511 (fp32).
 //
 // Online softmax with a lazily updated reference max: P = 2^(s*c - m) is
 // computed against the row's current reference m, which is only raised
 // (rescaling l and the TMEM-resident O by 2^(m_old - m_new)) when the tile
 // max exceeds it by more than kRescaleLog2; otherwise P <= 2^kRescaleLog2 =
-// 256, exact in fp16, and the result is mathematically unchanged.  This
-// removes the O rescale from almost every tile.
+// 256, exact in fp16, and the result is mathematically unchanged.
 //
 // Shared memory (1024-aligned, 128-B swizzle everywhere):
-//     Q  64 KB: 4 dim-chunks x [128 rows x 128 B]
-//     K  2 stages x 32 KB: 4 dim-chunks x [64 keys x 128 B]   (K-major B)
-//     V  2 stages x 32 KB: 4 dim-chunks x [64 keys x 128 B]   (MN-major B)
-//     row-max / row-sum exchange 3 KB, barriers
+//     K  3 stages x 32 KB: 4 dim-chunks x [64 keys x 128 B]   (K-major B)
+//     V  3 stages x 32 KB: 4 dim-chunks x [64 keys x 128 B]   (MN-major B)
+//     barriers, row-max / row-sum exchange 3 KB
 // ------------------------------------------------------------------------
 struct PrefillParams {
+    const __half *q;  // [8][T][256] fp16, normalised + rotated
     float *out;       // [T][8][256]
     int T;
     int start_pos;
@@ -593,6 +596,7 @@ constexpr int kPfSoftmaxThreads = 256;
 constexpr int kPfThreads = kPfSoftmaxThreads + 64;  // + producer warp + MMA warp
 constexpr int kPfWarpTma = 8;
 constexpr int kPfWarpMma = 9;
+constexpr int kPfStages = 3;
 constexpr float kRescaleLog2 = 8.0f;
 #ifndef G3_EXP_EMU_QUARTERS
 #define G3_EXP_EMU_QUARTERS 0
@@ -613,43 +617,42 @@ __device__ long long g3_pf_trace[8][256];
     do {                  \
     } while (0)
 #endif
-constexpr uint32_t kPfQBytes = 128 * 256 * 2;
+
 constexpr uint32_t kPfKVStage = 64 * 256 * 2;
-constexpr uint32_t kPfOffK = kPfQBytes;
-constexpr uint32_t kPfOffV = kPfOffK + 2 * kPfKVStage;
-constexpr uint32_t kPfOffBar = kPfOffV + 2 * kPfKVStage;
+constexpr uint32_t kPfOffK = 0;
+constexpr uint32_t kPfOffV = kPfOffK + kPfStages * kPfKVStage;
+constexpr uint32_t kPfOffBar = kPfOffV + kPfStages * kPfKVStage;
 constexpr uint32_t kPfOffRed = kPfOffBar + 256;
 constexpr uint32_t kPfSmem = kPfOffRed + 3072 + 1024;  // + alignment slack
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemS = 0;    // two 64-column S buffers
-constexpr uint32_t kTmemO = 128;  // 256 columns
-constexpr uint32_t kTmemP = 384;  // two 32-column fp16 P buffers
-
+constexpr uint32_t kTmemQ = 0;
+constexpr uint32_t kTmemS = 128;
+constexpr uint32_t kTmemP = 192;
+constexpr uint32_t kTmemO = 256;
 
 __global__ void __launch_bounds__(kPfThreads, 1)
-    prefill_fa_sm100(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                     const __grid_constant__ CUtensorMap tmV, const PrefillParams p) {
+    prefill_fa_sm100(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
+                     const PrefillParams p) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char *sm = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    unsigned char *sQ = sm;
     unsigned char *sK = sm + kPfOffK;
     unsigned char *sV = sm + kPfOffV;
-    float *red = reinterpret_cast<float *>(sm + kPfOffRed);  // [2 parity][2 half][128 rows] maxima, then [2][128] sums
+    float *red = reinterpret_cast<float *>(sm + kPfOffRed);  // [2 parity][2 half][128] maxima, then [2][128] sums
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kPfOffBar);
-    uint64_t *bar_q = bars + 0;
-    uint64_t *k_full = bars + 1;   // [2]
-    uint64_t *k_empty = bars + 3;  // [2]
-    uint64_t *v_full = bars + 5;   // [2]
-    uint64_t *v_empty = bars + 7;  // [2]
-    uint64_t *s_full = bars + 9;   // [2]
-    uint64_t *s_free = bars + 11;  // [2]
-    uint64_t *p_full = bars + 13;   // [2]
-    uint64_t *p_empty = bars + 15;  // [2]
-    uint64_t *mma_done = bars + 17;
-    uint64_t *red_bar = bars + 18;  // [2] row-max exchange, by tile parity
-    uint64_t *fin_bar = bars + 20;  // row-sum exchange before the epilogue
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 21);
-    volatile int *s_abort = reinterpret_cast<volatile int *>(bars + 22);
+    uint64_t *q_ready = bars + 0;   // Q written to TMEM (256 arrivals)
+    uint64_t *k_full = bars + 1;    // [3]
+    uint64_t *k_empty = bars + 4;   // [3]
+    uint64_t *v_full = bars + 7;    // [3]
+    uint64_t *v_empty = bars + 10;  // [3]
+    uint64_t *s_full = bars + 13;
+    uint64_t *s_free = bars + 14;   // 256 arrivals
+    uint64_t *p_full = bars + 15;   // [2], 256 arrivals
+    uint64_t *p_empty = bars + 17;  // [2]
+    uint64_t *mma_done = bars + 19;
+    uint64_t *red_bar = bars + 20;  // [2], 256 arrivals
+    uint64_t *fin_bar = bars + 22;  // 256 arrivals
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 23);
+    volatile int *s_abort = reinterpret_cast<volatile int *>(bars + 24);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nqb = gridDim.x;
@@ -664,9 +667,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     const int ntiles = j1 - j0;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 21; ++i) mbar_init(&bars[i], 1);
+        for (int i = 0; i < 23; ++i) mbar_init(&bars[i], 1);
+        mbar_init(q_ready, kPfSoftmaxThreads);
+        mbar_init(s_free, kPfSoftmaxThreads);
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&s_free[b], kPfSoftmaxThreads);
             mbar_init(&p_full[b], kPfSoftmaxThreads);
             mbar_init(&red_bar[b], kPfSoftmaxThreads);
         }
@@ -683,21 +687,17 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     if (warp == kPfWarpTma) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
-            prefetch_tmap(&tmQ);
             prefetch_tmap(&tmK);
             prefetch_tmap(&tmV);
-            mbar_expect_tx(bar_q, kPfQBytes);
-            for (int c = 0; c < 4; ++c)
-                for (int hh = 0; hh < 2; ++hh)
-                    tma_load_3d(sQ + c * 16384 + hh * 8192, &tmQ, 64 * c, t0, 2 * g + hh, bar_q);
             for (int i = 0; i < ntiles && !*s_abort; ++i) {
-                const int s = i & 1;
+                const int s = i % kPfStages, n = i / kPfStages;
                 const int krow = (j0 + i) * 64;
-                if (i >= 2 && !mbar_wait(&k_empty[s], ((i - 2) >> 1) & 1, p.err)) { *s_abort = 1; break; }
+                if (n >= 1 && !mbar_wait(&k_empty[s], (n - 1) & 1, p.err)) { *s_abort = 1; break; }
+                G3_TRACE(5, i);
                 mbar_expect_tx(&k_full[s], kPfKVStage);
                 for (int c = 0; c < 4; ++c)
                     tma_load_3d(sK + s * kPfKVStage + c * 8192, &tmK, 64 * c, krow, g, &k_full[s]);
-                if (i >= 2 && !mbar_wait(&v_empty[s], ((i - 2) >> 1) & 1, p.err)) { *s_abort = 1; break; }
+                if (n >= 1 && !mbar_wait(&v_empty[s], (n - 1) & 1, p.err)) { *s_abort = 1; break; }
                 mbar_expect_tx(&v_full[s], kPfKVStage);
                 for (int c = 0; c < 4; ++c)
                     tma_load_3d(sV + s * kPfKVStage + c * 8192, &tmV, 64 * c, krow, g, &v_full[s]);
@@ -708,40 +708,46 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         if (lane == 0) {
             constexpr uint32_t idS = idesc_f16_f32(128, 64, 0, 0);
             constexpr uint32_t idO = idesc_f16_f32(128, 256, 0, 1);
-            const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV);
-            bool ok = mbar_wait(bar_q, 0, p.err);
+            // Descriptors are built once; per MMA only the start-address field
+            // (bits 0-13, address >> 4, no carry for addresses < 256 KB)
+            // advances, by compile-time constants.
+            const uint64_t dK0 = smem_desc_sw128(smem_u32(sK), 16, 1024);
+            const uint64_t dV0 = smem_desc_sw128(smem_u32(sV), 8192, 1024);
+            bool ok = mbar_wait(q_ready, 0, p.err);
             tc_fence_after();
             for (int i = 0; ok && i <= ntiles; ++i) {
                 if (*s_abort) { ok = false; break; }
                 if (i < ntiles) {
-                    const int s = i & 1;
-                    if (!mbar_wait(&k_full[s], (i >> 1) & 1, p.err)) { ok = false; break; }
-                    if (i >= 2 && !mbar_wait(&s_free[s], ((i - 2) >> 1) & 1, p.err)) { ok = false; break; }
+                    const int s = i % kPfStages;
+                    if (!mbar_wait(&k_full[s], (i / kPfStages) & 1, p.err)) { ok = false; break; }
+                    G3_TRACE(6, i);
+                    // the single S buffer is free once softmax(i-1) has read it
+                    if (i >= 1 && !mbar_wait(s_free, (i - 1) & 1, p.err)) { ok = false; break; }
                     tc_fence_after();
+                    G3_TRACE(7, i);
+                    const uint64_t dK = dK0 + (uint64_t)((s * kPfKVStage) >> 4);
 #pragma unroll
-                    for (int kk = 0; kk < 16; ++kk) {
-                        const uint64_t a = smem_desc_sw128(aQ + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
-                        const uint64_t bd = smem_desc_sw128(aK + s * kPfKVStage + (kk >> 2) * 8192 + (kk & 3) * 32, 16, 1024);
-                        tc_mma_f16(tmem + kTmemS + s * 64, a, bd, idS, kk > 0 ? 1u : 0u);
-                    }
+                    for (int kk = 0; kk < 16; ++kk)
+                        tc_mma_f16_ts(tmem + kTmemS, tmem + kTmemQ + kk * 8,
+                                      dK + (uint64_t)(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4), idS,
+                                      kk > 0 ? 1u : 0u);
                     tc_commit(&k_empty[s]);
-                    tc_commit(&s_full[s]);
+                    tc_commit(s_full);
                     G3_TRACE(0, i);
                 }
                 if (i >= 1) {
-                    const int u = i - 1, su = u & 1;
-                    if (!mbar_wait(&p_full[su], (u >> 1) & 1, p.err)) { ok = false; break; }
+                    const int u = i - 1, su = u % kPfStages, pb = u & 1;
+                    if (!mbar_wait(&p_full[pb], (u >> 1) & 1, p.err)) { ok = false; break; }
                     G3_TRACE(1, u);
-                    if (!mbar_wait(&v_full[su], (u >> 1) & 1, p.err)) { ok = false; break; }
+                    if (!mbar_wait(&v_full[su], (u / kPfStages) & 1, p.err)) { ok = false; break; }
                     tc_fence_after();
+                    const uint64_t dV = dV0 + (uint64_t)((su * kPfKVStage) >> 4);
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
-                        const uint64_t bd = smem_desc_sw128(aV + su * kPfKVStage + kk * 2048, 8192, 1024);
-                        tc_mma_f16_ts(tmem + kTmemO, tmem + kTmemP + su * 32 + kk * 8, bd, idO,
-                                      (u > 0 || kk > 0) ? 1u : 0u);
-                    }
+                    for (int kk = 0; kk < 4; ++kk)
+                        tc_mma_f16_ts(tmem + kTmemO, tmem + kTmemP + pb * 32 + kk * 8,
+                                      dV + (uint64_t)((kk * 2048) >> 4), idO, (u > 0 || kk > 0) ? 1u : 0u);
                     tc_commit(&v_empty[su]);
-                    tc_commit(&p_empty[su]);
+                    tc_commit(&p_empty[pb]);
                 }
             }
             if (!ok) *s_abort = 1;
@@ -757,24 +763,46 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const int qpos = p.start_pos + t0 + tr;
         const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
         const int lo_ok = p.is_global ? INT_MIN : qpos - (kWindow - 1);
+        {
+            // Q rows into TMEM: this thread's 128 dims = 64 columns of fp16 pairs.
+            const bool have = (t0 + tr) < p.T;
+            const uint4 *src = reinterpret_cast<const uint4 *>(
+                p.q + ((size_t)(2 * g + hh) * p.T + (have ? t0 + tr : 0)) * kHeadDim + half * 128);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                uint32_t w[16];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const uint4 u = have ? src[j * 4 + c] : make_uint4(0, 0, 0, 0);
+                    w[4 * c] = u.x;
+                    w[4 * c + 1] = u.y;
+                    w[4 * c + 2] = u.z;
+                    w[4 * c + 3] = u.w;
+                }
+                tmem_st16(lane_base + kTmemQ + half * 64 + j * 16, w);
+            }
+            tc_wait_st();
+            tc_fence_before();
+            mbar_arrive(q_ready);
+        }
         float m = -INFINITY;  // reference max of the row, log2 domain
         float l = 0.f;        // this half's share of the row sum
         bool ok = true;
         for (int i = 0; i < ntiles; ++i) {
-            const int s = i & 1;
+            const int pb = i & 1;
             // every wait's outcome is made warp-uniform so the warp-collective
             // tcgen05 and vote instructions below never run diverged
-            if (!__all_sync(0xffffffffu, !*s_abort && mbar_wait(&s_full[s], (i >> 1) & 1, p.err))) {
+            if (!__all_sync(0xffffffffu, !*s_abort && mbar_wait(s_full, i & 1, p.err))) {
                 ok = false;
                 break;
             }
             tc_fence_after();
             if (threadIdx.x == 0) G3_TRACE(2, i);
             float x[32];
-            tmem_ld32(lane_base + kTmemS + s * 64 + half * 32, x);
+            tmem_ld32(lane_base + kTmemS + half * 32, x);
             tc_wait_ld();
             tc_fence_before();
-            mbar_arrive(&s_free[s]);
+            mbar_arrive(s_free);
             const int tb = p.kv_pos0 + (j0 + i) * 64;  // position of the tile's first key
             const bool edge = (tb + 63 > qlo) || (!p.is_global && tb < qhi - (kWindow - 1));
             float mx = -INFINITY;
@@ -791,14 +819,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 for (int k = 0; k < 32; ++k) mx = fmaxf(mx, x[k]);
             }
             mx *= kScaleLog2;
-            red[(s * 2 + half) * 128 + row] = mx;
-            mbar_arrive(&red_bar[s]);
-            if (!__all_sync(0xffffffffu, mbar_wait(&red_bar[s], (i >> 1) & 1, p.err))) {
+            red[(pb * 2 + half) * 128 + row] = mx;
+            mbar_arrive(&red_bar[pb]);
+            if (!__all_sync(0xffffffffu, mbar_wait(&red_bar[pb], (i >> 1) & 1, p.err))) {
                 ok = false;
                 break;
             }
             if (threadIdx.x == 0) G3_TRACE(3, i);
-            mx = fmaxf(mx, red[(s * 2 + (half ^ 1)) * 128 + row]);
+            mx = fmaxf(mx, red[(pb * 2 + (half ^ 1)) * 128 + row]);
             const bool raise = mx > m + kRescaleLog2;  // false while the row has no valid key
             const float m_new = raise ? mx : m;
             const float alpha = raise ? ex2_approx(m - m_new) : 1.f;
@@ -821,14 +849,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     pk[k] = pack_f16x2(e0, e1);
                 }
             }
-            // P buffer s was last read by PV(i-2); O is written by PV(i-1),
+            // P buffer pb was last read by PV(i-2); O is written by PV(i-1),
             // so an O rescale waits for that one too.
-            if (i >= 2 && !__all_sync(0xffffffffu, mbar_wait(&p_empty[s], ((i - 2) >> 1) & 1, p.err))) {
+            if (i >= 2 && !__all_sync(0xffffffffu, mbar_wait(&p_empty[pb], ((i - 2) >> 1) & 1, p.err))) {
                 ok = false;
                 break;
             }
             const bool rescale = i >= 1 && __any_sync(0xffffffffu, raise);
-            if (rescale && !__all_sync(0xffffffffu, mbar_wait(&p_empty[s ^ 1], ((i - 1) >> 1) & 1, p.err))) {
+            if (rescale && !__all_sync(0xffffffffu, mbar_wait(&p_empty[pb ^ 1], ((i - 1) >> 1) & 1, p.err))) {
                 ok = false;
                 break;
             }
@@ -848,11 +876,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             }
             l = l * alpha + rs;
             m = m_new;
-            tmem_st16(lane_base + kTmemP + s * 32 + half * 16, pk);
+            tmem_st16(lane_base + kTmemP + pb * 32 + half * 16, pk);
             tc_wait_st();
             tc_fence_before();
             if (threadIdx.x == 0) G3_TRACE(4, i);
-            mbar_arrive(&p_full[s]);
+            mbar_arrive(&p_full[pb]);
         }
         if (!ok) *s_abort = 1;
         // Epilogue: O / (l_half0 + l_half1) -> out[t][2g+hh][:]
@@ -887,7 +915,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     __syncthreads();
     if (warp == kPfWarpTma && lane == 0 && *s_abort) {
         // Let in-flight TMA copies land before the CTA's shared memory goes.
-        for (int s = 0; s < 2; ++s) {
+        for (int s = 0; s < kPfStages; ++s) {
             mbar_wait(&k_full[s], 0, nullptr);
             mbar_wait(&v_full[s], 0, nullptr);
         }
