@@ -565,7 +565,8 @@ __global__ void __launch_bounds__(256) merge_partials(const float *__restrict__ 
 // Keeping both A operands in TMEM leaves shared memory bandwidth to the K/V
 // tiles only (with Q in shared memory the narrow N=64 S MMAs were limited by
 // reading the 4 KB Q slice per instruction) and frees the space for a third
-// K/V stage.  Warp 8 issues the TMA loads, warp 9 the MMAs (one lane each).
+// K/V stage.  Warp 8 issues the TMA loads, warp 9 the S MMAs and warp 10 the
+// PV MMAs (one lane each).
 // Operands are fp16 (see prologue_prefill), accumulation fp32.
 //
 // TMEM columns (512): Q 0-127 (fp16 pairs), S 128-191 (fp32), P 192-255
@@ -593,9 +594,10 @@ struct PrefillParams {
 };
 
 constexpr int kPfSoftmaxThreads = 256;
-constexpr int kPfThreads = kPfSoftmaxThreads + 64;  // + producer warp + MMA warp
+constexpr int kPfThreads = kPfSoftmaxThreads + 96;  // + producer warp + two MMA warps
 constexpr int kPfWarpTma = 8;
-constexpr int kPfWarpMma = 9;
+constexpr int kPfWarpMma = 9;  // S MMAs; also owns the TMEM allocation
+constexpr int kPfWarpPv = 10;  // PV MMAs
 constexpr int kPfStages = 3;
 constexpr float kRescaleLog2 = 8.0f;
 #ifndef G3_EXP_EMU_QUARTERS
@@ -653,6 +655,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     uint64_t *fin_bar = bars + 22;  // 256 arrivals
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 23);
     volatile int *s_abort = reinterpret_cast<volatile int *>(bars + 24);
+    uint64_t *mma_done_pv = bars + 25;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nqb = gridDim.x;
@@ -675,6 +678,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             mbar_init(&red_bar[b], kPfSoftmaxThreads);
         }
         mbar_init(fin_bar, kPfSoftmaxThreads);
+        mbar_init(mma_done_pv, 1);
         *s_abort = 0;
         fence_mbar_init();
     }
@@ -704,56 +708,66 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             }
         }
     } else if (warp == kPfWarpMma) {
-        // ------------------------------------------------ MMA issuer
+        // ------------------------------------------------ S = Q.K^T issuer
+        // S and PV are issued by two different warps so that each MMA goes
+        // to the tensor pipe as soon as its own operands are ready: with one
+        // issuing thread, S(i+1) queued behind PV(i-1), which waits for the
+        // softmax of tile i-1.
         if (lane == 0) {
             constexpr uint32_t idS = idesc_f16_f32(128, 64, 0, 0);
-            constexpr uint32_t idO = idesc_f16_f32(128, 256, 0, 1);
             // Descriptors are built once; per MMA only the start-address field
             // (bits 0-13, address >> 4, no carry for addresses < 256 KB)
             // advances, by compile-time constants.
             const uint64_t dK0 = smem_desc_sw128(smem_u32(sK), 16, 1024);
-            const uint64_t dV0 = smem_desc_sw128(smem_u32(sV), 8192, 1024);
             bool ok = mbar_wait(q_ready, 0, p.err);
             tc_fence_after();
-            for (int i = 0; ok && i <= ntiles; ++i) {
+            for (int i = 0; ok && i < ntiles; ++i) {
                 if (*s_abort) { ok = false; break; }
-                if (i < ntiles) {
-                    const int s = i % kPfStages;
-                    if (!mbar_wait(&k_full[s], (i / kPfStages) & 1, p.err)) { ok = false; break; }
-                    G3_TRACE(6, i);
-                    // the single S buffer is free once softmax(i-1) has read it
-                    if (i >= 1 && !mbar_wait(s_free, (i - 1) & 1, p.err)) { ok = false; break; }
-                    tc_fence_after();
-                    G3_TRACE(7, i);
-                    const uint64_t dK = dK0 + (uint64_t)((s * kPfKVStage) >> 4);
+                const int s = i % kPfStages;
+                if (!mbar_wait(&k_full[s], (i / kPfStages) & 1, p.err)) { ok = false; break; }
+                G3_TRACE(6, i);
+                // the single S buffer is free once softmax(i-1) has read it
+                if (i >= 1 && !mbar_wait(s_free, (i - 1) & 1, p.err)) { ok = false; break; }
+                tc_fence_after();
+                G3_TRACE(7, i);
+                const uint64_t dK = dK0 + (uint64_t)((s * kPfKVStage) >> 4);
 #pragma unroll
-                    for (int kk = 0; kk < 16; ++kk)
-                        tc_mma_f16_ts(tmem + kTmemS, tmem + kTmemQ + kk * 8,
-                                      dK + (uint64_t)(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4), idS,
-                                      kk > 0 ? 1u : 0u);
-                    tc_commit(&k_empty[s]);
-                    tc_commit(s_full);
-                    G3_TRACE(0, i);
-                }
-                if (i >= 1) {
-                    const int u = i - 1, su = u % kPfStages, pb = u & 1;
-                    if (!mbar_wait(&p_full[pb], (u >> 1) & 1, p.err)) { ok = false; break; }
-                    G3_TRACE(1, u);
-                    if (!mbar_wait(&v_full[su], (u / kPfStages) & 1, p.err)) { ok = false; break; }
-                    tc_fence_after();
-                    const uint64_t dV = dV0 + (uint64_t)((su * kPfKVStage) >> 4);
-#pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        tc_mma_f16_ts(tmem + kTmemO, tmem + kTmemP + pb * 32 + kk * 8,
-                                      dV + (uint64_t)((kk * 2048) >> 4), idO, (u > 0 || kk > 0) ? 1u : 0u);
-                    tc_commit(&v_empty[su]);
-                    tc_commit(&p_empty[pb]);
-                }
+                for (int kk = 0; kk < 16; ++kk)
+                    tc_mma_f16_ts(tmem + kTmemS, tmem + kTmemQ + kk * 8,
+                                  dK + (uint64_t)(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4), idS, kk > 0 ? 1u : 0u);
+                tc_commit(&k_empty[s]);
+                tc_commit(s_full);
+                G3_TRACE(0, i);
             }
             if (!ok) *s_abort = 1;
-            // Drain: every MMA issued above has completed once this fires.
+            // Drain: every MMA this thread issued has completed once this fires.
             tc_commit(mma_done);
             mbar_wait(mma_done, 0, nullptr);
+        }
+    } else if (warp == kPfWarpPv) {
+        // ------------------------------------------------ O += P.V issuer
+        if (lane == 0) {
+            constexpr uint32_t idO = idesc_f16_f32(128, 256, 0, 1);
+            const uint64_t dV0 = smem_desc_sw128(smem_u32(sV), 8192, 1024);
+            bool ok = true;
+            for (int u = 0; u < ntiles; ++u) {
+                if (*s_abort) { ok = false; break; }
+                const int su = u % kPfStages, pb = u & 1;
+                if (!mbar_wait(&p_full[pb], (u >> 1) & 1, p.err)) { ok = false; break; }
+                G3_TRACE(1, u);
+                if (!mbar_wait(&v_full[su], (u / kPfStages) & 1, p.err)) { ok = false; break; }
+                tc_fence_after();
+                const uint64_t dV = dV0 + (uint64_t)((su * kPfKVStage) >> 4);
+#pragma unroll
+                for (int kk = 0; kk < 4; ++kk)
+                    tc_mma_f16_ts(tmem + kTmemO, tmem + kTmemP + pb * 32 + kk * 8, dV + (uint64_t)((kk * 2048) >> 4),
+                                  idO, (u > 0 || kk > 0) ? 1u : 0u);
+                tc_commit(&v_empty[su]);
+                tc_commit(&p_empty[pb]);
+            }
+            if (!ok) *s_abort = 1;
+            tc_commit(mma_done_pv);
+            mbar_wait(mma_done_pv, 0, nullptr);
         }
     } else {
         // ------------------------------------------------ softmax warps 0-7
