@@ -656,7 +656,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 23);
     volatile int *s_abort = reinterpret_cast<volatile int *>(bars + 24);
     uint64_t *mma_done_pv = bars + 25;
+    uint64_t *out_bar = bars + 26;  // O staged in shared memory (256 arrivals)
 
+    if (threadIdx.x == 0) G3_TRACE(7, 255);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nqb = gridDim.x;
     const int qb = nqb - 1 - blockIdx.x;  // longest causal rows first
@@ -679,6 +681,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
         mbar_init(fin_bar, kPfSoftmaxThreads);
         mbar_init(mma_done_pv, 1);
+        mbar_init(out_bar, kPfSoftmaxThreads);
         *s_abort = 0;
         fence_mbar_init();
     }
@@ -778,25 +781,26 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
         const int lo_ok = p.is_global ? INT_MIN : qpos - (kWindow - 1);
         {
-            // Q rows into TMEM: this thread's 128 dims = 64 columns of fp16 pairs.
+            // Q rows into TMEM: this thread's 128 dims = 64 columns of fp16
+            // pairs.  All 16 loads are issued before the first TMEM store so
+            // their latencies overlap.
             const bool have = (t0 + tr) < p.T;
             const uint4 *src = reinterpret_cast<const uint4 *>(
                 p.q + ((size_t)(2 * g + hh) * p.T + (have ? t0 + tr : 0)) * kHeadDim + half * 128);
+            uint32_t w[4][16];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                uint32_t w[16];
-#pragma unroll
-                for (int c = 0; c < 4; ++c) {
-                    const uint4 u = have ? src[j * 4 + c] : make_uint4(0, 0, 0, 0);
-                    w[4 * c] = u.x;
-                    w[4 * c + 1] = u.y;
-                    w[4 * c + 2] = u.z;
-                    w[4 * c + 3] = u.w;
-                }
-                tmem_st16(lane_base + kTmemQ + half * 64 + j * 16, w);
+            for (int c = 0; c < 16; ++c) {
+                const uint4 u = have ? src[c] : make_uint4(0, 0, 0, 0);
+                w[c >> 2][4 * (c & 3)] = u.x;
+                w[c >> 2][4 * (c & 3) + 1] = u.y;
+                w[c >> 2][4 * (c & 3) + 2] = u.z;
+                w[c >> 2][4 * (c & 3) + 3] = u.w;
             }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) tmem_st16(lane_base + kTmemQ + half * 64 + j * 16, w[j]);
             tc_wait_st();
             tc_fence_before();
+            if (threadIdx.x == 0) G3_TRACE(5, 254);
             mbar_arrive(q_ready);
         }
         float m = -INFINITY;  // reference max of the row, log2 domain
@@ -907,23 +911,40 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
         if (ok) {
             tc_fence_after();
+            if (threadIdx.x == 0) G3_TRACE(5, 253);
             const float lt = red[512 + row] + red[640 + row];
             const float inv = lt > 0.f ? 1.0f / lt : 0.f;
-            const bool store = (t0 + tr) < p.T;
-            float *dst = p.out + ((size_t)(t0 + tr) * kHeads + 2 * g + hh) * kHeadDim + half * 128;
+            // Stage O/l in the (now idle) K/V ring, rows padded to 1040 B so
+            // the per-row float4 writes of a warp hit distinct banks, then
+            // write it out with fully coalesced stores: output row r of the
+            // tile is out[t0 + (r & 63)][2g + (r >> 6)][:], 1 KB contiguous.
+            float *stage = reinterpret_cast<float *>(sK);
+            constexpr int kRowF = kHeadDim + 4;
 #pragma unroll 1
             for (int cc = 0; cc < 4; ++cc) {
                 float o[32];
                 tmem_ld32(lane_base + kTmemO + half * 128 + cc * 32, o);
                 tc_wait_ld();
-                if (store) {
+                float *dst = stage + row * kRowF + half * 128 + cc * 32;
 #pragma unroll
-                    for (int k = 0; k < 32; k += 4)
-                        *reinterpret_cast<float4 *>(dst + cc * 32 + k) =
-                            make_float4(o[k] * inv, o[k + 1] * inv, o[k + 2] * inv, o[k + 3] * inv);
+                for (int k = 0; k < 32; k += 4)
+                    *reinterpret_cast<float4 *>(dst + k) =
+                        make_float4(o[k] * inv, o[k + 1] * inv, o[k + 2] * inv, o[k + 3] * inv);
+            }
+            mbar_arrive(out_bar);
+            ok = __all_sync(0xffffffffu, mbar_wait(out_bar, 0, p.err));
+            if (ok) {
+                const int nrow_valid = min(64, p.T - t0);
+                for (int idx = threadIdx.x; idx < 128 * 64; idx += kPfSoftmaxThreads) {
+                    const int r = idx >> 6, c4 = idx & 63;
+                    if ((r & 63) >= nrow_valid) continue;
+                    const float4 v4 = *reinterpret_cast<const float4 *>(stage + r * kRowF + c4 * 4);
+                    float *dst = p.out + ((size_t)(t0 + (r & 63)) * kHeads + 2 * g + (r >> 6)) * kHeadDim;
+                    *reinterpret_cast<float4 *>(dst + c4 * 4) = v4;
                 }
             }
         }
+        if (!ok) *s_abort = 1;
     }
     tc_fence_before();
     __syncthreads();
@@ -939,6 +960,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
+    if (threadIdx.x == 0) G3_TRACE(6, 255);
 }
 
 // ------------------------------------------------------------------------
