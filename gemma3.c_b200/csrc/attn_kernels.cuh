@@ -633,15 +633,15 @@ constexpr uint32_t kTmemP = 192;
 constexpr uint32_t kTmemO = 256;
 
 __global__ void __launch_bounds__(kPfThreads, 1)
-    prefill_fa_sm100(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-                     const PrefillParams p) {
+    prefill_fa_sm100(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const PrefillParams p) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char *sm = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     unsigned char *sK = sm + kPfOffK;
     unsigned char *sV = sm + kPfOffV;
     float *red = reinterpret_cast<float *>(sm + kPfOffRed);  // [2 parity][2 half][128] maxima, then [2][128] sums
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kPfOffBar);
-    uint64_t *q_ready = bars + 0;   // Q written to TMEM (256 arrivals)
+    uint64_t *q_smem = bars + 0;    // Q tile landed in shared memory (TMA)
     uint64_t *k_full = bars + 1;    // [3]
     uint64_t *k_empty = bars + 4;   // [3]
     uint64_t *v_full = bars + 7;    // [3]
@@ -657,6 +657,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     volatile int *s_abort = reinterpret_cast<volatile int *>(bars + 24);
     uint64_t *mma_done_pv = bars + 25;
     uint64_t *out_bar = bars + 26;  // O staged in shared memory (256 arrivals)
+    uint64_t *q_tmem = bars + 27;   // Q copied into TMEM; its smem is free
 
     if (threadIdx.x == 0) G3_TRACE(7, 255);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -673,7 +674,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < 23; ++i) mbar_init(&bars[i], 1);
-        mbar_init(q_ready, kPfSoftmaxThreads);
         mbar_init(s_free, kPfSoftmaxThreads);
         for (int b = 0; b < 2; ++b) {
             mbar_init(&p_full[b], kPfSoftmaxThreads);
@@ -682,6 +682,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         mbar_init(fin_bar, kPfSoftmaxThreads);
         mbar_init(mma_done_pv, 1);
         mbar_init(out_bar, kPfSoftmaxThreads);
+        mbar_init(q_tmem, 1);
         *s_abort = 0;
         fence_mbar_init();
     }
@@ -694,8 +695,15 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     if (warp == kPfWarpTma) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
+            prefetch_tmap(&tmQ);
             prefetch_tmap(&tmK);
             prefetch_tmap(&tmV);
+            // Q goes through V stages 0-1 (64 KB, 128-B swizzled K-major
+            // layout: 4 dim-chunks x [128 rows x 128 B]) on its way to TMEM.
+            mbar_expect_tx(q_smem, 128 * 256 * 2);
+            for (int c = 0; c < 4; ++c)
+                for (int hh = 0; hh < 2; ++hh)
+                    tma_load_3d(sV + c * 16384 + hh * 8192, &tmQ, 64 * c, t0, 2 * g + hh, q_smem);
             for (int i = 0; i < ntiles && !*s_abort; ++i) {
                 const int s = i % kPfStages, n = i / kPfStages;
                 const int krow = (j0 + i) * 64;
@@ -705,6 +713,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 for (int c = 0; c < 4; ++c)
                     tma_load_3d(sK + s * kPfKVStage + c * 8192, &tmK, 64 * c, krow, g, &k_full[s]);
                 if (n >= 1 && !mbar_wait(&v_empty[s], (n - 1) & 1, p.err)) { *s_abort = 1; break; }
+                if (i == 0 && !mbar_wait(q_tmem, 0, p.err)) { *s_abort = 1; break; }
                 mbar_expect_tx(&v_full[s], kPfKVStage);
                 for (int c = 0; c < 4; ++c)
                     tma_load_3d(sV + s * kPfKVStage + c * 8192, &tmV, 64 * c, krow, g, &v_full[s]);
@@ -722,8 +731,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             // (bits 0-13, address >> 4, no carry for addresses < 256 KB)
             // advances, by compile-time constants.
             const uint64_t dK0 = smem_desc_sw128(smem_u32(sK), 16, 1024);
-            bool ok = mbar_wait(q_ready, 0, p.err);
+            bool ok = mbar_wait(q_smem, 0, p.err);
             tc_fence_after();
+            if (ok) {
+                // Q -> TMEM columns kTmemQ.. as 16 slices of K=16 (8 columns each)
+                const uint64_t dQ = smem_desc_sw128(smem_u32(sV), 16, 1024);
+#pragma unroll
+                for (int kk = 0; kk < 16; ++kk)
+                    tc_cp_128x256b(tmem + kTmemQ + kk * 8, dQ + (uint64_t)(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4));
+                tc_commit(q_tmem);
+            }
             for (int i = 0; ok && i < ntiles; ++i) {
                 if (*s_abort) { ok = false; break; }
                 const int s = i % kPfStages;
@@ -780,29 +797,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const int qpos = p.start_pos + t0 + tr;
         const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
         const int lo_ok = p.is_global ? INT_MIN : qpos - (kWindow - 1);
-        {
-            // Q rows into TMEM: this thread's 128 dims = 64 columns of fp16
-            // pairs.  All 16 loads are issued before the first TMEM store so
-            // their latencies overlap.
-            const bool have = (t0 + tr) < p.T;
-            const uint4 *src = reinterpret_cast<const uint4 *>(
-                p.q + ((size_t)(2 * g + hh) * p.T + (have ? t0 + tr : 0)) * kHeadDim + half * 128);
-            uint32_t w[4][16];
-#pragma unroll
-            for (int c = 0; c < 16; ++c) {
-                const uint4 u = have ? src[c] : make_uint4(0, 0, 0, 0);
-                w[c >> 2][4 * (c & 3)] = u.x;
-                w[c >> 2][4 * (c & 3) + 1] = u.y;
-                w[c >> 2][4 * (c & 3) + 2] = u.z;
-                w[c >> 2][4 * (c & 3) + 3] = u.w;
-            }
-#pragma unroll
-            for (int j = 0; j < 4; ++j) tmem_st16(lane_base + kTmemQ + half * 64 + j * 16, w[j]);
-            tc_wait_st();
-            tc_fence_before();
-            if (threadIdx.x == 0) G3_TRACE(5, 254);
-            mbar_arrive(q_ready);
-        }
         float m = -INFINITY;  // reference max of the row, log2 domain
         float l = 0.f;        // this half's share of the row sum
         bool ok = true;

@@ -416,8 +416,9 @@ static int prefill_impl(gemma3_cuda_ctx *ctx, int layer, int seq, const float *Q
                                                                      ctx->vst, ctx->st_rows, ctx->err);
     if (int r = check_launch(ctx, 1)) return r;
 
-    CUtensorMap tk, tv;
+    CUtensorMap tq, tk, tv;
     const size_t plane = (size_t)ctx->st_rows * kHeadDim;
+    if (int r = make_map(&tq, ctx->qst, T, (size_t)T * kHeadDim, kHeads)) return r;
     if (int r = make_map(&tk, ctx->kst, lrows, plane, kKvHeads)) return r;
     if (int r = make_map(&tv, ctx->vst, lrows, plane, kKvHeads)) return r;
     g3::PrefillParams p;
@@ -431,7 +432,7 @@ static int prefill_impl(gemma3_cuda_ctx *ctx, int layer, int seq, const float *Q
     const int nqb = (T + 63) / 64;
     size_t e0;
     prof_begin(ctx, &e0);
-    g3::prefill_fa_sm100<<<dim3(nqb, kKvHeads), g3::kPfThreads, g3::kPfSmem, ctx->stream>>>(tk, tv, p);
+    g3::prefill_fa_sm100<<<dim3(nqb, kKvHeads), g3::kPfThreads, g3::kPfSmem, ctx->stream>>>(tq, tk, tv, p);
     if (ctx->prof) {
         // algorithmic FLOPs: 2 (QK) + 2 (PV) x 256 x 8 heads per attended key
         double keys = 0;

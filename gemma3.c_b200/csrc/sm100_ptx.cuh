@@ -138,6 +138,12 @@ __device__ __forceinline__ void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, 
         "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
         "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate));
 }
+// Shared memory -> TMEM copy of a 128-row x 256-bit slice (128 lanes x 8
+// columns) described by a matrix descriptor; ordered with this thread's
+// later tcgen05.mma.
+__device__ __forceinline__ void tc_cp_128x256b(uint32_t taddr, uint64_t s_desc) {
+    asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(s_desc));
+}
 // Arrive once on an mbarrier when every previously issued tcgen05.mma of
 // this thread has completed.
 __device__ __forceinline__ void tc_commit(uint64_t *bar) {
