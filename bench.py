@@ -460,19 +460,18 @@ def secondary_decode1(args, torch, gc, pk, dev):
     return {"workload": "configs[1] global-layer decode, B=1, 8192 keys, L2 flushed between calls", **res}
 
 
-def ncu_traffic(kernel):
-    """DRAM bytes per launch of `kernel` from the committed ncu summary
-    (profiles/ncu_traffic.txt: '<kernel> <bytes_per_launch> <note>'), or None."""
+def ncu_traffic(kernel, bytes_per_launch):
+    """DRAM bytes per launch of `kernel`: the per-launch algorithmic bytes
+    scaled by the DRAM/algorithmic ratio of the committed ncu capture
+    (profiles/ncu_traffic.txt, measured on a smaller case of the same
+    kernel: traffic grows in proportion to the rows streamed), or None."""
     p = os.path.join(ROOT, "profiles", "ncu_traffic.txt")
-    if not os.path.exists(p):
+    if not os.path.exists(p) or not bytes_per_launch:
         return None
     for line in open(p):
         parts = line.split()
-        if len(parts) >= 2 and parts[0] == kernel and not line.startswith("#"):
-            try:
-                return float(parts[1])
-            except ValueError:
-                return None
+        if len(parts) >= 2 and parts[0] == kernel:
+            return round(float(parts[1]) * bytes_per_launch, 0)
     return None
 
 
@@ -556,7 +555,7 @@ def main():
         "clocks": h["clocks"],
     }
     rf = dict(h["roofline"])
-    tr = ncu_traffic("decode_splitkv_bf16")
+    tr = ncu_traffic("decode_splitkv_bf16", rf.get("bytes_per_launch"))
     rf["traffic"] = tr
     rf["peak_src"] = f"{pk['src']} hbm_gbs (MEASURED_PEAKS.json)" if pk["src"] == "measured" else "fallback 6.65 TB/s"
     for kk in ("achieved", "frac", "avg_launch_us", "bytes_per_launch"):
