@@ -1,0 +1,208 @@
+"""Context-parallel (split-KV) decode across GPUs: BASELINE configs[4].
+
+A global layer's KV range is split contiguously over R ranks; each rank emits a
+log-sum-exp partial (m, l, O) per (sequence, q head) for its shard, the
+partials are all-gathered and merged.
+
+  * test_lse_exchange_gloo   - CPU, two gloo processes: the exchange step with
+                               real collectives, partials computed in numpy;
+  * test_split_emulated_*    - one GPU: R contexts with kv_rank/kv_ranks set,
+                               partial + merge through the C-ABI, against an
+                               unsplit context;
+  * test_split_nccl_2gpu     - two GPUs: NCCL all-gather inside
+                               gemma3_cuda_attn_decode_dev (skipped with fewer).
+"""
+import os
+import socket
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+import synth
+from oracles import rel_err
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LOG2E = 1.4426950408889634
+
+
+def _partial(q, k, v):
+    """numpy (m, l, O) of one shard, log2 domain, q [8][256], k/v [rows][4][256]."""
+    out = np.zeros((8, 258))
+    for h in range(8):
+        s = (k[:, h // 2] @ q[h]) / 16.0 * LOG2E
+        if s.size == 0:
+            out[h, 0], out[h, 1] = -np.inf, 0.0
+            continue
+        m = s.max()
+        p = np.exp2(s - m)
+        out[h, 0], out[h, 1], out[h, 2:] = m, p.sum(), p @ v[:, h // 2]
+    return out
+
+
+def _merge(parts):
+    """parts [R][8][258] -> [8][256]."""
+    M = parts[:, :, 0].max(axis=0)
+    f = np.where(np.isfinite(parts[:, :, 0]), np.exp2(parts[:, :, 0] - M), 0.0)
+    L = (parts[:, :, 1] * f).sum(0)
+    O = (parts[:, :, 2:] * f[:, :, None]).sum(0)
+    return O / L[:, None]
+
+
+def _gloo_worker(rank, world, port, rows, result):
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    q = synth.normal(1, (8, 256)).astype(np.float64)
+    k = synth.normal(2, (rows, 4, 256)).astype(np.float64)
+    v = synth.normal(3, (rows, 4, 256)).astype(np.float64)
+    S = -(-rows // world)  # the library's shard: ceil(max_context / kv_ranks)
+    lo, hi = min(rows, rank * S), min(rows, rank * S + S)
+    mine = torch.from_numpy(_partial(q, k[lo:hi], v[lo:hi]))
+    gathered = [torch.zeros_like(mine) for _ in range(world)]
+    dist.all_gather(gathered, mine)
+    got = _merge(np.stack([g.numpy() for g in gathered]))
+    sys.path.insert(0, ROOT)
+    import bench
+    d = bench.Dist()
+    d.pg, d.world, d.rank = dist, world, rank
+    mx, sm = d.max(float(rank + 1)), d.sum(1.0)
+    if rank == 0:
+        want = _merge(_partial(q, k, v)[None])
+        result.put((float(np.max(np.abs(got - want))), mx, sm))
+    dist.destroy_process_group()
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+@pytest.mark.parametrize("world,rows", [(2, 1000), (2, 3), (3, 777)])
+def test_lse_exchange_gloo(world, rows):
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gloo_worker, args=(r, world, port, rows, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    err, mx, sm = q.get(timeout=5)
+    assert err < 1e-9
+    assert mx == world and sm == world
+
+
+# ---------------------------------------------------------------- GPU
+def _setup(gc, ctx, layer, seqs, ctxlen, full_k, full_v):
+    ctx.upload_rope(gc.rope_table(ctxlen, 1e4), gc.rope_table(ctxlen, 1e6))
+    qn, kn = synth.qk_norm_gains(4)
+    ctx.set_qk_norm(layer, qn, kn)
+    S = -(-ctxlen // ctx.cfg.kv_ranks)
+    lo = min(ctxlen, ctx.cfg.kv_rank * S)
+    hi = min(ctxlen, lo + S)
+    for s in range(seqs):
+        if hi > lo:
+            ctx.import_cache(layer, s, full_k[s][lo:hi], full_v[s][lo:hi])
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("R,kv", [(2, 0), (3, 1), (4, 1)])
+def test_split_emulated_one_gpu(R, kv):
+    import torch
+    import gemma3_cuda as gc
+    layer, ctxlen, B = 5, 4096, 3
+    pos = [4095, 2500, 700]
+    full_k = [synth.normal(10 + s, (ctxlen, 4, 256)) for s in range(B)]
+    full_v = [synth.normal(20 + s, (ctxlen, 4, 256)) for s in range(B)]
+    Q, K, V = synth.normal(30, (B, 2048)), synth.normal(31, (B, 1024)), synth.normal(32, (B, 1024))
+    ref = gc.Context(max_context=ctxlen, max_batch=B, kv_dtype=kv, max_prefill=64)
+    _setup(gc, ref, layer, B, ctxlen, full_k, full_v)
+    want = ref.attn_decode(layer, list(range(B)), pos, Q, K, V)
+    ref.close()
+    q, k, v = (torch.from_numpy(a).cuda() for a in (Q, K, V))
+    parts = torch.empty(R, B, 8, 258, device="cuda")
+    ctxs = []
+    for r in range(R):
+        c = gc.Context(max_context=ctxlen, max_batch=B, kv_dtype=kv, max_prefill=64, kv_rank=r, kv_ranks=R)
+        _setup(gc, c, layer, B, ctxlen, full_k, full_v)
+        c.attn_decode_partial_dev(layer, list(range(B)), pos, q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                  parts[r].data_ptr())
+        c.synchronize()
+        ctxs.append(c)
+    out = torch.empty(B, 2048, device="cuda")
+    ctxs[0].merge_partials_dev(R, B, parts.data_ptr(), out.data_ptr())
+    ctxs[0].synchronize()
+    assert rel_err(out.cpu().numpy(), want) <= 1e-3
+    # the new row landed only on the rank owning its position
+    S = -(-ctxlen // R)
+    for b, p in enumerate(pos):
+        owner = p // S
+        kd, vd = ctxs[owner].export_cache(layer, b)
+        assert np.allclose(vd[p - owner * S], V[b].reshape(4, 256), atol=1e-2)
+    for c in ctxs:
+        c.close()
+
+
+NCCL_CHILD = r'''
+import os, sys, json
+sys.path[:0] = [os.path.join(sys.argv[1], "gemma3.c_b200"), os.path.join(sys.argv[1], "oracle")]
+import numpy as np, torch, torch.distributed as dist
+import gemma3_cuda as gc, synth
+rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+torch.cuda.set_device(rank)
+dist.init_process_group("gloo")
+layer, ctxlen, B, pos = 5, 4096, 2, [4095, 1500]
+full_k = [synth.normal(10 + s, (ctxlen, 4, 256)) for s in range(B)]
+full_v = [synth.normal(20 + s, (ctxlen, 4, 256)) for s in range(B)]
+Q, K, V = synth.normal(30, (B, 2048)), synth.normal(31, (B, 1024)), synth.normal(32, (B, 1024))
+def setup(c):
+    c.upload_rope(gc.rope_table(ctxlen, 1e4), gc.rope_table(ctxlen, 1e6))
+    qn, kn = synth.qk_norm_gains(4); c.set_qk_norm(layer, qn, kn)
+    S = -(-ctxlen // c.cfg.kv_ranks); lo = min(ctxlen, c.cfg.kv_rank * S); hi = min(ctxlen, lo + S)
+    for s in range(B):
+        c.import_cache(layer, s, full_k[s][lo:hi], full_v[s][lo:hi])
+uid = [gc.Context.comm_unique_id() if rank == 0 else None]
+dist.broadcast_object_list(uid, src=0)
+c = gc.Context(max_context=ctxlen, max_batch=B, kv_dtype=gc.KV_BF16, device=rank, max_prefill=64,
+               kv_rank=rank, kv_ranks=world)
+setup(c)
+c.comm_init(uid[0])
+q, k, v = (torch.from_numpy(a).cuda() for a in (Q, K, V))
+out = torch.empty(B, 2048, device="cuda")
+c.attn_decode_dev(layer, [0, 1], pos, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr())
+c.synchronize()
+got = out.cpu().numpy()
+if rank == 0:
+    ref = gc.Context(max_context=ctxlen, max_batch=B, kv_dtype=gc.KV_BF16, device=0, max_prefill=64)
+    setup(ref)
+    want = ref.attn_decode(layer, [0, 1], pos, Q, K, V)
+    e = np.max(np.abs(got - want)) / np.sqrt(np.mean(want ** 2))
+    print(json.dumps({"err": float(e)}))
+c.close()
+dist.destroy_process_group()
+'''
+
+
+@pytest.mark.gpu
+def test_split_nccl_2gpu(tmp_path):
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    script = tmp_path / "child.py"
+    script.write_text(NCCL_CHILD)
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+                        "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), str(script), ROOT],
+                       capture_output=True, text=True, timeout=300, env=env)
+    assert r.returncode == 0, r.stderr[-3000:]
+    line = [l for l in r.stdout.splitlines() if l.startswith("{")][-1]
+    import json
+    assert json.loads(line)["err"] <= 1e-3
