@@ -53,33 +53,73 @@ struct KvType<__nv_bfloat16> {
 
 __device__ __forceinline__ float bf16_bits_to_f(uint16_t h) { return __uint_as_float((uint32_t)h << 16); }
 
-// Block-wide sum over the 128 threads of a prologue block.
-__device__ __forceinline__ float block128_sum(float v, float *red) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-    __syncthreads();
-    float s = red[0] + red[1] + red[2] + red[3];
-    __syncthreads();
-    return s;
+// A head row (256 values) is handled by one warp: lane l owns dims 4l..4l+3
+// and 128+4l..128+4l+3, i.e. the four rotate-half pairs (i, i+128) of its i's,
+// so RoPE never leaves the lane and the RMSNorm sum is one warp reduction.
+struct HeadRow {
+    float a[4];  // x[4l + j]
+    float b[4];  // x[128 + 4l + j]
+};
+
+__device__ __forceinline__ void load_head_row(const float *x, int lane, HeadRow &r) {
+    const float4 u = *reinterpret_cast<const float4 *>(x + 4 * lane);
+    const float4 v = *reinterpret_cast<const float4 *>(x + 128 + 4 * lane);
+    r.a[0] = u.x; r.a[1] = u.y; r.a[2] = u.z; r.a[3] = u.w;
+    r.b[0] = v.x; r.b[1] = v.y; r.b[2] = v.z; r.b[3] = v.w;
 }
 
-// One 256-wide head row: thread i (of 128) holds the rotate-half pair
-// (x[i], x[i+128]).  Applies RMSNorm with the (1+w) gain when w != null,
-// then RoPE at the given table row.
-__device__ __forceinline__ void norm_rope_pair(float &a, float &b, const uint16_t *w, float eps,
-                                               const float *rope_row, float *red) {
-    const int i = threadIdx.x;
+// RMSNorm with the (1+w) gain when w != null (gemma3_kernels.c:289-304),
+// then RoPE from the table row (gemma3_kernels.c:470-484).
+__device__ __forceinline__ void norm_rope_row(HeadRow &r, const uint16_t *w, float eps, const float *rope_row,
+                                              int lane) {
     if (w) {
-        float ss = block128_sum(a * a + b * b, red);
-        float r = 1.0f / sqrtf(ss / (float)kHeadDim + eps);
-        a = a * r * (1.0f + bf16_bits_to_f(w[i]));
-        b = b * r * (1.0f + bf16_bits_to_f(w[i + 128]));
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) ss += r.a[j] * r.a[j] + r.b[j] * r.b[j];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        const float rr = 1.0f / sqrtf(ss / (float)kHeadDim + eps);
+        const uint2 wa = *reinterpret_cast<const uint2 *>(w + 4 * lane);
+        const uint2 wb = *reinterpret_cast<const uint2 *>(w + 128 + 4 * lane);
+        const uint16_t ga[4] = {(uint16_t)(wa.x & 0xffff), (uint16_t)(wa.x >> 16), (uint16_t)(wa.y & 0xffff),
+                                (uint16_t)(wa.y >> 16)};
+        const uint16_t gb[4] = {(uint16_t)(wb.x & 0xffff), (uint16_t)(wb.x >> 16), (uint16_t)(wb.y & 0xffff),
+                                (uint16_t)(wb.y >> 16)};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            r.a[j] = r.a[j] * rr * (1.0f + bf16_bits_to_f(ga[j]));
+            r.b[j] = r.b[j] * rr * (1.0f + bf16_bits_to_f(gb[j]));
+        }
     }
-    const float c = rope_row[2 * i], s = rope_row[2 * i + 1];
-    const float x0 = a, x1 = b;
-    a = x0 * c - x1 * s;
-    b = x0 * s + x1 * c;
+    const float4 c0 = *reinterpret_cast<const float4 *>(rope_row + 8 * lane);      // (cos,sin) of i = 4l, 4l+1
+    const float4 c1 = *reinterpret_cast<const float4 *>(rope_row + 8 * lane + 4);  // i = 4l+2, 4l+3
+    const float cs[4] = {c0.x, c0.z, c1.x, c1.z}, sn[4] = {c0.y, c0.w, c1.y, c1.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float x0 = r.a[j], x1 = r.b[j];
+        r.a[j] = x0 * cs[j] - x1 * sn[j];
+        r.b[j] = x0 * sn[j] + x1 * cs[j];
+    }
+}
+
+template <typename KVT>
+__device__ __forceinline__ void store4(KVT *dst, const float (&v)[4]);
+template <>
+__device__ __forceinline__ void store4<float>(float *dst, const float (&v)[4]) {
+    *reinterpret_cast<float4 *>(dst) = make_float4(v[0], v[1], v[2], v[3]);
+}
+template <>
+__device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16 *dst, const float (&v)[4]) {
+    *reinterpret_cast<uint2 *>(dst) = make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
+}
+__device__ __forceinline__ void store4_half(__half *dst, const float (&v)[4]) {
+    *reinterpret_cast<uint2 *>(dst) = make_uint2(pack_f16x2(v[0], v[1]), pack_f16x2(v[2], v[3]));
+}
+// Rounds 4 values to the cache dtype and back (what the cache will hold).
+template <typename KVT>
+__device__ __forceinline__ void through_dtype(float (&v)[4]) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = KvType<KVT>::to_f(KvType<KVT>::from_f(v[j]));
 }
 
 struct LayerDev {
@@ -118,42 +158,36 @@ struct DecodeBatch {
 };
 
 template <typename KVT>
-__global__ void __launch_bounds__(128) prologue_decode(const float *__restrict__ Q, const float *__restrict__ K,
+__global__ void __launch_bounds__(512) prologue_decode(const float *__restrict__ Q, const float *__restrict__ K,
                                                        const float *__restrict__ V, LayerDev L, float eps,
                                                        const __grid_constant__ DecodeBatch batch,
                                                        float *__restrict__ qout) {
-    __shared__ float red[4];
-    const int b = blockIdx.x, y = blockIdx.y, i = threadIdx.x;
+    const int b = blockIdx.x, y = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pos = batch.pos[b], seq = batch.seq[b];
     const float *rope_row = L.rope + (size_t)pos * kHeadDim;
+    HeadRow r;
     if (y < kHeads) {
-        const float *x = Q + (size_t)b * kHeads * kHeadDim + y * kHeadDim;
-        float a = x[i], c = x[i + 128];
-        norm_rope_pair(a, c, L.qn && L.kn ? L.qn : nullptr, eps, rope_row, red);
+        load_head_row(Q + ((size_t)b * kHeads + y) * kHeadDim, lane, r);
+        norm_rope_row(r, L.qn && L.kn ? L.qn : nullptr, eps, rope_row, lane);
         float *o = qout + ((size_t)b * kHeads + y) * kHeadDim;
-        o[i] = a * kScaleLog2;
-        o[i + 128] = c * kScaleLog2;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            r.a[j] *= kScaleLog2;
+            r.b[j] *= kScaleLog2;
+        }
+        store4<float>(o + 4 * lane, r.a);
+        store4<float>(o + 128 + 4 * lane, r.b);
         return;
     }
     const int row = cache_row(L, pos);
-    if (y < kHeads + kKvHeads) {
-        const int h = y - kHeads;
-        const float *x = K + (size_t)b * kKvHeads * kHeadDim + h * kHeadDim;
-        float a = x[i], c = x[i + 128];
-        norm_rope_pair(a, c, L.qn && L.kn ? L.kn : nullptr, eps, rope_row, red);
-        if (row >= 0) {
-            KVT *dst = plane<KVT>(L, seq, 0, h) + (size_t)row * kHeadDim;
-            dst[i] = KvType<KVT>::from_f(a);
-            dst[i + 128] = KvType<KVT>::from_f(c);
-        }
-    } else {
-        const int h = y - kHeads - kKvHeads;
-        const float *x = V + (size_t)b * kKvHeads * kHeadDim + h * kHeadDim;
-        if (row >= 0) {
-            KVT *dst = plane<KVT>(L, seq, 1, h) + (size_t)row * kHeadDim;
-            dst[i] = KvType<KVT>::from_f(x[i]);
-            dst[i + 128] = KvType<KVT>::from_f(x[i + 128]);
-        }
+    const int sel = y < kHeads + kKvHeads ? 0 : 1;
+    const int h = y - kHeads - sel * kKvHeads;
+    load_head_row((sel ? V : K) + ((size_t)b * kKvHeads + h) * kHeadDim, lane, r);
+    if (!sel) norm_rope_row(r, L.qn && L.kn ? L.kn : nullptr, eps, rope_row, lane);
+    if (row >= 0) {
+        KVT *dst = plane<KVT>(L, seq, sel, h) + (size_t)row * kHeadDim;
+        store4<KVT>(dst + 4 * lane, r.a);
+        store4<KVT>(dst + 128 + 4 * lane, r.b);
     }
 }
 
@@ -172,58 +206,54 @@ __global__ void __launch_bounds__(128) prologue_decode(const float *__restrict__
 // N(0,1) data, above the 1e-2 parity bar; fp16's 11-bit significand is ~8x
 // tighter.
 // ------------------------------------------------------------------------
+__device__ __forceinline__ void check_half_range(const HeadRow &r, unsigned *err) {
+    bool bad = false;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) bad |= !(fabsf(r.a[j]) <= 65504.f) || !(fabsf(r.b[j]) <= 65504.f);
+    if (bad) atomicOr(err, kErrRange);
+}
+
 __device__ __forceinline__ __half to_half_checked(float x, unsigned *err) {
     if (!(fabsf(x) <= 65504.f)) atomicOr(err, kErrRange);
     return __float2half_rn(x);
 }
 
 template <typename KVT>
-__global__ void __launch_bounds__(128) prologue_prefill(const float *__restrict__ Q, const float *__restrict__ K,
+__global__ void __launch_bounds__(512) prologue_prefill(const float *__restrict__ Q, const float *__restrict__ K,
                                                         const float *__restrict__ V, LayerDev L, float eps, int seq,
                                                         int T, int start_pos, int kv_pos0,
                                                         __half *__restrict__ qst, __half *__restrict__ kst,
                                                         __half *__restrict__ vst, int st_rows, unsigned *err) {
-    __shared__ float red[4];
-    const int t = blockIdx.x, y = blockIdx.y, i = threadIdx.x;
+    const int t = blockIdx.x, y = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pos = start_pos + t;
     const float *rope_row = L.rope + (size_t)pos * kHeadDim;
+    HeadRow r;
     if (y < kHeads) {
-        const float *x = Q + (size_t)t * kHeads * kHeadDim + y * kHeadDim;
-        float a = x[i], c = x[i + 128];
-        norm_rope_pair(a, c, L.qn && L.kn ? L.qn : nullptr, eps, rope_row, red);
+        load_head_row(Q + ((size_t)t * kHeads + y) * kHeadDim, lane, r);
+        norm_rope_row(r, L.qn && L.kn ? L.qn : nullptr, eps, rope_row, lane);
         __half *o = qst + ((size_t)y * T + t) * kHeadDim;
-        o[i] = to_half_checked(a, err);
-        o[i + 128] = to_half_checked(c, err);
+        check_half_range(r, err);
+        store4_half(o + 4 * lane, r.a);
+        store4_half(o + 128 + 4 * lane, r.b);
         return;
     }
     const bool ring_ok = L.is_global || (pos >= start_pos + T - kWindow);
     const int row = ring_ok ? cache_row(L, pos) : -1;
-    const int srow = pos - kv_pos0;
-    float a, c;
-    int h, sel;
-    if (y < kHeads + kKvHeads) {
-        h = y - kHeads;
-        sel = 0;
-        const float *x = K + (size_t)t * kKvHeads * kHeadDim + h * kHeadDim;
-        a = x[i];
-        c = x[i + 128];
-        norm_rope_pair(a, c, L.qn && L.kn ? L.kn : nullptr, eps, rope_row, red);
-    } else {
-        h = y - kHeads - kKvHeads;
-        sel = 1;
-        const float *x = V + (size_t)t * kKvHeads * kHeadDim + h * kHeadDim;
-        a = x[i];
-        c = x[i + 128];
-    }
-    const KVT ka = KvType<KVT>::from_f(a), kc = KvType<KVT>::from_f(c);
+    const int sel = y < kHeads + kKvHeads ? 0 : 1;
+    const int h = y - kHeads - sel * kKvHeads;
+    load_head_row((sel ? V : K) + ((size_t)t * kKvHeads + h) * kHeadDim, lane, r);
+    if (!sel) norm_rope_row(r, L.qn && L.kn ? L.kn : nullptr, eps, rope_row, lane);
     if (row >= 0) {
         KVT *dst = plane<KVT>(L, seq, sel, h) + (size_t)row * kHeadDim;
-        dst[i] = ka;
-        dst[i + 128] = kc;
+        store4<KVT>(dst + 4 * lane, r.a);
+        store4<KVT>(dst + 128 + 4 * lane, r.b);
     }
-    __half *s = (sel ? vst : kst) + ((size_t)h * st_rows + srow) * kHeadDim;
-    s[i] = to_half_checked(KvType<KVT>::to_f(ka), err);
-    s[i + 128] = to_half_checked(KvType<KVT>::to_f(kc), err);
+    through_dtype<KVT>(r.a);
+    through_dtype<KVT>(r.b);
+    check_half_range(r, err);
+    __half *sdst = (sel ? vst : kst) + ((size_t)h * st_rows + (pos - kv_pos0)) * kHeadDim;
+    store4_half(sdst + 4 * lane, r.a);
+    store4_half(sdst + 128 + 4 * lane, r.b);
 }
 
 // Copies the cached rows of positions [kv_pos0, start_pos) into the fp16

@@ -411,7 +411,7 @@ static int prefill_impl(gemma3_cuda_ctx *ctx, int layer, int seq, const float *Q
                                                                           ctx->st_rows, ctx->err);
         if (int r = check_launch(ctx, 1)) return r;
     }
-    g3::prologue_prefill<KVT><<<dim3(T, 16), 128, 0, ctx->stream>>>(Q, K, V, L, ctx->cfg.rmsnorm_eps, seq, T,
+    g3::prologue_prefill<KVT><<<T, 512, 0, ctx->stream>>>(Q, K, V, L, ctx->cfg.rmsnorm_eps, seq, T,
                                                                      start_pos, kv_pos0, ctx->qst, ctx->kst,
                                                                      ctx->vst, ctx->st_rows, ctx->err);
     if (int r = check_launch(ctx, 1)) return r;
@@ -550,7 +550,7 @@ static int decode_impl(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_id
     DecodePlan pl;
     plan_decode<KVT>(ctx, layer, B, seq_ids, pos, pl);
     g3::LayerDev L = layer_dev(ctx, layer);
-    g3::prologue_decode<KVT><<<dim3(B, 16), 128, 0, ctx->stream>>>(Q, K, V, L, ctx->cfg.rmsnorm_eps, pl.batch,
+    g3::prologue_decode<KVT><<<B, 512, 0, ctx->stream>>>(Q, K, V, L, ctx->cfg.rmsnorm_eps, pl.batch,
                                                                     ctx->qdec);
     if (int r = check_launch(ctx, 1)) return r;
     g3::DecodeParams p;
