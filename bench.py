@@ -460,6 +460,58 @@ def secondary_decode1(args, torch, gc, pk, dev):
     return {"workload": "configs[1] global-layer decode, B=1, 8192 keys, L2 flushed between calls", **res}
 
 
+def secondary_context_parallel(args, dist, torch, gc, pk):
+    """B=4 sequences at 131,072 keys, BF16 KV; the 5 global layers'
+    KV range is split over the N ranks (partials merged with an NCCL
+    all-gather inside the library), the 29 local layers run on every rank.
+    Metric: the job's algorithmic KV bytes per step / max-over-ranks time."""
+    B, ctxlen = 4, 131072
+    pos = ctxlen - 1
+    dev = dist.local
+    c = gc.Context(max_context=ctxlen, max_batch=B, kv_dtype=gc.KV_BF16, device=dev, max_prefill=64,
+                   kv_rank=dist.rank, kv_ranks=dist.world)
+    c.upload_rope(gc.rope_table(ctxlen, 1e4), gc.rope_table(ctxlen, 1e6))
+    S = -(-ctxlen // dist.world)
+    lo = min(ctxlen, dist.rank * S)
+    for l in range(N_LAYERS):
+        for s_ in range(B):
+            rows = max(0, min(lo + S, pos) - lo) if l in GLOBAL_LAYERS else 1024
+            if rows:
+                c.fill_cache_random(l, s_, rows, 77 * s_ + l + (1000003 * dist.rank if l in GLOBAL_LAYERS else 0))
+    if dist.world > 1:
+        uid = [gc.Context.comm_unique_id() if dist.rank == 0 else None]
+        dist.pg.broadcast_object_list(uid, src=0)
+        c.comm_init(uid[0])
+    g = torch.Generator(device=f"cuda:{dev}").manual_seed(4321)
+    q = torch.randn(N_LAYERS, B, 2048, device=f"cuda:{dev}", generator=g)
+    k = torch.randn(N_LAYERS, B, 1024, device=f"cuda:{dev}", generator=g)
+    v = torch.randn(N_LAYERS, B, 1024, device=f"cuda:{dev}", generator=g)
+    out = torch.empty(N_LAYERS, B, 2048, device=f"cuda:{dev}")
+    stream = torch.cuda.ExternalStream(c.stream, device=f"cuda:{dev}")
+    seqs, poss = list(range(B)), [pos] * B
+
+    def step():
+        for l in range(N_LAYERS):
+            c.attn_decode_dev(l, seqs, poss, q[l].data_ptr(), k[l].data_ptr(), v[l].data_ptr(), out[l].data_ptr())
+
+    for _ in range(args.warmup):
+        step()
+    c.synchronize()
+    dist.barrier()
+    steps = max(args.steps, 10)
+    ms = dist.max(ev_time(torch, stream, lambda: [step() for _ in range(steps)]))
+    c.synchronize()
+    c.close()
+    del q, k, v, out
+    torch.cuda.empty_cache()
+    byts = (len(GLOBAL_LAYERS) * ctxlen + (N_LAYERS - len(GLOBAL_LAYERS)) * 1024) * B * ROW_BYTES_BF16
+    gbs = byts * steps / (ms / 1e3) / 1e9
+    return {"workload": "configs[4] long-context decode, B=4 @ 131072 keys, global-layer KV split over "
+                        f"{dist.world} GPU(s), NCCL all-gather + LSE merge; local layers on every rank",
+            "value": round(gbs, 1), "unit": "GB/s", "ms_per_step": round(ms / steps, 3),
+            "algorithmic_bytes_per_step": byts, "frac_of_n_x_hbm": round(gbs / (pk["hbm_gbs"] * dist.world), 4)}
+
+
 def ncu_traffic(kernel, bytes_per_launch):
     """DRAM bytes per launch of `kernel`: the per-launch algorithmic bytes
     scaled by the DRAM/algorithmic ratio of the committed ncu capture
@@ -562,10 +614,14 @@ def main():
         if rf.get(kk) is not None:
             rf[kk] = round(rf[kk], 4 if kk == "frac" else 2)
     line["roofline"] = rf
+    if not args.no_secondary:
+        cp = secondary_context_parallel(args, dist, torch, gc, pk)
     if dist.rank == 0 and dist.world == 1:
         if not args.no_secondary:
             line["secondary"] = {"prefill": secondary_prefill(args, torch, gc, pk, dist.local),
                                  "decode_b1": secondary_decode1(args, torch, gc, pk, dist.local)}
+    if not args.no_secondary:
+        line.setdefault("secondary", {})["context_parallel"] = cp
         if not args.no_cpu_baseline:
             try:
                 line["cpu_baseline"] = cpu_baseline_sample()
