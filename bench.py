@@ -569,6 +569,10 @@ def main():
     global B_TOTAL
     args = parse_args()
     B_TOTAL = args.seqs
+    # rank 0 prints exactly one JSON line on stdout: keep NCCL's version
+    # banner (printed to stdout at NCCL_DEBUG=VERSION) out of it
+    if os.environ.get("NCCL_DEBUG", "").upper() in ("", "VERSION"):
+        os.environ["NCCL_DEBUG"] = "WARN"
     if args.profile_case:
         return profile_case(args)
     dist = Dist()
