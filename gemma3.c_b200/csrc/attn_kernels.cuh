@@ -147,51 +147,6 @@ __device__ __forceinline__ int cache_row(const LayerDev &L, int pos) {
 }
 
 // ------------------------------------------------------------------------
-// Decode prologue: grid (B, 16); y<8 query head, 8..11 key head, 12..15
-// value head.  q goes to qout [B][8][256] fp32 (already scaled by
-// log2(e)/16 for the exp2 softmax); k and v are appended to the cache.
-// ------------------------------------------------------------------------
-struct DecodeBatch {
-    int B;
-    int seq[kMaxDecodeBatch];
-    int pos[kMaxDecodeBatch];
-};
-
-template <typename KVT>
-__global__ void __launch_bounds__(512) prologue_decode(const float *__restrict__ Q, const float *__restrict__ K,
-                                                       const float *__restrict__ V, LayerDev L, float eps,
-                                                       const __grid_constant__ DecodeBatch batch,
-                                                       float *__restrict__ qout) {
-    const int b = blockIdx.x, y = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int pos = batch.pos[b], seq = batch.seq[b];
-    const float *rope_row = L.rope + (size_t)pos * kHeadDim;
-    HeadRow r;
-    if (y < kHeads) {
-        load_head_row(Q + ((size_t)b * kHeads + y) * kHeadDim, lane, r);
-        norm_rope_row(r, L.qn && L.kn ? L.qn : nullptr, eps, rope_row, lane);
-        float *o = qout + ((size_t)b * kHeads + y) * kHeadDim;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            r.a[j] *= kScaleLog2;
-            r.b[j] *= kScaleLog2;
-        }
-        store4<float>(o + 4 * lane, r.a);
-        store4<float>(o + 128 + 4 * lane, r.b);
-        return;
-    }
-    const int row = cache_row(L, pos);
-    const int sel = y < kHeads + kKvHeads ? 0 : 1;
-    const int h = y - kHeads - sel * kKvHeads;
-    load_head_row((sel ? V : K) + ((size_t)b * kKvHeads + h) * kHeadDim, lane, r);
-    if (!sel) norm_rope_row(r, L.qn && L.kn ? L.kn : nullptr, eps, rope_row, lane);
-    if (row >= 0) {
-        KVT *dst = plane<KVT>(L, seq, sel, h) + (size_t)row * kHeadDim;
-        store4<KVT>(dst + 4 * lane, r.a);
-        store4<KVT>(dst + 128 + 4 * lane, r.b);
-    }
-}
-
-// ------------------------------------------------------------------------
 // Prefill prologue: grid (T, 16).  q -> qst fp16 [8][T][256]; k, v ->
 // cache (cache dtype) and the fp16 linear staging [4][st_rows][256] at row
 // pos - kv_pos0.  The staged k/v value is the cached value (rounded to the
@@ -285,7 +240,13 @@ __global__ void __launch_bounds__(32) stage_prefix(LayerDev L, int seq, int kv_p
 // of the GQA group are scored against every row.
 // ------------------------------------------------------------------------
 struct DecodeParams {
-    const float *q;        // [B][8][256], pre-scaled by log2(e)/16
+    const float *q;        // [B][8][256], pre-scaled by log2(e)/16 (used when qraw is null)
+    const float *qraw;     // raw projections [B][2048] / [B][1024]: when set, the kernel
+    const float *kraw;     //   normalises + rotates its own two q heads and the CTA holding
+    const float *vraw;     //   the new token's cache row appends k/v (fused prologue)
+    float eps;
+    unsigned *tickets;     // [B][4] arrival counters, all zero between calls: when set,
+                           //   the last split of each (seq, kv head) merges the partials
     LayerDev L;
     int chunk;             // rows per split (multiple of the tile)
     int nsplit;
@@ -298,6 +259,7 @@ struct DecodeRows {
     int B;
     int seq[kMaxDecodeBatch];
     int nrows[kMaxDecodeBatch];  // rows attended in this context's planes
+    int pos[kMaxDecodeBatch];    // position of the new token (fused prologue only)
 };
 
 template <typename KVT>
@@ -354,7 +316,9 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
     KVT *vbuf = reinterpret_cast<KVT *>(smem + NS * kPlaneTile);
     __shared__ uint64_t full[NS], empty[NS];
     __shared__ float wm[8][2], wl[8][2];
-    __shared__ int s_abort;
+    __shared__ int s_abort, s_last;
+    __shared__ __align__(16) float qsm[2][kHeadDim];
+    __shared__ __align__(16) KVT newkv[2][kHeadDim];
 
     const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -388,10 +352,45 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
     if (threadIdx.x == 0)
         for (int i = 0; i < NS && i < ntiles; ++i) issue(i);
 
+    // Fused prologue (gemma3_transformer.c:294-316): while the first tiles
+    // are in flight, warps 0-1 normalise + rotate the two query heads of the
+    // group, and in the CTA whose key range holds the new token's cache row,
+    // warps 2-3 build that k/v row, append it to the cache and keep it in
+    // shared memory: the bulk-copied copy of that row may be stale.
+    const int slot = p.qraw ? cache_row(p.L, rows.pos[b]) : -1;
+    const bool owner = slot >= r0 && slot < r1;
+    if (p.qraw) {
+        const float *rope_row = p.L.rope + (size_t)rows.pos[b] * kHeadDim;
+        const uint16_t *qn = p.L.qn && p.L.kn ? p.L.qn : nullptr;
+        const uint16_t *kn = p.L.qn && p.L.kn ? p.L.kn : nullptr;
+        HeadRow r;
+        if (warp < 2) {
+            load_head_row(p.qraw + ((size_t)b * kHeads + 2 * g + warp) * kHeadDim, lane, r);
+            norm_rope_row(r, qn, p.eps, rope_row, lane);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                r.a[j] *= kScaleLog2;
+                r.b[j] *= kScaleLog2;
+            }
+            store4<float>(&qsm[warp][4 * lane], r.a);
+            store4<float>(&qsm[warp][128 + 4 * lane], r.b);
+        } else if (warp < 4 && owner) {
+            const int sel = warp - 2;
+            load_head_row((sel ? p.vraw : p.kraw) + ((size_t)b * kKvHeads + g) * kHeadDim, lane, r);
+            if (!sel) norm_rope_row(r, kn, p.eps, rope_row, lane);
+            KVT *dst = plane<KVT>(p.L, seq, sel, g) + (size_t)slot * kHeadDim;
+            store4<KVT>(dst + 4 * lane, r.a);
+            store4<KVT>(dst + 128 + 4 * lane, r.b);
+            store4<KVT>(&newkv[sel][4 * lane], r.a);
+            store4<KVT>(&newkv[sel][128 + 4 * lane], r.b);
+        }
+        __syncthreads();
+    }
+
     // Query rows of the two heads sharing kv head g, the lane's 8 dims.
     float q0[8], q1[8];
     {
-        const float *qa = p.q + ((size_t)b * kHeads + 2 * g) * kHeadDim;
+        const float *qa = p.qraw ? &qsm[0][0] : p.q + ((size_t)b * kHeads + 2 * g) * kHeadDim;
         const float *qb = qa + kHeadDim;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -420,7 +419,8 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
             const int row = warp + 8 * r;
             float k[8];
             if (row < nr) {
-                load_row8<KVT>(kt + (size_t)row * kHeadDim, lane, k);
+                const bool fresh = owner && (r0 + i * TK + row == slot);
+                load_row8<KVT>(fresh ? &newkv[0][0] : kt + (size_t)row * kHeadDim, lane, k);
             } else {
 #pragma unroll
                 for (int j = 0; j < 8; ++j) k[j] = 0.f;
@@ -471,7 +471,8 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
                 l0 += p0;
                 l1 += p1;
                 float v[8];
-                load_row8<KVT>(vt + (size_t)row * kHeadDim, lane, v);
+                const bool fresh = owner && (r0 + i * TK + row == slot);
+                load_row8<KVT>(fresh ? &newkv[1][0] : vt + (size_t)row * kHeadDim, lane, v);
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
                     o0[j] = fmaf(p0, v[j], o0[j]);
@@ -536,6 +537,35 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
         }
         dst[2 + d] = A;
         dst[3 + d] = Bv;
+        if (p.tickets) {
+            // Split-K style completion: the last split of this (seq, kv head)
+            // to finish merges all partials; no CTA ever waits for another.
+            __threadfence();
+            __syncthreads();
+            if (threadIdx.x == 0) s_last = atomicAdd(&p.tickets[b * kKvHeads + g], 1u) == (unsigned)(p.nsplit - 1);
+            __syncthreads();
+            if (!s_last) return;
+            __threadfence();
+            const float *base = p.partial + ((size_t)b * kHeads + h) * p.nsplit * (kHeadDim + 2);
+            float Mx = -INFINITY;
+            for (int i = 0; i < p.nsplit; ++i) Mx = fmaxf(Mx, __ldcg(base + (size_t)i * (kHeadDim + 2)));
+            float Lt = 0.f, At = 0.f, Bt = 0.f;
+            if (Mx != -INFINITY) {
+                for (int i = 0; i < p.nsplit; ++i) {
+                    const float *pp = base + (size_t)i * (kHeadDim + 2);
+                    const float mi = __ldcg(pp);
+                    if (mi == -INFINITY) continue;
+                    const float f = ex2_approx(mi - Mx);
+                    Lt += __ldcg(pp + 1) * f;
+                    At += __ldcg(pp + 2 + d) * f;
+                    Bt += __ldcg(pp + 3 + d) * f;
+                }
+            }
+            const float inv = Lt > 0.f ? 1.0f / Lt : 0.f;
+            *reinterpret_cast<float2 *>(p.out + (size_t)b * kHeads * kHeadDim + h * kHeadDim + d) =
+                make_float2(At * inv, Bt * inv);
+            if (threadIdx.x == 0) p.tickets[b * kKvHeads + g] = 0u;
+        }
     } else {
         const float inv = Ls > 0.f ? 1.0f / Ls : 0.f;
         float2 *dst = reinterpret_cast<float2 *>(p.out + (size_t)b * kHeads * kHeadDim + h * kHeadDim + d);

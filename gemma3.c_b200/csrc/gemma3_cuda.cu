@@ -137,7 +137,7 @@ struct gemma3_cuda_ctx {
     __half *kst = nullptr, *vst = nullptr;  // [4][st_rows][256] fp16
     int st_rows = 0;
     // decode scratch
-    float *qdec = nullptr;     // [max_batch][8][256]
+    unsigned *tickets = nullptr;  // [max_batch][4] split arrival counters (zero between calls)
     float *partial = nullptr;  // [max_batch][8][kMaxSplit][258]
     float *emit = nullptr;     // [max_batch][8][258]
     float *gather = nullptr;   // [kv_ranks][max_batch][8][258]
@@ -210,7 +210,7 @@ static void ctx_release(gemma3_cuda_ctx *c) {
     cudaFree(c->qst);
     cudaFree(c->kst);
     cudaFree(c->vst);
-    cudaFree(c->qdec);
+    cudaFree(c->tickets);
     cudaFree(c->partial);
     cudaFree(c->emit);
     cudaFree(c->gather);
@@ -247,7 +247,8 @@ static int ctx_alloc(gemma3_cuda_ctx *c) {
         CU_TRY(cudaMalloc(&L.kn, kHeadDim * 2));
     }
     CU_TRY(cudaMalloc(&c->qst, (size_t)kHeads * k.max_prefill * kHeadDim * 2));
-    CU_TRY(cudaMalloc(&c->qdec, (size_t)k.max_batch * kHeads * kHeadDim * 4));
+    CU_TRY(cudaMalloc(&c->tickets, (size_t)k.max_batch * kKvHeads * sizeof(unsigned)));
+    CU_TRY(cudaMemsetAsync(c->tickets, 0, (size_t)k.max_batch * kKvHeads * sizeof(unsigned), c->stream));
     CU_TRY(cudaMalloc(&c->partial, (size_t)k.max_batch * kHeads * kMaxSplit * kPartialStride * 4));
     CU_TRY(cudaMalloc(&c->emit, (size_t)k.max_batch * kHeads * kPartialStride * 4));
     CU_TRY(cudaMalloc(&c->gather, (size_t)k.kv_ranks * k.max_batch * kHeads * kPartialStride * 4));
@@ -307,6 +308,8 @@ extern "C" int gemma3_cuda_synchronize(gemma3_cuda_ctx *ctx) {
     unsigned e = 0;
     CU_TRY(cudaMemcpy(&e, ctx->err, sizeof e, cudaMemcpyDeviceToHost));
     if (e) {
+        // an aborted launch may leave split tickets counted: start clean
+        cudaMemsetAsync(ctx->tickets, 0, (size_t)ctx->cfg.max_batch * kKvHeads * sizeof(unsigned), ctx->stream);
         cudaMemsetAsync(ctx->err, 0, sizeof(unsigned), ctx->stream);
         cudaStreamSynchronize(ctx->stream);
         return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "device status 0x%x (%s)", e,
@@ -487,7 +490,6 @@ extern "C" int gemma3_cuda_attn_prefill(gemma3_cuda_ctx *ctx, int layer, int seq
 
 // ------------------------------------------------------------------ decode
 struct DecodePlan {
-    g3::DecodeBatch batch;
     g3::DecodeRows rows;
     int chunk = 0, nsplit = 0;
 };
@@ -514,12 +516,12 @@ template <typename KVT>
 static void plan_decode(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_ids, const int *pos, DecodePlan &pl) {
     const LayerState &L = ctx->layers[layer];
     constexpr int TK = g3::DecodeCfg<KVT>::TK;
-    pl.batch.B = pl.rows.B = B;
+    pl.rows.B = B;
     long long total = 0;
     int maxrows = 0;
     for (int b = 0; b < B; ++b) {
-        pl.batch.seq[b] = pl.rows.seq[b] = seq_ids[b];
-        pl.batch.pos[b] = pos[b];
+        pl.rows.seq[b] = seq_ids[b];
+        pl.rows.pos[b] = pos[b];
         int n;
         if (L.is_global) {
             n = std::min(pos[b] + 1, ctx->shard_hi) - ctx->shard_lo;
@@ -541,20 +543,23 @@ static void plan_decode(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_i
     pl.nsplit = std::max(1, (int)((maxrows + chunk - 1) / chunk));
 }
 
-// Runs the prologue and the split-KV kernel.  mode 0: final output into out
-// (merging splits if needed); mode 1: one merged (m, l, O) partial per
-// (seq, head) into `partial_out` [B][8][258].
+// Runs the split-KV kernel (with the q/k/v prologue fused in).  partial_out
+// null: final output into out, the last split of each (seq, kv head)
+// merging the partials in the same launch; otherwise one merged (m, l, O)
+// partial per (seq, head) into `partial_out` [B][8][258] via merge_partials.
 template <typename KVT>
 static int decode_impl(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_ids, const int *pos, const float *Q,
                        const float *K, const float *V, float *out, float *partial_out) {
     DecodePlan pl;
     plan_decode<KVT>(ctx, layer, B, seq_ids, pos, pl);
     g3::LayerDev L = layer_dev(ctx, layer);
-    g3::prologue_decode<KVT><<<B, 512, 0, ctx->stream>>>(Q, K, V, L, ctx->cfg.rmsnorm_eps, pl.batch,
-                                                                    ctx->qdec);
-    if (int r = check_launch(ctx, 1)) return r;
     g3::DecodeParams p;
-    p.q = ctx->qdec;
+    p.q = nullptr;
+    p.qraw = Q;
+    p.kraw = K;
+    p.vraw = V;
+    p.eps = ctx->cfg.rmsnorm_eps;
+    p.tickets = partial_out ? nullptr : ctx->tickets;
     p.L = L;
     p.chunk = pl.chunk;
     p.nsplit = pl.nsplit;
@@ -573,7 +578,7 @@ static int decode_impl(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_id
         prof_end(ctx, 0, e0, rows * kKvHeads * 2.0 * kHeadDim * sizeof(KVT));
     }
     if (int r = check_launch(ctx, 1)) return r;
-    if (p.write_partial) {
+    if (partial_out) {
         const size_t hs = (size_t)pl.nsplit * kPartialStride;
         g3::merge_partials<<<B * kHeads, 256, 0, ctx->stream>>>(ctx->partial, pl.nsplit, kHeads * hs, hs,
                                                                  kPartialStride, out, partial_out);
@@ -881,9 +886,13 @@ extern "C" int gemma3_cuda_gqa_decode_noalloc(const float *q, const void *kv, in
     for (int b = 0; b < B; ++b) {
         rws.seq[b] = b;
         rws.nrows[b] = nrows[b];
+        rws.pos[b] = 0;
     }
     g3::DecodeParams p;
     p.q = qs;
+    p.qraw = p.kraw = p.vraw = nullptr;
+    p.eps = 0.f;
+    p.tickets = nullptr;
     p.L.kv = const_cast<void *>(kv);
     p.L.rows = rows;
     p.L.is_global = 1;
