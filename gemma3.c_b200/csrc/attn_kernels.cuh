@@ -35,6 +35,7 @@ constexpr int kKvHeads = 4;
 constexpr int kHeadDim = 256;
 constexpr int kWindow = 1024;
 constexpr int kMaxDecodeBatch = 256;
+constexpr int kMaxSplitFused = 128;  // splits the in-kernel merge can hold (host caps nsplit at this)
 // softmax(x/16) evaluated as 2^(x * log2(e)/16)
 constexpr float kScaleLog2 = 0.0901684400555602f;
 
@@ -357,7 +358,7 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
     // group, and in the CTA whose key range holds the new token's cache row,
     // warps 2-3 build that k/v row, append it to the cache and keep it in
     // shared memory: the bulk-copied copy of that row may be stale.
-    const int slot = p.qraw ? cache_row(p.L, rows.pos[b]) : -1;
+    const int slot = p.qraw ? cache_row(p.L, rows.pos[b]) : -1;  // cache row of the new token
     const bool owner = slot >= r0 && slot < r1;
     if (p.qraw) {
         const float *rope_row = p.L.rope + (size_t)rows.pos[b] * kHeadDim;
@@ -546,19 +547,30 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
             __syncthreads();
             if (!s_last) return;
             __threadfence();
-            const float *base = p.partial + ((size_t)b * kHeads + h) * p.nsplit * (kHeadDim + 2);
+            // (m, l) of every split and head in one parallel round of loads,
+            // then the O sums with eight independent loads in flight.
+            float *sm_m = reinterpret_cast<float *>(smem);          // [2][nsplit]
+            float *sm_l = sm_m + 2 * kMaxSplitFused;                 // [2][nsplit]
+            for (int t = threadIdx.x; t < 2 * p.nsplit; t += 256) {
+                const int th = t / p.nsplit, ts = t % p.nsplit;
+                const float *pp = p.partial + (((size_t)b * kHeads + 2 * g + th) * p.nsplit + ts) * (kHeadDim + 2);
+                sm_m[th * kMaxSplitFused + ts] = __ldcg(pp);
+                sm_l[th * kMaxSplitFused + ts] = __ldcg(pp + 1);
+            }
+            __syncthreads();
+            const float *mh = sm_m + hh * kMaxSplitFused, *lh = sm_l + hh * kMaxSplitFused;
             float Mx = -INFINITY;
-            for (int i = 0; i < p.nsplit; ++i) Mx = fmaxf(Mx, __ldcg(base + (size_t)i * (kHeadDim + 2)));
+            for (int i = 0; i < p.nsplit; ++i) Mx = fmaxf(Mx, mh[i]);
+            const float *base = p.partial + ((size_t)b * kHeads + h) * p.nsplit * (kHeadDim + 2);
             float Lt = 0.f, At = 0.f, Bt = 0.f;
             if (Mx != -INFINITY) {
+#pragma unroll 8
                 for (int i = 0; i < p.nsplit; ++i) {
-                    const float *pp = base + (size_t)i * (kHeadDim + 2);
-                    const float mi = __ldcg(pp);
-                    if (mi == -INFINITY) continue;
-                    const float f = ex2_approx(mi - Mx);
-                    Lt += __ldcg(pp + 1) * f;
-                    At += __ldcg(pp + 2 + d) * f;
-                    Bt += __ldcg(pp + 3 + d) * f;
+                    const float f = mh[i] == -INFINITY ? 0.f : ex2_approx(mh[i] - Mx);
+                    const float2 o = __ldcg(reinterpret_cast<const float2 *>(base + (size_t)i * (kHeadDim + 2) + 2 + d));
+                    Lt += lh[i] * f;
+                    At += o.x * f;
+                    Bt += o.y * f;
                 }
             }
             const float inv = Lt > 0.f ? 1.0f / Lt : 0.f;
