@@ -533,10 +533,15 @@ static void plan_decode(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_i
         total += (long long)n * kKvHeads;
         maxrows = std::max(maxrows, n);
     }
-    // Aim for ~8 CTAs per SM over the call (2 resident x 4 waves) and at
+    // Aim for ~8 CTAs per SM over the call (2 resident x 4 waves), but give
+    // every CTA at least 512 rows when there is work for a full wave of
+    // those (each CTA pays a fixed start -- barrier set-up, its q prologue,
+    // the first copies' latency -- that short CTAs cannot amortise); at
     // least 4 tiles per CTA; never more than kMaxSplit splits.
     const long long target = 148LL * 8;
+    const long long one_wave = 148LL * 2;
     long long chunk = std::max<long long>(4 * TK, (total + target - 1) / target);
+    chunk = std::max<long long>(chunk, std::min<long long>(512, (total + one_wave - 1) / one_wave));
     chunk = std::max<long long>(chunk, (maxrows + kMaxSplit - 1) / kMaxSplit);
     chunk = (chunk + TK - 1) / TK * TK;
     pl.chunk = (int)chunk;
