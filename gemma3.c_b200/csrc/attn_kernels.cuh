@@ -412,16 +412,26 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
         }
         if (s_abort) break;
         const int nr = min(TK, r1 - (r0 + i * TK));
-        const KVT *kt = kbuf + (size_t)s * TK * kHeadDim;
-        const KVT *vt = vbuf + (size_t)s * TK * kHeadDim;
+        KVT *kt = kbuf + (size_t)s * TK * kHeadDim;
+        KVT *vt = vbuf + (size_t)s * TK * kHeadDim;
+        // The copied row of the new token may predate its append: the one
+        // warp that reads that row overwrites it with the fresh k/v first.
+        if (owner && (slot - r0) / TK == i && warp == ((slot - r0) % TK) % 8) {
+            const int rr = (slot - r0) % TK;
+            constexpr int kVec = kHeadDim * sizeof(KVT) / 16;  // 16-byte pieces per row
+            for (int c = lane; c < kVec; c += 32) {
+                reinterpret_cast<uint4 *>(kt + (size_t)rr * kHeadDim)[c] = reinterpret_cast<const uint4 *>(&newkv[0][0])[c];
+                reinterpret_cast<uint4 *>(vt + (size_t)rr * kHeadDim)[c] = reinterpret_cast<const uint4 *>(&newkv[1][0])[c];
+            }
+            __syncwarp();
+        }
         float sc0[RW], sc1[RW];
 #pragma unroll
         for (int r = 0; r < RW; ++r) {
             const int row = warp + 8 * r;
             float k[8];
             if (row < nr) {
-                const bool fresh = owner && (r0 + i * TK + row == slot);
-                load_row8<KVT>(fresh ? &newkv[0][0] : kt + (size_t)row * kHeadDim, lane, k);
+                load_row8<KVT>(kt + (size_t)row * kHeadDim, lane, k);
             } else {
 #pragma unroll
                 for (int j = 0; j < 8; ++j) k[j] = 0.f;
@@ -472,8 +482,7 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
                 l0 += p0;
                 l1 += p1;
                 float v[8];
-                const bool fresh = owner && (r0 + i * TK + row == slot);
-                load_row8<KVT>(fresh ? &newkv[1][0] : vt + (size_t)row * kHeadDim, lane, v);
+                load_row8<KVT>(vt + (size_t)row * kHeadDim, lane, v);
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {
                     o0[j] = fmaf(p0, v[j], o0[j]);
