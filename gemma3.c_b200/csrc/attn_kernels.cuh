@@ -260,8 +260,48 @@ struct DecodeRows {
     int B;
     int seq[kMaxDecodeBatch];
     int nrows[kMaxDecodeBatch];  // rows attended in this context's planes
-    int pos[kMaxDecodeBatch];    // position of the new token (fused prologue only)
+    int pos[kMaxDecodeBatch];    // position of the new token
 };
+
+// Decode prologue as its own kernel, for calls whose CTAs stream long key
+// ranges: grid (B), block 512 = 16 warps, warp y < 8 query head y, 8..11 key
+// head, 12..15 value head.  q goes to qout [B][8][256] fp32 (scaled by
+// log2(e)/16); k and v are appended to the cache.  Short-range calls fold
+// this work into decode_splitkv instead (see DecodeParams::qraw).
+template <typename KVT>
+__global__ void __launch_bounds__(512) prologue_decode(const float *__restrict__ Q, const float *__restrict__ K,
+                                                       const float *__restrict__ V, LayerDev L, float eps,
+                                                       const __grid_constant__ DecodeRows rows,
+                                                       float *__restrict__ qout) {
+    const int b = blockIdx.x, y = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int pos = rows.pos[b], seq = rows.seq[b];
+    const float *rope_row = L.rope + (size_t)pos * kHeadDim;
+    HeadRow r;
+    if (y < kHeads) {
+        load_head_row(Q + ((size_t)b * kHeads + y) * kHeadDim, lane, r);
+        norm_rope_row(r, L.qn && L.kn ? L.qn : nullptr, eps, rope_row, lane);
+        float *o = qout + ((size_t)b * kHeads + y) * kHeadDim;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            r.a[j] *= kScaleLog2;
+            r.b[j] *= kScaleLog2;
+        }
+        store4<float>(o + 4 * lane, r.a);
+        store4<float>(o + 128 + 4 * lane, r.b);
+        return;
+    }
+    const int row = cache_row(L, pos);
+    const int sel = y < kHeads + kKvHeads ? 0 : 1;
+    const int h = y - kHeads - sel * kKvHeads;
+    load_head_row((sel ? V : K) + ((size_t)b * kKvHeads + h) * kHeadDim, lane, r);
+    if (!sel) norm_rope_row(r, L.qn && L.kn ? L.kn : nullptr, eps, rope_row, lane);
+    if (row >= 0) {
+        KVT *dst = plane<KVT>(L, seq, sel, h) + (size_t)row * kHeadDim;
+        store4<KVT>(dst + 4 * lane, r.a);
+        store4<KVT>(dst + 128 + 4 * lane, r.b);
+    }
+}
+
 
 template <typename KVT>
 struct DecodeCfg;
