@@ -305,6 +305,10 @@ __global__ void __launch_bounds__(512) prologue_decode(const float *__restrict__
 
 template <typename KVT>
 struct DecodeCfg;
+// extra dynamic shared memory of a fused-prologue launch: q (2 heads, fp32)
+// + the new token's k and v rows (cache dtype)
+template <typename KVT>
+constexpr int kFusedExtra = 2 * kHeadDim * sizeof(float) + 2 * kHeadDim * sizeof(KVT);
 template <>
 struct DecodeCfg<__nv_bfloat16> {
     static constexpr int TK = 32;  // rows per tile (16 KB per plane)
@@ -358,8 +362,11 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
     __shared__ uint64_t full[NS], empty[NS];
     __shared__ float wm[8][2], wl[8][2];
     __shared__ int s_abort, s_last;
-    __shared__ __align__(16) float qsm[2][kHeadDim];
-    __shared__ __align__(16) KVT newkv[2][kHeadDim];
+    // q and fresh-row buffers of the fused prologue live after the ring in
+    // dynamic shared memory, requested only by fused launches, so that the
+    // long-range launches keep the smaller footprint (and larger L1 carve-out).
+    float(*qsm)[kHeadDim] = reinterpret_cast<float(*)[kHeadDim]>(smem + 2 * NS * kPlaneTile);
+    KVT(*newkv)[kHeadDim] = reinterpret_cast<KVT(*)[kHeadDim]>(smem + 2 * NS * kPlaneTile + 2 * kHeadDim * sizeof(float));
 
     const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;

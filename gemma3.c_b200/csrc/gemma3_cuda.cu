@@ -262,8 +262,10 @@ static int ctx_alloc(gemma3_cuda_ctx *c) {
     CU_TRY(cudaFuncSetAttribute(g3::prefill_fa_sm100, cudaFuncAttributeMaxDynamicSharedMemorySize, g3::kPfSmem));
     const int dsm_bf = g3::DecodeCfg<__nv_bfloat16>::NS * 2 * g3::DecodeCfg<__nv_bfloat16>::TK * kHeadDim * 2;
     const int dsm_f = g3::DecodeCfg<float>::NS * 2 * g3::DecodeCfg<float>::TK * kHeadDim * 4;
-    CU_TRY(cudaFuncSetAttribute(g3::decode_splitkv<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, dsm_bf));
-    CU_TRY(cudaFuncSetAttribute(g3::decode_splitkv<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, dsm_f));
+    CU_TRY(cudaFuncSetAttribute(g3::decode_splitkv<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                dsm_bf + g3::kFusedExtra<__nv_bfloat16>));
+    CU_TRY(cudaFuncSetAttribute(g3::decode_splitkv<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                dsm_f + g3::kFusedExtra<float>));
     if (int r = load_encode()) return r;
     CU_TRY(cudaStreamSynchronize(c->stream));
     return 0;
@@ -588,7 +590,8 @@ static int decode_impl(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_id
     p.out = out;
     p.write_partial = (pl.nsplit > 1 || partial_out) ? 1 : 0;
     p.err = ctx->err;
-    constexpr int smem = g3::DecodeCfg<KVT>::NS * 2 * g3::DecodeCfg<KVT>::TK * kHeadDim * sizeof(KVT);
+    const int smem = g3::DecodeCfg<KVT>::NS * 2 * g3::DecodeCfg<KVT>::TK * kHeadDim * sizeof(KVT) +
+                     (fused ? g3::kFusedExtra<KVT> : 0);
     size_t e0;
     prof_begin(ctx, &e0);
     g3::decode_splitkv<KVT><<<dim3(pl.nsplit, kKvHeads, B), 256, smem, ctx->stream>>>(p, pl.rows);
