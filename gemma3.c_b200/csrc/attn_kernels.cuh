@@ -362,11 +362,6 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
     __shared__ uint64_t full[NS], empty[NS];
     __shared__ float wm[8][2], wl[8][2];
     __shared__ int s_abort, s_last;
-    // q and fresh-row buffers of the fused prologue live after the ring in
-    // dynamic shared memory, requested only by fused launches, so that the
-    // long-range launches keep the smaller footprint (and larger L1 carve-out).
-    float(*qsm)[kHeadDim] = reinterpret_cast<float(*)[kHeadDim]>(smem + 2 * NS * kPlaneTile);
-    KVT(*newkv)[kHeadDim] = reinterpret_cast<KVT(*)[kHeadDim]>(smem + 2 * NS * kPlaneTile + 2 * kHeadDim * sizeof(float));
 
     const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -389,15 +384,50 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
     }
     __syncthreads();
 
+    // q and fresh-row buffers of the fused prologue live after the ring.
+    float(*qsm)[kHeadDim] = reinterpret_cast<float(*)[kHeadDim]>(smem + 2 * NS * kPlaneTile);
+    KVT(*newkv)[kHeadDim] = reinterpret_cast<KVT(*)[kHeadDim]>(smem + 2 * NS * kPlaneTile + 2 * kHeadDim * sizeof(float));
+    const int slot = p.qraw ? cache_row(p.L, rows.pos[b]) : -1;  // cache row of the new token
+    const bool owner = slot >= r0 && slot < r1;
+
+    // Thread 0 fills the ring.  In the fused form the new token's row may
+    // not be in global memory yet when its tile is copied, so that tile is
+    // copied around the row and thread 0 writes the fresh row (built by the
+    // prologue below) into shared memory itself before arming the barrier.
     auto issue = [&](int i) {
         const int s = i % NS;
-        const int nr = min(TK, r1 - (r0 + i * TK));
-        const uint32_t bytes = (uint32_t)nr * kHeadDim * sizeof(KVT);
-        mbar_expect_tx(&full[s], 2 * bytes);
-        bulk_g2s(kbuf + (size_t)s * TK * kHeadDim, Kp + (size_t)i * TK * kHeadDim, bytes, &full[s]);
-        bulk_g2s(vbuf + (size_t)s * TK * kHeadDim, Vp + (size_t)i * TK * kHeadDim, bytes, &full[s]);
+        const int base = r0 + i * TK;
+        const int nr = min(TK, r1 - base);
+        const uint32_t row_b = kHeadDim * sizeof(KVT);
+        KVT *ks = kbuf + (size_t)s * TK * kHeadDim, *vs = vbuf + (size_t)s * TK * kHeadDim;
+        const KVT *kg = Kp + (size_t)i * TK * kHeadDim, *vg = Vp + (size_t)i * TK * kHeadDim;
+        if (owner && slot >= base && slot < base + nr) {
+            const int rr = slot - base, after = nr - rr - 1;
+            constexpr int kVec = kHeadDim * sizeof(KVT) / 16;
+            for (int c = 0; c < kVec; ++c) {
+                reinterpret_cast<uint4 *>(ks + (size_t)rr * kHeadDim)[c] = reinterpret_cast<const uint4 *>(newkv[0])[c];
+                reinterpret_cast<uint4 *>(vs + (size_t)rr * kHeadDim)[c] = reinterpret_cast<const uint4 *>(newkv[1])[c];
+            }
+            // order these generic writes before later bulk copies into the same slot
+            fence_proxy_async_smem();
+            mbar_expect_tx(&full[s], 2 * (uint32_t)(nr - 1) * row_b);
+            if (rr > 0) {
+                bulk_g2s(ks, kg, rr * row_b, &full[s]);
+                bulk_g2s(vs, vg, rr * row_b, &full[s]);
+            }
+            if (after > 0) {
+                bulk_g2s(ks + (size_t)(rr + 1) * kHeadDim, kg + (size_t)(rr + 1) * kHeadDim, after * row_b, &full[s]);
+                bulk_g2s(vs + (size_t)(rr + 1) * kHeadDim, vg + (size_t)(rr + 1) * kHeadDim, after * row_b, &full[s]);
+            }
+            return;
+        }
+        mbar_expect_tx(&full[s], 2 * (uint32_t)nr * row_b);
+        bulk_g2s(ks, kg, nr * row_b, &full[s]);
+        bulk_g2s(vs, vg, nr * row_b, &full[s]);
     };
-    if (threadIdx.x == 0)
+    // The owner CTA (one per sequence and kv head) starts copying after its
+    // prologue has built the fresh row; every other CTA right away.
+    if (threadIdx.x == 0 && !owner)
         for (int i = 0; i < NS && i < ntiles; ++i) issue(i);
 
     // Fused prologue (gemma3_transformer.c:294-316): while the first tiles
@@ -405,8 +435,6 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
     // group, and in the CTA whose key range holds the new token's cache row,
     // warps 2-3 build that k/v row, append it to the cache and keep it in
     // shared memory: the bulk-copied copy of that row may be stale.
-    const int slot = p.qraw ? cache_row(p.L, rows.pos[b]) : -1;  // cache row of the new token
-    const bool owner = slot >= r0 && slot < r1;
     if (p.qraw) {
         const float *rope_row = p.L.rope + (size_t)rows.pos[b] * kHeadDim;
         const uint16_t *qn = p.L.qn && p.L.kn ? p.L.qn : nullptr;
@@ -433,6 +461,8 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
             store4<KVT>(&newkv[sel][128 + 4 * lane], r.b);
         }
         __syncthreads();
+        if (threadIdx.x == 0 && owner)
+            for (int i = 0; i < NS && i < ntiles; ++i) issue(i);
     }
 
     // Query rows of the two heads sharing kv head g, the lane's 8 dims.
@@ -459,19 +489,8 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
         }
         if (s_abort) break;
         const int nr = min(TK, r1 - (r0 + i * TK));
-        KVT *kt = kbuf + (size_t)s * TK * kHeadDim;
-        KVT *vt = vbuf + (size_t)s * TK * kHeadDim;
-        // The copied row of the new token may predate its append: the one
-        // warp that reads that row overwrites it with the fresh k/v first.
-        if (owner && (slot - r0) / TK == i && warp == ((slot - r0) % TK) % 8) {
-            const int rr = (slot - r0) % TK;
-            constexpr int kVec = kHeadDim * sizeof(KVT) / 16;  // 16-byte pieces per row
-            for (int c = lane; c < kVec; c += 32) {
-                reinterpret_cast<uint4 *>(kt + (size_t)rr * kHeadDim)[c] = reinterpret_cast<const uint4 *>(&newkv[0][0])[c];
-                reinterpret_cast<uint4 *>(vt + (size_t)rr * kHeadDim)[c] = reinterpret_cast<const uint4 *>(&newkv[1][0])[c];
-            }
-            __syncwarp();
-        }
+        const KVT *kt = kbuf + (size_t)s * TK * kHeadDim;
+        const KVT *vt = vbuf + (size_t)s * TK * kHeadDim;
         float sc0[RW], sc1[RW];
 #pragma unroll
         for (int r = 0; r < RW; ++r) {

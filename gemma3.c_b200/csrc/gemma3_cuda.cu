@@ -881,8 +881,11 @@ extern "C" int gemma3_cuda_gqa_decode_noalloc(const float *q, const void *kv, in
             // array's device address; the host-side symbol is not it.
             void *p = nullptr;
             CU_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
-            const int smem_bf = g3::DecodeCfg<__nv_bfloat16>::NS * 2 * g3::DecodeCfg<__nv_bfloat16>::TK * kHeadDim * 2;
-            const int smem_f = g3::DecodeCfg<float>::NS * 2 * g3::DecodeCfg<float>::TK * kHeadDim * 4;
+            // same limits the context path sets (the attribute is per function)
+            const int smem_bf = g3::DecodeCfg<__nv_bfloat16>::NS * 2 * g3::DecodeCfg<__nv_bfloat16>::TK * kHeadDim * 2 +
+                                g3::kFusedExtra<__nv_bfloat16>;
+            const int smem_f = g3::DecodeCfg<float>::NS * 2 * g3::DecodeCfg<float>::TK * kHeadDim * 4 +
+                               g3::kFusedExtra<float>;
             CU_TRY(cudaFuncSetAttribute(g3::decode_splitkv<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         smem_bf));
             CU_TRY(cudaFuncSetAttribute(g3::decode_splitkv<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_f));
