@@ -578,11 +578,10 @@ static int decode_impl(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_id
     p.kraw = K;
     p.vraw = V;
     p.eps = ctx->cfg.rmsnorm_eps;
-#ifdef G3_DEV_NO_TICKETS
-    p.tickets = nullptr;
-#else
-    p.tickets = partial_out ? nullptr : ctx->tickets;
-#endif
+    // In-kernel merge (last split merges) for the short fused calls, where a
+    // second launch is a large share of the call; long calls keep the
+    // separate merge kernel, which measured faster on them.
+    p.tickets = (partial_out || !fused) ? nullptr : ctx->tickets;
     p.L = L;
     p.chunk = pl.chunk;
     p.nsplit = pl.nsplit;
@@ -602,11 +601,7 @@ static int decode_impl(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_id
         prof_end(ctx, 0, e0, rows * kKvHeads * 2.0 * kHeadDim * sizeof(KVT));
     }
     if (int r = check_launch(ctx, 1)) return r;
-#ifdef G3_DEV_NO_TICKETS
-    if (p.write_partial) {
-#else
-    if (partial_out) {
-#endif
+    if (p.write_partial && !p.tickets) {
         const size_t hs = (size_t)pl.nsplit * kPartialStride;
         g3::merge_partials<<<B * kHeads, 256, 0, ctx->stream>>>(ctx->partial, pl.nsplit, kHeads * hs, hs,
                                                                  kPartialStride, out, partial_out);
