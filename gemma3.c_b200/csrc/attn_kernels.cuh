@@ -350,7 +350,11 @@ __device__ __forceinline__ void load_row8<float>(const float *row, int lane, flo
     x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
 }
 
-template <typename KVT>
+// kFused: the form for short key ranges, with the q/k/v prologue folded in
+// (DecodeParams::qraw) and the in-kernel merge (DecodeParams::tickets); the
+// plain form is compiled without that code, which measurably slows the long
+// streaming loop even when it is not executed.
+template <typename KVT, bool kFused>
 __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, const __grid_constant__ DecodeRows rows) {
     constexpr int TK = DecodeCfg<KVT>::TK;
     constexpr int NS = DecodeCfg<KVT>::NS;
@@ -387,7 +391,7 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
     // q and fresh-row buffers of the fused prologue live after the ring.
     float(*qsm)[kHeadDim] = reinterpret_cast<float(*)[kHeadDim]>(smem + 2 * NS * kPlaneTile);
     KVT(*newkv)[kHeadDim] = reinterpret_cast<KVT(*)[kHeadDim]>(smem + 2 * NS * kPlaneTile + 2 * kHeadDim * sizeof(float));
-    const int slot = p.qraw ? cache_row(p.L, rows.pos[b]) : -1;  // cache row of the new token
+    const int slot = kFused ? cache_row(p.L, rows.pos[b]) : -1;  // cache row of the new token
     const bool owner = slot >= r0 && slot < r1;
 
     // Thread 0 fills the ring.  In the fused form the new token's row may
@@ -401,7 +405,7 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
         const uint32_t row_b = kHeadDim * sizeof(KVT);
         KVT *ks = kbuf + (size_t)s * TK * kHeadDim, *vs = vbuf + (size_t)s * TK * kHeadDim;
         const KVT *kg = Kp + (size_t)i * TK * kHeadDim, *vg = Vp + (size_t)i * TK * kHeadDim;
-        if (owner && slot >= base && slot < base + nr) {
+        if (kFused && owner && slot >= base && slot < base + nr) {
             const int rr = slot - base, after = nr - rr - 1;
             constexpr int kVec = kHeadDim * sizeof(KVT) / 16;
             for (int c = 0; c < kVec; ++c) {
@@ -427,7 +431,7 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
     };
     // The owner CTA (one per sequence and kv head) starts copying after its
     // prologue has built the fresh row; every other CTA right away.
-    if (threadIdx.x == 0 && !owner)
+    if (threadIdx.x == 0 && !(kFused && owner))
         for (int i = 0; i < NS && i < ntiles; ++i) issue(i);
 
     // Fused prologue (gemma3_transformer.c:294-316): while the first tiles
@@ -435,7 +439,7 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
     // group, and in the CTA whose key range holds the new token's cache row,
     // warps 2-3 build that k/v row, append it to the cache and keep it in
     // shared memory: the bulk-copied copy of that row may be stale.
-    if (p.qraw) {
+    if constexpr (kFused) {
         const float *rope_row = p.L.rope + (size_t)rows.pos[b] * kHeadDim;
         const uint16_t *qn = p.L.qn && p.L.kn ? p.L.qn : nullptr;
         const uint16_t *kn = p.L.qn && p.L.kn ? p.L.kn : nullptr;
@@ -468,7 +472,7 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
     // Query rows of the two heads sharing kv head g, the lane's 8 dims.
     float q0[8], q1[8];
     {
-        const float *qa = p.qraw ? &qsm[0][0] : p.q + ((size_t)b * kHeads + 2 * g) * kHeadDim;
+        const float *qa = kFused ? &qsm[0][0] : p.q + ((size_t)b * kHeads + 2 * g) * kHeadDim;
         const float *qb = qa + kHeadDim;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
@@ -613,7 +617,7 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
         }
         dst[2 + d] = A;
         dst[3 + d] = Bv;
-        if (p.tickets) {
+        if (kFused && p.tickets) {
             // Split-K style completion: the last split of this (seq, kv head)
             // to finish merges all partials; no CTA ever waits for another.
             __threadfence();

@@ -262,10 +262,12 @@ static int ctx_alloc(gemma3_cuda_ctx *c) {
     CU_TRY(cudaFuncSetAttribute(g3::prefill_fa_sm100, cudaFuncAttributeMaxDynamicSharedMemorySize, g3::kPfSmem));
     const int dsm_bf = g3::DecodeCfg<__nv_bfloat16>::NS * 2 * g3::DecodeCfg<__nv_bfloat16>::TK * kHeadDim * 2;
     const int dsm_f = g3::DecodeCfg<float>::NS * 2 * g3::DecodeCfg<float>::TK * kHeadDim * 4;
-    CU_TRY(cudaFuncSetAttribute(g3::decode_splitkv<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    CU_TRY(cudaFuncSetAttribute(g3::decode_splitkv<__nv_bfloat16, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 dsm_bf + g3::kFusedExtra<__nv_bfloat16>));
-    CU_TRY(cudaFuncSetAttribute(g3::decode_splitkv<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    CU_TRY(cudaFuncSetAttribute(g3::decode_splitkv<float, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 dsm_f + g3::kFusedExtra<float>));
+    CU_TRY(cudaFuncSetAttribute(g3::decode_splitkv<__nv_bfloat16, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, dsm_bf));
+    CU_TRY(cudaFuncSetAttribute(g3::decode_splitkv<float, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, dsm_f));
     if (int r = load_encode()) return r;
     CU_TRY(cudaStreamSynchronize(c->stream));
     return 0;
@@ -593,7 +595,10 @@ static int decode_impl(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_id
                      (fused ? g3::kFusedExtra<KVT> : 0);
     size_t e0;
     prof_begin(ctx, &e0);
-    g3::decode_splitkv<KVT><<<dim3(pl.nsplit, kKvHeads, B), 256, smem, ctx->stream>>>(p, pl.rows);
+    if (fused)
+        g3::decode_splitkv<KVT, true><<<dim3(pl.nsplit, kKvHeads, B), 256, smem, ctx->stream>>>(p, pl.rows);
+    else
+        g3::decode_splitkv<KVT, false><<<dim3(pl.nsplit, kKvHeads, B), 256, smem, ctx->stream>>>(p, pl.rows);
     if (ctx->prof) {
         // algorithmic bytes: every attended K and V row once
         double rows = 0;
@@ -876,14 +881,14 @@ extern "C" int gemma3_cuda_gqa_decode_noalloc(const float *q, const void *kv, in
             // array's device address; the host-side symbol is not it.
             void *p = nullptr;
             CU_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
-            // same limits the context path sets (the attribute is per function)
-            const int smem_bf = g3::DecodeCfg<__nv_bfloat16>::NS * 2 * g3::DecodeCfg<__nv_bfloat16>::TK * kHeadDim * 2 +
-                                g3::kFusedExtra<__nv_bfloat16>;
-            const int smem_f = g3::DecodeCfg<float>::NS * 2 * g3::DecodeCfg<float>::TK * kHeadDim * 4 +
-                               g3::kFusedExtra<float>;
-            CU_TRY(cudaFuncSetAttribute(g3::decode_splitkv<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        smem_bf));
-            CU_TRY(cudaFuncSetAttribute(g3::decode_splitkv<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_f));
+            // same limits the context path sets for the plain form (the
+            // attribute is per function)
+            const int smem_bf = g3::DecodeCfg<__nv_bfloat16>::NS * 2 * g3::DecodeCfg<__nv_bfloat16>::TK * kHeadDim * 2;
+            const int smem_f = g3::DecodeCfg<float>::NS * 2 * g3::DecodeCfg<float>::TK * kHeadDim * 4;
+            CU_TRY(cudaFuncSetAttribute(g3::decode_splitkv<__nv_bfloat16, false>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bf));
+            CU_TRY(cudaFuncSetAttribute(g3::decode_splitkv<float, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        smem_f));
             g_noalloc_addr[dev] = static_cast<float *>(p);
         }
         scratch = g_noalloc_addr[dev];
@@ -934,10 +939,10 @@ extern "C" int gemma3_cuda_gqa_decode_noalloc(const float *q, const void *kv, in
     p.err = status;
     if (bf) {
         constexpr int smem = g3::DecodeCfg<__nv_bfloat16>::NS * 2 * g3::DecodeCfg<__nv_bfloat16>::TK * kHeadDim * 2;
-        g3::decode_splitkv<__nv_bfloat16><<<dim3(nsplit, kKvHeads, B), 256, smem, st>>>(p, rws);
+        g3::decode_splitkv<__nv_bfloat16, false><<<dim3(nsplit, kKvHeads, B), 256, smem, st>>>(p, rws);
     } else {
         constexpr int smem = g3::DecodeCfg<float>::NS * 2 * g3::DecodeCfg<float>::TK * kHeadDim * 4;
-        g3::decode_splitkv<float><<<dim3(nsplit, kKvHeads, B), 256, smem, st>>>(p, rws);
+        g3::decode_splitkv<float, false><<<dim3(nsplit, kKvHeads, B), 256, smem, st>>>(p, rws);
     }
     const size_t hs = (size_t)nsplit * kPartialStride;
     g3::merge_partials<<<B * kHeads, 256, 0, st>>>(part, nsplit, kHeads * hs, hs, kPartialStride, out, nullptr);
