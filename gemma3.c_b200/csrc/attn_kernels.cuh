@@ -701,11 +701,14 @@ __global__ void __launch_bounds__(256) merge_partials(const float *__restrict__ 
 }
 
 // ------------------------------------------------------------------------
-// Prefill flash attention on tcgen05 / TMEM.
+// Prefill flash attention on tcgen05 / TMEM (persistent CTAs).
 //
-// CTA = (block of 64 query tokens, kv head g); the MMA M dimension stacks
-// the two query heads of the group (rows 0-63 head 2g, 64-127 head 2g+1),
-// so each K/V tile feeds both.  Per key tile of 64 rows:
+// Work unit = (block of 64 query tokens, kv head g); the MMA M dimension
+// stacks the two query heads of the group (rows 0-63 head 2g, 64-127 head
+// 2g+1), so each K/V tile feeds both.  One CTA per SM walks the units
+// heaviest first (round-robin over the cost-sorted list), so a unit's Q load
+// and first MMAs overlap the previous unit's last tiles and epilogue.
+// Per key tile of 64 rows:
 //     S[128x64]  = Q[128x256] . K^T   16 MMAs (K=16); A = Q resident in TMEM,
 //                                      B = K tile from shared memory
 //     softmax    warps 0-7: row r is shared by threads r (keys 0-31, O cols
@@ -713,12 +716,10 @@ __global__ void __launch_bounds__(256) merge_partials(const float *__restrict__ 
 //                to TMEM as fp16 (two buffers)
 //     O[128x256] += P[128x64] . V     4 MMAs (K=16); A = P from TMEM,
 //                                      B = V tile (MN-major) from shared memory
-// Keeping both A operands in TMEM leaves shared memory bandwidth to the K/V
-// tiles only (with Q in shared memory the narrow N=64 S MMAs were limited by
-// reading the 4 KB Q slice per instruction) and frees the space for a third
-// K/V stage.  Warp 8 issues the TMA loads, warp 9 the S MMAs and warp 10 the
-// PV MMAs (one lane each).
-// Operands are fp16 (see prologue_prefill), accumulation fp32.
+// Warp 8 issues the TMA loads, warp 9 the Q copies into TMEM and the S MMAs,
+// warp 10 the PV MMAs (one lane each): each MMA goes to the tensor pipe as
+// soon as its own operands are ready.  Operands are fp16 (see
+// prologue_prefill), accumulation fp32.
 //
 // TMEM columns (512): Q 0-127 (fp16 pairs), S 128-191 (fp32), P 192-255
 // (2 x 32, fp16 pairs), O 256-511 (fp32).
@@ -729,52 +730,43 @@ __global__ void __launch_bounds__(256) merge_partials(const float *__restrict__ 
 // max exceeds it by more than kRescaleLog2; otherwise P <= 2^kRescaleLog2 =
 // 256, exact in fp16, and the result is mathematically unchanged.
 //
-// Shared memory (1024-aligned, 128-B swizzle everywhere):
-//     K  3 stages x 32 KB: 4 dim-chunks x [64 keys x 128 B]   (K-major B)
-//     V  3 stages x 32 KB: 4 dim-chunks x [64 keys x 128 B]   (MN-major B)
-//     barriers, row-max / row-sum exchange 3 KB
+// Shared memory (1024-aligned, 128-B swizzle for every MMA operand):
+//     Q staging 64 KB: 4 dim-chunks x [128 rows x 128 B]   (TMA -> tcgen05.cp)
+//     K  2 stages x 32 KB: 4 dim-chunks x [64 keys x 128 B]   (K-major B)
+//     V  2 stages x 32 KB: 4 dim-chunks x [64 keys x 128 B]   (MN-major B)
+//     output staging 8 warps x 32 rows x 20 floats, barriers, row-max/sum exchange
+// All barrier phases run on per-CTA counters (tile counter gi, unit counter
+// uk) that continue across units.
 // ------------------------------------------------------------------------
 struct PrefillParams {
-    const __half *q;  // [8][T][256] fp16, normalised + rotated
     float *out;       // [T][8][256]
     int T;
     int start_pos;
     int kv_pos0;      // position of K/V row 0
     int is_global;
+    int nqb;          // query blocks of 64 tokens
     unsigned *err;
 };
 
 constexpr int kPfSoftmaxThreads = 256;
 constexpr int kPfThreads = kPfSoftmaxThreads + 96;  // + producer warp + two MMA warps
 constexpr int kPfWarpTma = 8;
-constexpr int kPfWarpMma = 9;  // S MMAs; also owns the TMEM allocation
+constexpr int kPfWarpMma = 9;  // Q copies + S MMAs; also owns the TMEM allocation
 constexpr int kPfWarpPv = 10;  // PV MMAs
-constexpr int kPfStages = 3;
 constexpr float kRescaleLog2 = 8.0f;
 #ifndef G3_EXP_EMU_QUARTERS
 #define G3_EXP_EMU_QUARTERS 0
 #endif
 constexpr int kExpEmuQuarters = G3_EXP_EMU_QUARTERS;
 
-// Development-only per-tile timestamps of CTA (0,0) (build with
-// -DG3_PF_TRACE); compiled out of the library.
-#ifdef G3_PF_TRACE
-__device__ long long g3_pf_trace[8][256];
-#define G3_TRACE(slot, i)                                                     \
-    do {                                                                      \
-        if (blockIdx.x == 0 && blockIdx.y == 0 && (i) < 256)                  \
-            g3_pf_trace[slot][i] = clock64();                                 \
-    } while (0)
-#else
-#define G3_TRACE(slot, i) \
-    do {                  \
-    } while (0)
-#endif
-
+constexpr uint32_t kPfQBytes = 128 * 256 * 2;
 constexpr uint32_t kPfKVStage = 64 * 256 * 2;
-constexpr uint32_t kPfOffK = 0;
-constexpr uint32_t kPfOffV = kPfOffK + kPfStages * kPfKVStage;
-constexpr uint32_t kPfOffBar = kPfOffV + kPfStages * kPfKVStage;
+constexpr int kPfOutRowF = 20;  // staging row stride (floats): 16 data + 4 pad
+constexpr uint32_t kPfOffQ = 0;
+constexpr uint32_t kPfOffK = kPfOffQ + kPfQBytes;
+constexpr uint32_t kPfOffV = kPfOffK + 2 * kPfKVStage;
+constexpr uint32_t kPfOffOut = kPfOffV + 2 * kPfKVStage;
+constexpr uint32_t kPfOffBar = kPfOffOut + 8 * 32 * kPfOutRowF * 4;
 constexpr uint32_t kPfOffRed = kPfOffBar + 256;
 constexpr uint32_t kPfSmem = kPfOffRed + 3072 + 1024;  // + alignment slack
 constexpr uint32_t kTmemCols = 512;
@@ -783,57 +775,64 @@ constexpr uint32_t kTmemS = 128;
 constexpr uint32_t kTmemP = 192;
 constexpr uint32_t kTmemO = 256;
 
+// The unit list: index -> (query block, kv head), costliest blocks first
+// (causal rows grow with the block index; local-layer blocks are equal).
+struct PfUnit {
+    int t0, qlo, qhi, j0, ntiles, g;
+};
+__device__ __forceinline__ PfUnit pf_unit(const PrefillParams &p, int idx) {
+    PfUnit u;
+    const int qb = p.nqb - 1 - idx / kKvHeads;
+    u.g = idx % kKvHeads;
+    u.t0 = qb * 64;
+    u.qlo = p.start_pos + u.t0;
+    u.qhi = p.start_pos + min(u.t0 + 64, p.T) - 1;
+    const int kmin = p.is_global ? 0 : max(0, u.qlo - (kWindow - 1));
+    u.j0 = (kmin - p.kv_pos0) / 64;
+    u.ntiles = (u.qhi - p.kv_pos0) / 64 + 1 - u.j0;
+    return u;
+}
+
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_fa_sm100(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const PrefillParams p) {
     extern __shared__ unsigned char smem_raw[];
     unsigned char *sm = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned char *sQ = sm + kPfOffQ;
     unsigned char *sK = sm + kPfOffK;
     unsigned char *sV = sm + kPfOffV;
     float *red = reinterpret_cast<float *>(sm + kPfOffRed);  // [2 parity][2 half][128] maxima, then [2][128] sums
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kPfOffBar);
-    uint64_t *q_smem = bars + 0;    // Q tile landed in shared memory (TMA)
-    uint64_t *k_full = bars + 1;    // [3]
-    uint64_t *k_empty = bars + 4;   // [3]
-    uint64_t *v_full = bars + 7;    // [3]
-    uint64_t *v_empty = bars + 10;  // [3]
-    uint64_t *s_full = bars + 13;
-    uint64_t *s_free = bars + 14;   // 256 arrivals
-    uint64_t *p_full = bars + 15;   // [2], 256 arrivals
-    uint64_t *p_empty = bars + 17;  // [2]
-    uint64_t *mma_done = bars + 19;
-    uint64_t *red_bar = bars + 20;  // [2], 256 arrivals
-    uint64_t *fin_bar = bars + 22;  // 256 arrivals
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 23);
-    volatile int *s_abort = reinterpret_cast<volatile int *>(bars + 24);
-    uint64_t *mma_done_pv = bars + 25;
-    uint64_t *out_bar = bars + 26;  // O staged in shared memory (256 arrivals)
-    uint64_t *q_tmem = bars + 27;   // Q copied into TMEM; its smem is free
+    uint64_t *q_smem = bars + 0;    // Q tile landed in staging (TMA)
+    uint64_t *k_full = bars + 1;    // [2]
+    uint64_t *k_empty = bars + 3;   // [2]
+    uint64_t *v_full = bars + 5;    // [2]
+    uint64_t *v_empty = bars + 7;   // [2]
+    uint64_t *s_full = bars + 9;
+    uint64_t *s_free = bars + 10;   // 256 arrivals
+    uint64_t *p_full = bars + 11;   // [2], 256 arrivals
+    uint64_t *p_empty = bars + 13;  // [2]
+    uint64_t *mma_done = bars + 15;
+    uint64_t *mma_done_pv = bars + 16;
+    uint64_t *q_tmem = bars + 17;   // Q copied into TMEM; staging free
+    uint64_t *red_bar = bars + 18;  // [2], 256 arrivals
+    uint64_t *fin_bar = bars + 20;  // 256 arrivals, once per unit
+    uint64_t *o_free = bars + 21;   // 256 arrivals: epilogue has read O
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 22);
+    volatile int *s_abort = reinterpret_cast<volatile int *>(bars + 23);
 
-    if (threadIdx.x == 0) G3_TRACE(7, 255);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nqb = gridDim.x;
-    const int qb = nqb - 1 - blockIdx.x;  // longest causal rows first
-    const int g = blockIdx.y;
-    const int t0 = qb * 64;
-    const int qlo = p.start_pos + t0;
-    const int qhi = p.start_pos + min(t0 + 64, p.T) - 1;
-    const int kmin = p.is_global ? 0 : max(0, qlo - (kWindow - 1));
-    const int j0 = (kmin - p.kv_pos0) / 64;
-    const int j1 = (qhi - p.kv_pos0) / 64 + 1;
-    const int ntiles = j1 - j0;
+    const int nunits = p.nqb * kKvHeads;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 23; ++i) mbar_init(&bars[i], 1);
+        for (int i = 0; i < 22; ++i) mbar_init(&bars[i], 1);
         mbar_init(s_free, kPfSoftmaxThreads);
         for (int b = 0; b < 2; ++b) {
             mbar_init(&p_full[b], kPfSoftmaxThreads);
             mbar_init(&red_bar[b], kPfSoftmaxThreads);
         }
         mbar_init(fin_bar, kPfSoftmaxThreads);
-        mbar_init(mma_done_pv, 1);
-        mbar_init(out_bar, kPfSoftmaxThreads);
-        mbar_init(q_tmem, 1);
+        mbar_init(o_free, kPfSoftmaxThreads);
         *s_abort = 0;
         fence_mbar_init();
     }
@@ -849,92 +848,97 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             prefetch_tmap(&tmQ);
             prefetch_tmap(&tmK);
             prefetch_tmap(&tmV);
-            // Q goes through V stages 0-1 (64 KB, 128-B swizzled K-major
-            // layout: 4 dim-chunks x [128 rows x 128 B]) on its way to TMEM.
-            mbar_expect_tx(q_smem, 128 * 256 * 2);
-            for (int c = 0; c < 4; ++c)
-                for (int hh = 0; hh < 2; ++hh)
-                    tma_load_3d(sV + c * 16384 + hh * 8192, &tmQ, 64 * c, t0, 2 * g + hh, q_smem);
-            for (int i = 0; i < ntiles && !*s_abort; ++i) {
-                const int s = i % kPfStages, n = i / kPfStages;
-                const int krow = (j0 + i) * 64;
-                if (n >= 1 && !mbar_wait(&k_empty[s], (n - 1) & 1, p.err)) { *s_abort = 1; break; }
-                G3_TRACE(5, i);
-                mbar_expect_tx(&k_full[s], kPfKVStage);
+            int gi = 0, uk = 0;
+            for (int idx = blockIdx.x; idx < nunits && !*s_abort; idx += gridDim.x, ++uk) {
+                const PfUnit u = pf_unit(p, idx);
+                // the staging holds the previous unit's Q until it is in TMEM
+                if (uk >= 1 && !mbar_wait(q_tmem, (uk - 1) & 1, p.err)) { *s_abort = 1; break; }
+                mbar_expect_tx(q_smem, kPfQBytes);
                 for (int c = 0; c < 4; ++c)
-                    tma_load_3d(sK + s * kPfKVStage + c * 8192, &tmK, 64 * c, krow, g, &k_full[s]);
-                if (n >= 1 && !mbar_wait(&v_empty[s], (n - 1) & 1, p.err)) { *s_abort = 1; break; }
-                if (i == 0 && !mbar_wait(q_tmem, 0, p.err)) { *s_abort = 1; break; }
-                mbar_expect_tx(&v_full[s], kPfKVStage);
-                for (int c = 0; c < 4; ++c)
-                    tma_load_3d(sV + s * kPfKVStage + c * 8192, &tmV, 64 * c, krow, g, &v_full[s]);
+                    for (int hh = 0; hh < 2; ++hh)
+                        tma_load_3d(sQ + c * 16384 + hh * 8192, &tmQ, 64 * c, u.t0, 2 * u.g + hh, q_smem);
+                for (int i = 0; i < u.ntiles; ++i, ++gi) {
+                    const int s = gi & 1, n = gi >> 1;
+                    const int krow = (u.j0 + i) * 64;
+                    if (n >= 1 && !mbar_wait(&k_empty[s], (n - 1) & 1, p.err)) { *s_abort = 1; break; }
+                    mbar_expect_tx(&k_full[s], kPfKVStage);
+                    for (int c = 0; c < 4; ++c)
+                        tma_load_3d(sK + s * kPfKVStage + c * 8192, &tmK, 64 * c, krow, u.g, &k_full[s]);
+                    if (n >= 1 && !mbar_wait(&v_empty[s], (n - 1) & 1, p.err)) { *s_abort = 1; break; }
+                    mbar_expect_tx(&v_full[s], kPfKVStage);
+                    for (int c = 0; c < 4; ++c)
+                        tma_load_3d(sV + s * kPfKVStage + c * 8192, &tmV, 64 * c, krow, u.g, &v_full[s]);
+                }
             }
         }
     } else if (warp == kPfWarpMma) {
-        // ------------------------------------------------ S = Q.K^T issuer
-        // S and PV are issued by two different warps so that each MMA goes
-        // to the tensor pipe as soon as its own operands are ready: with one
-        // issuing thread, S(i+1) queued behind PV(i-1), which waits for the
-        // softmax of tile i-1.
+        // ------------------------------------------------ Q -> TMEM, S = Q.K^T
         if (lane == 0) {
             constexpr uint32_t idS = idesc_f16_f32(128, 64, 0, 0);
             // Descriptors are built once; per MMA only the start-address field
             // (bits 0-13, address >> 4, no carry for addresses < 256 KB)
             // advances, by compile-time constants.
+            const uint64_t dQ = smem_desc_sw128(smem_u32(sQ), 16, 1024);
             const uint64_t dK0 = smem_desc_sw128(smem_u32(sK), 16, 1024);
-            bool ok = mbar_wait(q_smem, 0, p.err);
-            tc_fence_after();
-            if (ok) {
-                // Q -> TMEM columns kTmemQ.. as 16 slices of K=16 (8 columns each)
-                const uint64_t dQ = smem_desc_sw128(smem_u32(sV), 16, 1024);
+            bool ok = true;
+            int gi = 0, uk = 0;
+            for (int idx = blockIdx.x; ok && idx < nunits; idx += gridDim.x, ++uk) {
+                const PfUnit u = pf_unit(p, idx);
+                if (*s_abort || !mbar_wait(q_smem, uk & 1, p.err)) { ok = false; break; }
+                tc_fence_after();
+                // Issued after the previous unit's S MMAs: tcgen05 operations
+                // of one thread execute in order, so they have read the old Q.
 #pragma unroll
                 for (int kk = 0; kk < 16; ++kk)
                     tc_cp_128x256b(tmem + kTmemQ + kk * 8, dQ + (uint64_t)(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4));
                 tc_commit(q_tmem);
-            }
-            for (int i = 0; ok && i < ntiles; ++i) {
-                if (*s_abort) { ok = false; break; }
-                const int s = i % kPfStages;
-                if (!mbar_wait(&k_full[s], (i / kPfStages) & 1, p.err)) { ok = false; break; }
-                G3_TRACE(6, i);
-                // the single S buffer is free once softmax(i-1) has read it
-                if (i >= 1 && !mbar_wait(s_free, (i - 1) & 1, p.err)) { ok = false; break; }
-                tc_fence_after();
-                G3_TRACE(7, i);
-                const uint64_t dK = dK0 + (uint64_t)((s * kPfKVStage) >> 4);
+                for (int i = 0; i < u.ntiles; ++i, ++gi) {
+                    if (*s_abort) { ok = false; break; }
+                    const int s = gi & 1;
+                    if (!mbar_wait(&k_full[s], (gi >> 1) & 1, p.err)) { ok = false; break; }
+                    // the single S buffer is free once the softmax has read the last one
+                    if (gi >= 1 && !mbar_wait(s_free, (gi - 1) & 1, p.err)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint64_t dK = dK0 + (uint64_t)((s * kPfKVStage) >> 4);
 #pragma unroll
-                for (int kk = 0; kk < 16; ++kk)
-                    tc_mma_f16_ts(tmem + kTmemS, tmem + kTmemQ + kk * 8,
-                                  dK + (uint64_t)(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4), idS, kk > 0 ? 1u : 0u);
-                tc_commit(&k_empty[s]);
-                tc_commit(s_full);
-                G3_TRACE(0, i);
+                    for (int kk = 0; kk < 16; ++kk)
+                        tc_mma_f16_ts(tmem + kTmemS, tmem + kTmemQ + kk * 8,
+                                      dK + (uint64_t)(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4), idS, kk > 0 ? 1u : 0u);
+                    tc_commit(&k_empty[s]);
+                    tc_commit(s_full);
+                }
             }
             if (!ok) *s_abort = 1;
-            // Drain: every MMA this thread issued has completed once this fires.
+            // Drain: every tcgen05 operation this thread issued has completed.
             tc_commit(mma_done);
             mbar_wait(mma_done, 0, nullptr);
         }
     } else if (warp == kPfWarpPv) {
-        // ------------------------------------------------ O += P.V issuer
+        // ------------------------------------------------ O += P.V
         if (lane == 0) {
             constexpr uint32_t idO = idesc_f16_f32(128, 256, 0, 1);
             const uint64_t dV0 = smem_desc_sw128(smem_u32(sV), 8192, 1024);
             bool ok = true;
-            for (int u = 0; u < ntiles; ++u) {
-                if (*s_abort) { ok = false; break; }
-                const int su = u % kPfStages, pb = u & 1;
-                if (!mbar_wait(&p_full[pb], (u >> 1) & 1, p.err)) { ok = false; break; }
-                G3_TRACE(1, u);
-                if (!mbar_wait(&v_full[su], (u / kPfStages) & 1, p.err)) { ok = false; break; }
-                tc_fence_after();
-                const uint64_t dV = dV0 + (uint64_t)((su * kPfKVStage) >> 4);
+            int gi = 0, uk = 0;
+            for (int idx = blockIdx.x; ok && idx < nunits; idx += gridDim.x, ++uk) {
+                const PfUnit u = pf_unit(p, idx);
+                for (int i = 0; i < u.ntiles; ++i, ++gi) {
+                    if (*s_abort) { ok = false; break; }
+                    const int su = gi & 1, pb = gi & 1;
+                    if (!mbar_wait(&p_full[pb], (gi >> 1) & 1, p.err)) { ok = false; break; }
+                    if (!mbar_wait(&v_full[su], (gi >> 1) & 1, p.err)) { ok = false; break; }
+                    // the first PV of a unit overwrites O: the previous unit's
+                    // epilogue must have read it
+                    if (i == 0 && uk >= 1 && !mbar_wait(o_free, (uk - 1) & 1, p.err)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint64_t dV = dV0 + (uint64_t)((su * kPfKVStage) >> 4);
 #pragma unroll
-                for (int kk = 0; kk < 4; ++kk)
-                    tc_mma_f16_ts(tmem + kTmemO, tmem + kTmemP + pb * 32 + kk * 8, dV + (uint64_t)((kk * 2048) >> 4),
-                                  idO, (u > 0 || kk > 0) ? 1u : 0u);
-                tc_commit(&v_empty[su]);
-                tc_commit(&p_empty[pb]);
+                    for (int kk = 0; kk < 4; ++kk)
+                        tc_mma_f16_ts(tmem + kTmemO, tmem + kTmemP + pb * 32 + kk * 8, dV + (uint64_t)((kk * 2048) >> 4),
+                                      idO, (i > 0 || kk > 0) ? 1u : 0u);
+                    tc_commit(&v_empty[su]);
+                    tc_commit(&p_empty[pb]);
+                }
             }
             if (!ok) *s_abort = 1;
             tc_commit(mma_done_pv);
@@ -945,148 +949,151 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const int row = threadIdx.x & 127;  // TMEM lane == S/O row
         const int half = threadIdx.x >> 7;  // keys [32*half, +32), O cols [128*half, +128)
         const int tr = row & 63, hh = row >> 6;
-        const int qpos = p.start_pos + t0 + tr;
         const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-        const int lo_ok = p.is_global ? INT_MIN : qpos - (kWindow - 1);
-        float m = -INFINITY;  // reference max of the row, log2 domain
-        float l = 0.f;        // this half's share of the row sum
+        float *stage = reinterpret_cast<float *>(sm + kPfOffOut) + warp * 32 * kPfOutRowF;
         bool ok = true;
-        for (int i = 0; i < ntiles; ++i) {
-            const int pb = i & 1;
-            // every wait's outcome is made warp-uniform so the warp-collective
-            // tcgen05 and vote instructions below never run diverged
-            if (!__all_sync(0xffffffffu, !*s_abort && mbar_wait(s_full, i & 1, p.err))) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            if (threadIdx.x == 0) G3_TRACE(2, i);
-            float x[32];
-            tmem_ld32(lane_base + kTmemS + half * 32, x);
-            tc_wait_ld();
-            tc_fence_before();
-            mbar_arrive(s_free);
-            const int tb = p.kv_pos0 + (j0 + i) * 64;  // position of the tile's first key
-            const bool edge = (tb + 63 > qlo) || (!p.is_global && tb < qhi - (kWindow - 1));
-            float mx = -INFINITY;
-            if (edge) {
-                const int kb = tb + half * 32;
-#pragma unroll
-                for (int k = 0; k < 32; ++k) {
-                    const int kp = kb + k;
-                    if (!(kp <= qpos && kp >= lo_ok)) x[k] = -INFINITY;
-                    mx = fmaxf(mx, x[k]);
+        int gi = 0, uk = 0;
+        for (int idx = blockIdx.x; ok && idx < nunits; idx += gridDim.x, ++uk) {
+            const PfUnit u = pf_unit(p, idx);
+            const int qpos = p.start_pos + u.t0 + tr;
+            const int lo_ok = p.is_global ? INT_MIN : qpos - (kWindow - 1);
+            float m = -INFINITY;  // reference max of the row, log2 domain
+            float l = 0.f;        // this half's share of the row sum
+            for (int i = 0; i < u.ntiles; ++i, ++gi) {
+                const int pb = gi & 1;
+                // every wait's outcome is made warp-uniform so the warp-collective
+                // tcgen05 and vote instructions below never run diverged
+                if (!__all_sync(0xffffffffu, !*s_abort && mbar_wait(s_full, gi & 1, p.err))) {
+                    ok = false;
+                    break;
                 }
-            } else {
+                tc_fence_after();
+                float x[32];
+                tmem_ld32(lane_base + kTmemS + half * 32, x);
+                tc_wait_ld();
+                tc_fence_before();
+                mbar_arrive(s_free);
+                const int tb = p.kv_pos0 + (u.j0 + i) * 64;  // position of the tile's first key
+                const bool edge = (tb + 63 > u.qlo) || (!p.is_global && tb < u.qhi - (kWindow - 1));
+                float mx = -INFINITY;
+                if (edge) {
+                    const int kb = tb + half * 32;
 #pragma unroll
-                for (int k = 0; k < 32; ++k) mx = fmaxf(mx, x[k]);
-            }
-            mx *= kScaleLog2;
-            red[(pb * 2 + half) * 128 + row] = mx;
-            mbar_arrive(&red_bar[pb]);
-            if (!__all_sync(0xffffffffu, mbar_wait(&red_bar[pb], (i >> 1) & 1, p.err))) {
-                ok = false;
-                break;
-            }
-            if (threadIdx.x == 0) G3_TRACE(3, i);
-            mx = fmaxf(mx, red[(pb * 2 + (half ^ 1)) * 128 + row]);
-            const bool raise = mx > m + kRescaleLog2;  // false while the row has no valid key
-            const float m_new = raise ? mx : m;
-            const float alpha = raise ? ex2_approx(m - m_new) : 1.f;
-            float rs = 0.f;
-            uint32_t pk[16];
-            if (m_new == -INFINITY) {
+                    for (int k = 0; k < 32; ++k) {
+                        const int kp = kb + k;
+                        if (!(kp <= qpos && kp >= lo_ok)) x[k] = -INFINITY;
+                        mx = fmaxf(mx, x[k]);
+                    }
+                } else {
 #pragma unroll
-                for (int k = 0; k < 16; ++k) pk[k] = 0u;
-            } else {
-                const float nm = -m_new;
-#pragma unroll
-                for (int k = 0; k < 16; ++k) {
-                    // kExpEmuQuarters of every four element pairs use the
-                    // FMA-pipe exp2, the rest the transcendental unit.
-                    const bool emu = (k & 3) < kExpEmuQuarters;
-                    const float a0 = fmaf(x[2 * k], kScaleLog2, nm), a1 = fmaf(x[2 * k + 1], kScaleLog2, nm);
-                    const float e0 = emu ? ex2_poly(a0) : ex2_approx(a0);
-                    const float e1 = emu ? ex2_poly(a1) : ex2_approx(a1);
-                    rs += e0 + e1;
-                    pk[k] = pack_f16x2(e0, e1);
+                    for (int k = 0; k < 32; ++k) mx = fmaxf(mx, x[k]);
                 }
-            }
-            // P buffer pb was last read by PV(i-2); O is written by PV(i-1),
-            // so an O rescale waits for that one too.
-            if (i >= 2 && !__all_sync(0xffffffffu, mbar_wait(&p_empty[pb], ((i - 2) >> 1) & 1, p.err))) {
-                ok = false;
-                break;
-            }
-            const bool rescale = i >= 1 && __any_sync(0xffffffffu, raise);
-            if (rescale && !__all_sync(0xffffffffu, mbar_wait(&p_empty[pb ^ 1], ((i - 1) >> 1) & 1, p.err))) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            if (rescale) {
+                mx *= kScaleLog2;
+                red[(pb * 2 + half) * 128 + row] = mx;
+                mbar_arrive(&red_bar[pb]);
+                if (!__all_sync(0xffffffffu, mbar_wait(&red_bar[pb], (gi >> 1) & 1, p.err))) {
+                    ok = false;
+                    break;
+                }
+                mx = fmaxf(mx, red[(pb * 2 + (half ^ 1)) * 128 + row]);
+                const bool raise = mx > m + kRescaleLog2;  // false while the row has no valid key
+                const float m_new = raise ? mx : m;
+                const float alpha = raise ? ex2_approx(m - m_new) : 1.f;
+                float rs = 0.f;
+                uint32_t pk[16];
+                if (m_new == -INFINITY) {
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) pk[k] = 0u;
+                } else {
+                    const float nm = -m_new;
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) {
+                        // kExpEmuQuarters of every four element pairs use the
+                        // FMA-pipe exp2, the rest the transcendental unit.
+                        const bool emu = (k & 3) < kExpEmuQuarters;
+                        const float a0 = fmaf(x[2 * k], kScaleLog2, nm), a1 = fmaf(x[2 * k + 1], kScaleLog2, nm);
+                        const float e0 = emu ? ex2_poly(a0) : ex2_approx(a0);
+                        const float e1 = emu ? ex2_poly(a1) : ex2_approx(a1);
+                        rs += e0 + e1;
+                        pk[k] = pack_f16x2(e0, e1);
+                    }
+                }
+                // P buffer pb was last read by PV(gi-2); O is written by PV(gi-1),
+                // so an O rescale waits for that one too (never on a unit's first tile).
+                if (gi >= 2 && !__all_sync(0xffffffffu, mbar_wait(&p_empty[pb], ((gi - 2) >> 1) & 1, p.err))) {
+                    ok = false;
+                    break;
+                }
+                const bool rescale = i >= 1 && __any_sync(0xffffffffu, raise);
+                if (rescale && !__all_sync(0xffffffffu, mbar_wait(&p_empty[pb ^ 1], ((gi - 1) >> 1) & 1, p.err))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                if (rescale) {
 #pragma unroll 1
-                for (int cc = 0; cc < 4; ++cc) {
-                    float o[32];
-                    const uint32_t ta = lane_base + kTmemO + half * 128 + cc * 32;
-                    tmem_ld32(ta, o);
-                    tc_wait_ld();
+                    for (int cc = 0; cc < 4; ++cc) {
+                        float o[32];
+                        const uint32_t ta = lane_base + kTmemO + half * 128 + cc * 32;
+                        tmem_ld32(ta, o);
+                        tc_wait_ld();
 #pragma unroll
-                    for (int k = 0; k < 32; ++k) o[k] *= alpha;
-                    tmem_st32(ta, o);
+                        for (int k = 0; k < 32; ++k) o[k] *= alpha;
+                        tmem_st32(ta, o);
+                    }
+                    tc_wait_st();
                 }
+                l = l * alpha + rs;
+                m = m_new;
+                tmem_st16(lane_base + kTmemP + pb * 32 + half * 16, pk);
                 tc_wait_st();
+                tc_fence_before();
+                mbar_arrive(&p_full[pb]);
             }
-            l = l * alpha + rs;
-            m = m_new;
-            tmem_st16(lane_base + kTmemP + pb * 32 + half * 16, pk);
-            tc_wait_st();
-            tc_fence_before();
-            if (threadIdx.x == 0) G3_TRACE(4, i);
-            mbar_arrive(&p_full[pb]);
-        }
-        if (!ok) *s_abort = 1;
-        // Epilogue: O / (l_half0 + l_half1) -> out[t][2g+hh][:]
-        if (ok) {
+            if (!ok) break;
+            // ---- epilogue of the unit: O / (l_half0 + l_half1) -> out[t][2g+hh][:]
             red[512 + half * 128 + row] = l;
             mbar_arrive(fin_bar);
-            const int u = ntiles - 1;
-            ok = __all_sync(0xffffffffu, mbar_wait(fin_bar, 0, p.err) &&
-                                             mbar_wait(&p_empty[u & 1], (u >> 1) & 1, p.err));
-        }
-        if (ok) {
+            const int gl = gi - 1;  // the unit's last tile
+            if (!__all_sync(0xffffffffu, mbar_wait(fin_bar, uk & 1, p.err) &&
+                                             mbar_wait(&p_empty[gl & 1], (gl >> 1) & 1, p.err))) {
+                ok = false;
+                break;
+            }
             tc_fence_after();
-            if (threadIdx.x == 0) G3_TRACE(5, 253);
             const float lt = red[512 + row] + red[640 + row];
             const float inv = lt > 0.f ? 1.0f / lt : 0.f;
-            // Stage O/l in the (now idle) K/V ring, rows padded to 1040 B so
-            // the per-row float4 writes of a warp hit distinct banks, then
-            // write it out with fully coalesced stores: output row r of the
-            // tile is out[t0 + (r & 63)][2g + (r >> 6)][:], 1 KB contiguous.
-            float *stage = reinterpret_cast<float *>(sK);
-            constexpr int kRowF = kHeadDim + 4;
+            const int nvalid = min(64, p.T - u.t0);
+            // 16 columns at a time: TMEM -> this warp's staging rows -> stores
+            // of 64 contiguous bytes per 4 lanes.
 #pragma unroll 1
-            for (int cc = 0; cc < 4; ++cc) {
-                float o[32];
-                tmem_ld32(lane_base + kTmemO + half * 128 + cc * 32, o);
+            for (int cc = 0; cc < 8; ++cc) {
+                float o[16];
+                tmem_ld16(lane_base + kTmemO + half * 128 + cc * 16, o);
                 tc_wait_ld();
-                float *dst = stage + row * kRowF + half * 128 + cc * 32;
-#pragma unroll
-                for (int k = 0; k < 32; k += 4)
-                    *reinterpret_cast<float4 *>(dst + k) =
-                        make_float4(o[k] * inv, o[k + 1] * inv, o[k + 2] * inv, o[k + 3] * inv);
-            }
-            mbar_arrive(out_bar);
-            ok = __all_sync(0xffffffffu, mbar_wait(out_bar, 0, p.err));
-            if (ok) {
-                const int nrow_valid = min(64, p.T - t0);
-                for (int idx = threadIdx.x; idx < 128 * 64; idx += kPfSoftmaxThreads) {
-                    const int r = idx >> 6, c4 = idx & 63;
-                    if ((r & 63) >= nrow_valid) continue;
-                    const float4 v4 = *reinterpret_cast<const float4 *>(stage + r * kRowF + c4 * 4);
-                    float *dst = p.out + ((size_t)(t0 + (r & 63)) * kHeads + 2 * g + (r >> 6)) * kHeadDim;
-                    *reinterpret_cast<float4 *>(dst + c4 * 4) = v4;
+                if (cc == 7) {
+                    // all of O read from TMEM: the next unit's PV may overwrite it
+                    tc_fence_before();
+                    mbar_arrive(o_free);
                 }
+                float *srow = stage + lane * kPfOutRowF;
+#pragma unroll
+                for (int k = 0; k < 16; k += 4)
+                    *reinterpret_cast<float4 *>(srow + k) = make_float4(o[k] * inv, o[k + 1] * inv, o[k + 2] * inv, o[k + 3] * inv);
+                __syncwarp();
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    const int e = j * 32 + lane;
+                    const int rl = e >> 2, c4 = e & 3;  // row within the warp, float4 within 16 columns
+                    const int rr = (warp & 3) * 32 + rl;  // tile row
+                    if ((rr & 63) < nvalid) {
+                        const float4 v4 = *reinterpret_cast<const float4 *>(stage + rl * kPfOutRowF + c4 * 4);
+                        float *dst = p.out + ((size_t)(u.t0 + (rr & 63)) * kHeads + 2 * u.g + (rr >> 6)) * kHeadDim +
+                                     half * 128 + cc * 16 + c4 * 4;
+                        *reinterpret_cast<float4 *>(dst) = v4;
+                    }
+                }
+                __syncwarp();
             }
         }
         if (!ok) *s_abort = 1;
@@ -1095,7 +1102,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     __syncthreads();
     if (warp == kPfWarpTma && lane == 0 && *s_abort) {
         // Let in-flight TMA copies land before the CTA's shared memory goes.
-        for (int s = 0; s < kPfStages; ++s) {
+        mbar_wait(q_smem, 0, nullptr);
+        for (int s = 0; s < 2; ++s) {
             mbar_wait(&k_full[s], 0, nullptr);
             mbar_wait(&v_full[s], 0, nullptr);
         }
@@ -1105,7 +1113,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         tc_fence_after();
         tmem_dealloc(tmem, kTmemCols);
     }
-    if (threadIdx.x == 0) G3_TRACE(6, 255);
 }
 
 // ------------------------------------------------------------------------

@@ -147,6 +147,7 @@ struct gemma3_cuda_ctx {
     size_t io_rows = 0;
     unsigned *err = nullptr;
     long long launches = 0;
+    int sm_count = 148;
     g3NcclComm comm = nullptr;
     // profiling of the dominant kernels (decode_splitkv = 0, prefill_fa = 1)
     bool prof = false;
@@ -233,6 +234,7 @@ static int ctx_alloc(gemma3_cuda_ctx *c) {
         return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "device %d is sm_%d%d; this library is built for sm_100a only",
                     k.device, major, minor);
     CU_TRY(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+    CU_TRY(cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, k.device));
     c->esz = k.kv_dtype == GEMMA3_CUDA_KV_BF16 ? 2 : 4;
     const int S = (k.max_context + k.kv_ranks - 1) / k.kv_ranks;
     c->shard_lo = std::min(k.max_context, k.kv_rank * S);
@@ -432,7 +434,6 @@ static int prefill_impl(gemma3_cuda_ctx *ctx, int layer, int seq, const float *Q
     if (int r = make_map(&tk, ctx->kst, lrows, plane, kKvHeads)) return r;
     if (int r = make_map(&tv, ctx->vst, lrows, plane, kKvHeads)) return r;
     g3::PrefillParams p;
-    p.q = ctx->qst;
     p.out = out;
     p.T = T;
     p.start_pos = start_pos;
@@ -440,9 +441,11 @@ static int prefill_impl(gemma3_cuda_ctx *ctx, int layer, int seq, const float *Q
     p.is_global = global;
     p.err = ctx->err;
     const int nqb = (T + 63) / 64;
+    p.nqb = nqb;
+    const int grid = std::min(nqb * kKvHeads, ctx->sm_count);  // persistent: one CTA per SM
     size_t e0;
     prof_begin(ctx, &e0);
-    g3::prefill_fa_sm100<<<dim3(nqb, kKvHeads), g3::kPfThreads, g3::kPfSmem, ctx->stream>>>(tq, tk, tv, p);
+    g3::prefill_fa_sm100<<<grid, g3::kPfThreads, g3::kPfSmem, ctx->stream>>>(tq, tk, tv, p);
     if (ctx->prof) {
         // algorithmic FLOPs: 2 (QK) + 2 (PV) x 256 x 8 heads per attended key
         double keys = 0;

@@ -217,3 +217,50 @@ def test_errors_are_reported(ropes):
         ctx.attn_prefill(0, 0, Q, K, V, 0)
     assert e.value.code == gc.ERR_INVALID_ARG
     ctx.synchronize()
+
+
+def _norm_rope_np(X, heads, w, rope, start_pos):
+    """numpy restatement of per-head RMSNorm with (1+w) gain
+    (gemma3_kernels.c:289-304) and rotate-half RoPE from the table
+    (gemma3_kernels.c:470-484), for T tokens at positions start_pos..."""
+    T = X.shape[0]
+    x = X.reshape(T, heads, 256).astype(np.float64)
+    if w is not None:
+        g = 1.0 + synth.bf16_to_f32(np.asarray(w)).astype(np.float64)
+        x = x / np.sqrt((x * x).mean(-1, keepdims=True) + 1e-6) * g
+    tab = rope[start_pos:start_pos + T].astype(np.float64)  # [T][128][2]
+    c, s = tab[:, None, :, 0], tab[:, None, :, 1]
+    a, b = x[..., :128], x[..., 128:]
+    return np.concatenate([a * c - b * s, a * s + b * c], -1).reshape(T, heads * 256).astype(np.float32)
+
+
+@pytest.mark.parametrize("layer", [0, 5])
+def test_prefill_8192_many_units_per_cta(ropes, layer):
+    """T=8192: 512 (block, kv head) units on at most one CTA per SM, so every
+    CTA carries Q, S, P and O across several units.  Checked against exact
+    fp32 attention (torch, GPU) of the reference's semantics on the bf16
+    cache contents."""
+    import torch
+    T = 8192
+    glob = gc.is_global_layer(layer)
+    rope = ropes[1] if glob else ropes[0]
+    qn, kn = synth.qk_norm_gains(321)
+    Q, K, V = qkv(4242, T)
+    ctx = make_ctx(ropes, gc.KV_BF16, max_context=T, max_prefill=T)
+    ctx.set_qk_norm(layer, qn, kn)
+    got = ctx.attn_prefill(layer, 0, Q, K, V, 0)
+    ctx.close()
+    Qn = torch.from_numpy(_norm_rope_np(Q, 8, qn, rope, 0)).cuda().view(T, 8, 256)
+    Kn = torch.from_numpy(bf16_round(_norm_rope_np(K, 4, kn, rope, 0))).cuda().view(T, 4, 256)
+    Vb = torch.from_numpy(bf16_round(V)).cuda().view(T, 4, 256)
+    pos = torch.arange(T, device="cuda")
+    ok = pos[None, :] <= pos[:, None]
+    if not glob:
+        ok &= pos[None, :] > pos[:, None] - 1024
+    want = torch.empty(T, 8, 256, device="cuda")
+    for h in range(8):
+        s = (Qn[:, h] @ Kn[:, h // 2].T) / 16.0
+        want[:, h] = torch.softmax(s.masked_fill(~ok, float("-inf")), dim=1) @ Vb[:, h // 2]
+    want = want.view(T, 2048).cpu().numpy()
+    assert np.isfinite(got).all()
+    assert rel_err(got, want) <= TOL, rel_err(got, want)
