@@ -718,7 +718,8 @@ __global__ void __launch_bounds__(256) merge_partials(const float *__restrict__ 
 //                                      B = V tile (MN-major) from shared memory
 // Warp 8 issues the TMA loads, warp 9 the Q copies into TMEM and the S MMAs,
 // warp 10 the PV MMAs (one lane each): each MMA goes to the tensor pipe as
-// soon as its own operands are ready.  Operands are fp16 (see
+// soon as its own operands are ready.  Warps 11-14 write each finished unit's
+// O / l out while the softmax warps already work on the next unit.  Operands are fp16 (see
 // prologue_prefill), accumulation fp32.
 //
 // TMEM columns (512): Q 0-127 (fp16 pairs), S 128-191 (fp32), P 192-255
@@ -734,7 +735,7 @@ __global__ void __launch_bounds__(256) merge_partials(const float *__restrict__ 
 //     Q staging 64 KB: 4 dim-chunks x [128 rows x 128 B]   (TMA -> tcgen05.cp)
 //     K  2 stages x 32 KB: 4 dim-chunks x [64 keys x 128 B]   (K-major B)
 //     V  2 stages x 32 KB: 4 dim-chunks x [64 keys x 128 B]   (MN-major B)
-//     output staging 8 warps x 32 rows x 20 floats, barriers, row-max/sum exchange
+//     output staging 4 warps x 32 rows x 36 floats, barriers, row-max/sum exchange
 // All barrier phases run on per-CTA counters (tile counter gi, unit counter
 // uk) that continue across units.
 // ------------------------------------------------------------------------
@@ -749,26 +750,41 @@ struct PrefillParams {
 };
 
 constexpr int kPfSoftmaxThreads = 256;
-constexpr int kPfThreads = kPfSoftmaxThreads + 96;  // + producer warp + two MMA warps
+constexpr int kPfThreads = kPfSoftmaxThreads + 96 + 128;  // + producer, two MMA warps, 4 epilogue warps
 constexpr int kPfWarpTma = 8;
 constexpr int kPfWarpMma = 9;  // Q copies + S MMAs; also owns the TMEM allocation
 constexpr int kPfWarpPv = 10;  // PV MMAs
+constexpr int kPfWarpEpi = 11; // 11-14: epilogue, one per TMEM lane quadrant
 constexpr float kRescaleLog2 = 8.0f;
 #ifndef G3_EXP_EMU_QUARTERS
 #define G3_EXP_EMU_QUARTERS 0
 #endif
 constexpr int kExpEmuQuarters = G3_EXP_EMU_QUARTERS;
 
+// Development-only per-tile timestamps of CTA 0 (build with -DG3_PF_TRACE);
+// compiled out of the library.
+#ifdef G3_PF_TRACE
+__device__ long long g3_pf_trace[8][512];
+#define G3_TRACE(slot, i)                                                     \
+    do {                                                                      \
+        if (blockIdx.x == 0 && (i) < 512) g3_pf_trace[slot][i] = clock64();   \
+    } while (0)
+#else
+#define G3_TRACE(slot, i) \
+    do {                  \
+    } while (0)
+#endif
+
 constexpr uint32_t kPfQBytes = 128 * 256 * 2;
 constexpr uint32_t kPfKVStage = 64 * 256 * 2;
-constexpr int kPfOutRowF = 20;  // staging row stride (floats): 16 data + 4 pad
+constexpr int kPfOutRowF = 36;  // staging row stride (floats): 32 data + 4 pad
 constexpr uint32_t kPfOffQ = 0;
 constexpr uint32_t kPfOffK = kPfOffQ + kPfQBytes;
 constexpr uint32_t kPfOffV = kPfOffK + 2 * kPfKVStage;
 constexpr uint32_t kPfOffOut = kPfOffV + 2 * kPfKVStage;
-constexpr uint32_t kPfOffBar = kPfOffOut + 8 * 32 * kPfOutRowF * 4;
+constexpr uint32_t kPfOffBar = kPfOffOut + 4 * 32 * kPfOutRowF * 4;
 constexpr uint32_t kPfOffRed = kPfOffBar + 256;
-constexpr uint32_t kPfSmem = kPfOffRed + 3072 + 1024;  // + alignment slack
+constexpr uint32_t kPfSmem = kPfOffRed + 4096 + 1024;  // + alignment slack
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemQ = 0;
 constexpr uint32_t kTmemS = 128;
@@ -780,6 +796,16 @@ constexpr uint32_t kTmemO = 256;
 struct PfUnit {
     int t0, qlo, qhi, j0, ntiles, g;
 };
+// Unit k of this CTA: the cost-sorted list is dealt out in rounds of
+// gridDim.x, alternating direction each round (snake order), which evens out
+// the per-CTA totals of the causal cost ramp.  -1 when the round is short.
+__device__ __forceinline__ int pf_unit_index(int k, int nunits) {
+    const int G = gridDim.x;
+    const int idx = k * G + ((k & 1) ? (G - 1 - (int)blockIdx.x) : (int)blockIdx.x);
+    return idx < nunits ? idx : -1;
+}
+__device__ __forceinline__ int pf_unit_rounds(int nunits) { return (nunits + gridDim.x - 1) / gridDim.x; }
+
 __device__ __forceinline__ PfUnit pf_unit(const PrefillParams &p, int idx) {
     PfUnit u;
     const int qb = p.nqb - 1 - idx / kKvHeads;
@@ -801,7 +827,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     unsigned char *sQ = sm + kPfOffQ;
     unsigned char *sK = sm + kPfOffK;
     unsigned char *sV = sm + kPfOffV;
-    float *red = reinterpret_cast<float *>(sm + kPfOffRed);  // [2 parity][2 half][128] maxima, then [2][128] sums
+    float *red = reinterpret_cast<float *>(sm + kPfOffRed);  // [2 parity][2 half][128] maxima, then [2 unit parity][2 half][128] sums
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kPfOffBar);
     uint64_t *q_smem = bars + 0;    // Q tile landed in staging (TMA)
     uint64_t *k_full = bars + 1;    // [2]
@@ -817,10 +843,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     uint64_t *q_tmem = bars + 17;   // Q copied into TMEM; staging free
     uint64_t *red_bar = bars + 18;  // [2], 256 arrivals
     uint64_t *fin_bar = bars + 20;  // 256 arrivals, once per unit
-    uint64_t *o_free = bars + 21;   // 256 arrivals: epilogue has read O
+    uint64_t *o_free = bars + 21;   // 128 arrivals: the epilogue warps have read O
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 22);
     volatile int *s_abort = reinterpret_cast<volatile int *>(bars + 23);
 
+    if (threadIdx.x == 0) G3_TRACE(7, 0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nunits = p.nqb * kKvHeads;
 
@@ -832,7 +859,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             mbar_init(&red_bar[b], kPfSoftmaxThreads);
         }
         mbar_init(fin_bar, kPfSoftmaxThreads);
-        mbar_init(o_free, kPfSoftmaxThreads);
+        mbar_init(o_free, 128);
         *s_abort = 0;
         fence_mbar_init();
     }
@@ -849,10 +876,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             prefetch_tmap(&tmK);
             prefetch_tmap(&tmV);
             int gi = 0, uk = 0;
-            for (int idx = blockIdx.x; idx < nunits && !*s_abort; idx += gridDim.x, ++uk) {
+            for (int k = 0; k < pf_unit_rounds(nunits) && !*s_abort; ++k) {
+                const int idx = pf_unit_index(k, nunits);
+                if (idx < 0) continue;
                 const PfUnit u = pf_unit(p, idx);
+                const int ukc = uk++;
                 // the staging holds the previous unit's Q until it is in TMEM
-                if (uk >= 1 && !mbar_wait(q_tmem, (uk - 1) & 1, p.err)) { *s_abort = 1; break; }
+                if (ukc >= 1 && !mbar_wait(q_tmem, (ukc - 1) & 1, p.err)) { *s_abort = 1; break; }
+                G3_TRACE(3, ukc);
                 mbar_expect_tx(q_smem, kPfQBytes);
                 for (int c = 0; c < 4; ++c)
                     for (int hh = 0; hh < 2; ++hh)
@@ -882,9 +913,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             const uint64_t dK0 = smem_desc_sw128(smem_u32(sK), 16, 1024);
             bool ok = true;
             int gi = 0, uk = 0;
-            for (int idx = blockIdx.x; ok && idx < nunits; idx += gridDim.x, ++uk) {
+            for (int k = 0; ok && k < pf_unit_rounds(nunits); ++k) {
+                const int idx = pf_unit_index(k, nunits);
+                if (idx < 0) continue;
                 const PfUnit u = pf_unit(p, idx);
-                if (*s_abort || !mbar_wait(q_smem, uk & 1, p.err)) { ok = false; break; }
+                const int ukc = uk++;
+                if (*s_abort || !mbar_wait(q_smem, ukc & 1, p.err)) { ok = false; break; }
                 tc_fence_after();
                 // Issued after the previous unit's S MMAs: tcgen05 operations
                 // of one thread execute in order, so they have read the old Q.
@@ -906,6 +940,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                                       dK + (uint64_t)(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4), idS, kk > 0 ? 1u : 0u);
                     tc_commit(&k_empty[s]);
                     tc_commit(s_full);
+                    G3_TRACE(0, gi);
                 }
             }
             if (!ok) *s_abort = 1;
@@ -920,16 +955,20 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             const uint64_t dV0 = smem_desc_sw128(smem_u32(sV), 8192, 1024);
             bool ok = true;
             int gi = 0, uk = 0;
-            for (int idx = blockIdx.x; ok && idx < nunits; idx += gridDim.x, ++uk) {
+            for (int k = 0; ok && k < pf_unit_rounds(nunits); ++k) {
+                const int idx = pf_unit_index(k, nunits);
+                if (idx < 0) continue;
                 const PfUnit u = pf_unit(p, idx);
+                const int ukc = uk++;
                 for (int i = 0; i < u.ntiles; ++i, ++gi) {
                     if (*s_abort) { ok = false; break; }
                     const int su = gi & 1, pb = gi & 1;
                     if (!mbar_wait(&p_full[pb], (gi >> 1) & 1, p.err)) { ok = false; break; }
                     if (!mbar_wait(&v_full[su], (gi >> 1) & 1, p.err)) { ok = false; break; }
+                    G3_TRACE(1, gi);
                     // the first PV of a unit overwrites O: the previous unit's
                     // epilogue must have read it
-                    if (i == 0 && uk >= 1 && !mbar_wait(o_free, (uk - 1) & 1, p.err)) { ok = false; break; }
+                    if (i == 0 && ukc >= 1 && !mbar_wait(o_free, (ukc - 1) & 1, p.err)) { ok = false; break; }
                     tc_fence_after();
                     const uint64_t dV = dV0 + (uint64_t)((su * kPfKVStage) >> 4);
 #pragma unroll
@@ -944,17 +983,78 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             tc_commit(mma_done_pv);
             mbar_wait(mma_done_pv, 0, nullptr);
         }
+    } else if (warp >= kPfWarpEpi) {
+        // ------------------------------------------------ epilogue warps
+        // O / (l_half0 + l_half1) -> out[t][2g+hh][:]: one warp per TMEM lane
+        // quadrant, thread = row, 32 columns at a time through this warp's
+        // staging rows, stored 128 contiguous bytes per 8 lanes.
+        const int quad = warp & 3;
+        const int row = quad * 32 + lane;
+        const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+        float *stage = reinterpret_cast<float *>(sm + kPfOffOut) + (warp - kPfWarpEpi) * 32 * kPfOutRowF;
+        bool ok = true;
+        int gi = 0, uk = 0;
+        for (int k = 0; ok && k < pf_unit_rounds(nunits); ++k) {
+            const int idx = pf_unit_index(k, nunits);
+            if (idx < 0) continue;
+            const PfUnit u = pf_unit(p, idx);
+            const int ukc = uk++;
+            gi += u.ntiles;
+            const int gl = gi - 1;  // the unit's last tile
+            if (!__all_sync(0xffffffffu, !*s_abort && mbar_wait(fin_bar, ukc & 1, p.err) &&
+                                             mbar_wait(&p_empty[gl & 1], (gl >> 1) & 1, p.err))) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const float lt = red[512 + (ukc & 1) * 256 + row] + red[512 + (ukc & 1) * 256 + 128 + row];
+            const float inv = lt > 0.f ? 1.0f / lt : 0.f;
+            const int nvalid = min(64, p.T - u.t0);
+#pragma unroll 1
+            for (int cc = 0; cc < 8; ++cc) {
+                float o[32];
+                tmem_ld32(lane_base + kTmemO + cc * 32, o);
+                tc_wait_ld();
+                if (cc == 7) {
+                    // all of O read from TMEM: the next unit's PV may overwrite it
+                    tc_fence_before();
+                    mbar_arrive(o_free);
+                }
+                float *srow = stage + lane * kPfOutRowF;
+#pragma unroll
+                for (int k4 = 0; k4 < 32; k4 += 4)
+                    *reinterpret_cast<float4 *>(srow + k4) =
+                        make_float4(o[k4] * inv, o[k4 + 1] * inv, o[k4 + 2] * inv, o[k4 + 3] * inv);
+                __syncwarp();
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const int e = j * 32 + lane;
+                    const int rl = e >> 3, c4 = e & 7;  // row within the quadrant, float4 within 32 columns
+                    const int rr = quad * 32 + rl;      // tile row
+                    if ((rr & 63) < nvalid) {
+                        const float4 v4 = *reinterpret_cast<const float4 *>(stage + rl * kPfOutRowF + c4 * 4);
+                        float *dst = p.out + ((size_t)(u.t0 + (rr & 63)) * kHeads + 2 * u.g + (rr >> 6)) * kHeadDim +
+                                     cc * 32 + c4 * 4;
+                        *reinterpret_cast<float4 *>(dst) = v4;
+                    }
+                }
+                __syncwarp();
+            }
+        }
+        if (!ok) *s_abort = 1;
     } else {
         // ------------------------------------------------ softmax warps 0-7
         const int row = threadIdx.x & 127;  // TMEM lane == S/O row
         const int half = threadIdx.x >> 7;  // keys [32*half, +32), O cols [128*half, +128)
         const int tr = row & 63, hh = row >> 6;
         const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-        float *stage = reinterpret_cast<float *>(sm + kPfOffOut) + warp * 32 * kPfOutRowF;
         bool ok = true;
         int gi = 0, uk = 0;
-        for (int idx = blockIdx.x; ok && idx < nunits; idx += gridDim.x, ++uk) {
+        for (int k = 0; ok && k < pf_unit_rounds(nunits); ++k) {
+            const int idx = pf_unit_index(k, nunits);
+            if (idx < 0) continue;
             const PfUnit u = pf_unit(p, idx);
+            const int ukc = uk++;
             const int qpos = p.start_pos + u.t0 + tr;
             const int lo_ok = p.is_global ? INT_MIN : qpos - (kWindow - 1);
             float m = -INFINITY;  // reference max of the row, log2 domain
@@ -968,6 +1068,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     break;
                 }
                 tc_fence_after();
+                if (threadIdx.x == 0) G3_TRACE(2, gi);
                 float x[32];
                 tmem_ld32(lane_base + kTmemS + half * 32, x);
                 tc_wait_ld();
@@ -1048,56 +1149,24 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 tmem_st16(lane_base + kTmemP + pb * 32 + half * 16, pk);
                 tc_wait_st();
                 tc_fence_before();
+                if (threadIdx.x == 0) G3_TRACE(4, gi);
                 mbar_arrive(&p_full[pb]);
             }
             if (!ok) break;
-            // ---- epilogue of the unit: O / (l_half0 + l_half1) -> out[t][2g+hh][:]
-            red[512 + half * 128 + row] = l;
-            mbar_arrive(fin_bar);
-            const int gl = gi - 1;  // the unit's last tile
-            if (!__all_sync(0xffffffffu, mbar_wait(fin_bar, uk & 1, p.err) &&
-                                             mbar_wait(&p_empty[gl & 1], (gl >> 1) & 1, p.err))) {
+            // ---- hand the unit to the epilogue warps: this half's row sum,
+            // double-buffered by unit parity.  Stay at most one unit ahead of
+            // the epilogue (its barriers count phases by parity).
+            if (threadIdx.x == 0) G3_TRACE(5, ukc);
+            if (ukc >= 1 && !__all_sync(0xffffffffu, mbar_wait(o_free, (ukc - 1) & 1, p.err))) {
                 ok = false;
                 break;
             }
-            tc_fence_after();
-            const float lt = red[512 + row] + red[640 + row];
-            const float inv = lt > 0.f ? 1.0f / lt : 0.f;
-            const int nvalid = min(64, p.T - u.t0);
-            // 16 columns at a time: TMEM -> this warp's staging rows -> stores
-            // of 64 contiguous bytes per 4 lanes.
-#pragma unroll 1
-            for (int cc = 0; cc < 8; ++cc) {
-                float o[16];
-                tmem_ld16(lane_base + kTmemO + half * 128 + cc * 16, o);
-                tc_wait_ld();
-                if (cc == 7) {
-                    // all of O read from TMEM: the next unit's PV may overwrite it
-                    tc_fence_before();
-                    mbar_arrive(o_free);
-                }
-                float *srow = stage + lane * kPfOutRowF;
-#pragma unroll
-                for (int k = 0; k < 16; k += 4)
-                    *reinterpret_cast<float4 *>(srow + k) = make_float4(o[k] * inv, o[k + 1] * inv, o[k + 2] * inv, o[k + 3] * inv);
-                __syncwarp();
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const int e = j * 32 + lane;
-                    const int rl = e >> 2, c4 = e & 3;  // row within the warp, float4 within 16 columns
-                    const int rr = (warp & 3) * 32 + rl;  // tile row
-                    if ((rr & 63) < nvalid) {
-                        const float4 v4 = *reinterpret_cast<const float4 *>(stage + rl * kPfOutRowF + c4 * 4);
-                        float *dst = p.out + ((size_t)(u.t0 + (rr & 63)) * kHeads + 2 * u.g + (rr >> 6)) * kHeadDim +
-                                     half * 128 + cc * 16 + c4 * 4;
-                        *reinterpret_cast<float4 *>(dst) = v4;
-                    }
-                }
-                __syncwarp();
-            }
+            red[512 + (ukc & 1) * 256 + half * 128 + row] = l;
+            mbar_arrive(fin_bar);
         }
         if (!ok) *s_abort = 1;
     }
+    if (threadIdx.x == 0) G3_TRACE(6, 0);
     tc_fence_before();
     __syncthreads();
     if (warp == kPfWarpTma && lane == 0 && *s_abort) {
