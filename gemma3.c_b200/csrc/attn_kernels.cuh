@@ -875,19 +875,32 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             prefetch_tmap(&tmQ);
             prefetch_tmap(&tmK);
             prefetch_tmap(&tmV);
+            // Q of unit uk is loaded one unit ahead: right after the first
+            // tile of unit uk-1 (once that unit's Q has left the staging).
+            auto load_q = [&](int idx) {
+                const PfUnit u = pf_unit(p, idx);
+                mbar_expect_tx(q_smem, kPfQBytes);
+                for (int c = 0; c < 4; ++c)
+                    for (int hh = 0; hh < 2; ++hh)
+                        tma_load_3d(sQ + c * 16384 + hh * 8192, &tmQ, 64 * c, u.t0, 2 * u.g + hh, q_smem);
+            };
+            auto next_unit = [&](int k) {
+                for (++k; k < pf_unit_rounds(nunits); ++k)
+                    if (pf_unit_index(k, nunits) >= 0) return pf_unit_index(k, nunits);
+                return -1;
+            };
             int gi = 0, uk = 0;
+            {
+                const int first = pf_unit_index(0, nunits);
+                if (first >= 0) load_q(first);
+            }
             for (int k = 0; k < pf_unit_rounds(nunits) && !*s_abort; ++k) {
                 const int idx = pf_unit_index(k, nunits);
                 if (idx < 0) continue;
                 const PfUnit u = pf_unit(p, idx);
                 const int ukc = uk++;
-                // the staging holds the previous unit's Q until it is in TMEM
-                if (ukc >= 1 && !mbar_wait(q_tmem, (ukc - 1) & 1, p.err)) { *s_abort = 1; break; }
+                const int nxt = next_unit(k);
                 G3_TRACE(3, ukc);
-                mbar_expect_tx(q_smem, kPfQBytes);
-                for (int c = 0; c < 4; ++c)
-                    for (int hh = 0; hh < 2; ++hh)
-                        tma_load_3d(sQ + c * 16384 + hh * 8192, &tmQ, 64 * c, u.t0, 2 * u.g + hh, q_smem);
                 for (int i = 0; i < u.ntiles; ++i, ++gi) {
                     const int s = gi & 1, n = gi >> 1;
                     const int krow = (u.j0 + i) * 64;
@@ -899,6 +912,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     mbar_expect_tx(&v_full[s], kPfKVStage);
                     for (int c = 0; c < 4; ++c)
                         tma_load_3d(sV + s * kPfKVStage + c * 8192, &tmV, 64 * c, krow, u.g, &v_full[s]);
+                    if (i == 0 && nxt >= 0) {
+                        if (!mbar_wait(q_tmem, ukc & 1, p.err)) { *s_abort = 1; break; }
+                        load_q(nxt);
+                    }
                 }
             }
         }
