@@ -733,9 +733,9 @@ __global__ void __launch_bounds__(256) merge_partials(const float *__restrict__ 
 //
 // Shared memory (1024-aligned, 128-B swizzle for every MMA operand):
 //     Q staging 64 KB: 4 dim-chunks x [128 rows x 128 B]   (TMA -> tcgen05.cp)
-//     K  2 stages x 32 KB: 4 dim-chunks x [64 keys x 128 B]   (K-major B)
+//     K  3 stages x 32 KB: 4 dim-chunks x [64 keys x 128 B]   (K-major B)
 //     V  2 stages x 32 KB: 4 dim-chunks x [64 keys x 128 B]   (MN-major B)
-//     output staging 4 warps x 32 rows x 36 floats, barriers, row-max/sum exchange
+//     barriers, row-max (bf16) / row-sum exchange
 // All barrier phases run on per-CTA counters (tile counter gi, unit counter
 // uk) that continue across units.
 // ------------------------------------------------------------------------
@@ -777,14 +777,15 @@ __device__ long long g3_pf_trace[8][512];
 
 constexpr uint32_t kPfQBytes = 128 * 256 * 2;
 constexpr uint32_t kPfKVStage = 64 * 256 * 2;
-constexpr int kPfOutRowF = 36;  // staging row stride (floats): 32 data + 4 pad
+constexpr int kPfKStages = 3;  // K tiles need ~2 tiles of lead, V tiles get it from the pipeline
+constexpr int kPfVStages = 2;
 constexpr uint32_t kPfOffQ = 0;
 constexpr uint32_t kPfOffK = kPfOffQ + kPfQBytes;
-constexpr uint32_t kPfOffV = kPfOffK + 2 * kPfKVStage;
-constexpr uint32_t kPfOffOut = kPfOffV + 2 * kPfKVStage;
-constexpr uint32_t kPfOffBar = kPfOffOut + 4 * 32 * kPfOutRowF * 4;
+constexpr uint32_t kPfOffV = kPfOffK + kPfKStages * kPfKVStage;
+constexpr uint32_t kPfOffBar = kPfOffV + kPfVStages * kPfKVStage;
 constexpr uint32_t kPfOffRed = kPfOffBar + 256;
-constexpr uint32_t kPfSmem = kPfOffRed + 4096 + 1024;  // + alignment slack
+// row-max exchange: bf16 [2 parity][2 half][128] (1 KB); row sums fp32 [2 half][128] (1 KB)
+constexpr uint32_t kPfSmem = kPfOffRed + 2048;  // 231,680 B: needs a 1024-aligned base (checked)
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemQ = 0;
 constexpr uint32_t kTmemS = 128;
@@ -822,37 +823,45 @@ __device__ __forceinline__ PfUnit pf_unit(const PrefillParams &p, int idx) {
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_fa_sm100(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const PrefillParams p) {
-    extern __shared__ unsigned char smem_raw[];
-    unsigned char *sm = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // The 128-byte-swizzled TMA / MMA tiles need 1024-byte alignment and the
+    // layout uses all of the 227 KB, so there is no room to realign: refuse
+    // to run (status bit, no memory touched) if the base is not aligned.
+    if (smem_u32(smem_raw) & 1023u) {
+        if (threadIdx.x == 0) atomicOr(p.err, kErrBadIndex);
+        return;
+    }
+    unsigned char *sm = smem_raw;
     unsigned char *sQ = sm + kPfOffQ;
     unsigned char *sK = sm + kPfOffK;
     unsigned char *sV = sm + kPfOffV;
-    float *red = reinterpret_cast<float *>(sm + kPfOffRed);  // [2 parity][2 half][128] maxima, then [2 unit parity][2 half][128] sums
+    __nv_bfloat16 *redm = reinterpret_cast<__nv_bfloat16 *>(sm + kPfOffRed);  // [2 parity][2 half][128] maxima
+    float *reds = reinterpret_cast<float *>(sm + kPfOffRed + 1024);             // [2 half][128] row sums
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kPfOffBar);
     uint64_t *q_smem = bars + 0;    // Q tile landed in staging (TMA)
-    uint64_t *k_full = bars + 1;    // [2]
-    uint64_t *k_empty = bars + 3;   // [2]
-    uint64_t *v_full = bars + 5;    // [2]
-    uint64_t *v_empty = bars + 7;   // [2]
-    uint64_t *s_full = bars + 9;
-    uint64_t *s_free = bars + 10;   // 256 arrivals
-    uint64_t *p_full = bars + 11;   // [2], 256 arrivals
-    uint64_t *p_empty = bars + 13;  // [2]
-    uint64_t *mma_done = bars + 15;
-    uint64_t *mma_done_pv = bars + 16;
-    uint64_t *q_tmem = bars + 17;   // Q copied into TMEM; staging free
-    uint64_t *red_bar = bars + 18;  // [2], 256 arrivals
-    uint64_t *fin_bar = bars + 20;  // 256 arrivals, once per unit
-    uint64_t *o_free = bars + 21;   // 128 arrivals: the epilogue warps have read O
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 22);
-    volatile int *s_abort = reinterpret_cast<volatile int *>(bars + 23);
+    uint64_t *k_full = bars + 1;    // [3]
+    uint64_t *k_empty = bars + 4;   // [3]
+    uint64_t *v_full = bars + 7;    // [2]
+    uint64_t *v_empty = bars + 9;   // [2]
+    uint64_t *s_full = bars + 11;
+    uint64_t *s_free = bars + 12;   // 256 arrivals
+    uint64_t *p_full = bars + 13;   // [2], 256 arrivals
+    uint64_t *p_empty = bars + 15;  // [2]
+    uint64_t *mma_done = bars + 17;
+    uint64_t *mma_done_pv = bars + 18;
+    uint64_t *q_tmem = bars + 19;   // Q copied into TMEM; staging free
+    uint64_t *red_bar = bars + 20;  // [2], 256 arrivals
+    uint64_t *fin_bar = bars + 22;  // 256 arrivals, once per unit
+    uint64_t *o_free = bars + 23;   // 128 arrivals: the epilogue warps have read O
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 24);
+    volatile int *s_abort = reinterpret_cast<volatile int *>(bars + 25);
 
     if (threadIdx.x == 0) G3_TRACE(7, 0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nunits = p.nqb * kKvHeads;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < 22; ++i) mbar_init(&bars[i], 1);
+        for (int i = 0; i < 24; ++i) mbar_init(&bars[i], 1);
         mbar_init(s_free, kPfSoftmaxThreads);
         for (int b = 0; b < 2; ++b) {
             mbar_init(&p_full[b], kPfSoftmaxThreads);
@@ -902,16 +911,17 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 const int nxt = next_unit(k);
                 G3_TRACE(3, ukc);
                 for (int i = 0; i < u.ntiles; ++i, ++gi) {
-                    const int s = gi & 1, n = gi >> 1;
+                    const int sk = gi % kPfKStages, nk = gi / kPfKStages;
+                    const int sv = gi % kPfVStages, nv = gi / kPfVStages;
                     const int krow = (u.j0 + i) * 64;
-                    if (n >= 1 && !mbar_wait(&k_empty[s], (n - 1) & 1, p.err)) { *s_abort = 1; break; }
-                    mbar_expect_tx(&k_full[s], kPfKVStage);
+                    if (nk >= 1 && !mbar_wait(&k_empty[sk], (nk - 1) & 1, p.err)) { *s_abort = 1; break; }
+                    mbar_expect_tx(&k_full[sk], kPfKVStage);
                     for (int c = 0; c < 4; ++c)
-                        tma_load_3d(sK + s * kPfKVStage + c * 8192, &tmK, 64 * c, krow, u.g, &k_full[s]);
-                    if (n >= 1 && !mbar_wait(&v_empty[s], (n - 1) & 1, p.err)) { *s_abort = 1; break; }
-                    mbar_expect_tx(&v_full[s], kPfKVStage);
+                        tma_load_3d(sK + sk * kPfKVStage + c * 8192, &tmK, 64 * c, krow, u.g, &k_full[sk]);
+                    if (nv >= 1 && !mbar_wait(&v_empty[sv], (nv - 1) & 1, p.err)) { *s_abort = 1; break; }
+                    mbar_expect_tx(&v_full[sv], kPfKVStage);
                     for (int c = 0; c < 4; ++c)
-                        tma_load_3d(sV + s * kPfKVStage + c * 8192, &tmV, 64 * c, krow, u.g, &v_full[s]);
+                        tma_load_3d(sV + sv * kPfKVStage + c * 8192, &tmV, 64 * c, krow, u.g, &v_full[sv]);
                     if (i == 0 && nxt >= 0) {
                         if (!mbar_wait(q_tmem, ukc & 1, p.err)) { *s_abort = 1; break; }
                         load_q(nxt);
@@ -945,8 +955,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 tc_commit(q_tmem);
                 for (int i = 0; i < u.ntiles; ++i, ++gi) {
                     if (*s_abort) { ok = false; break; }
-                    const int s = gi & 1;
-                    if (!mbar_wait(&k_full[s], (gi >> 1) & 1, p.err)) { ok = false; break; }
+                    const int s = gi % kPfKStages;
+                    if (!mbar_wait(&k_full[s], (gi / kPfKStages) & 1, p.err)) { ok = false; break; }
                     // the single S buffer is free once the softmax has read the last one
                     if (gi >= 1 && !mbar_wait(s_free, (gi - 1) & 1, p.err)) { ok = false; break; }
                     tc_fence_after();
@@ -979,9 +989,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 const int ukc = uk++;
                 for (int i = 0; i < u.ntiles; ++i, ++gi) {
                     if (*s_abort) { ok = false; break; }
-                    const int su = gi & 1, pb = gi & 1;
+                    const int su = gi % kPfVStages, pb = gi & 1;
                     if (!mbar_wait(&p_full[pb], (gi >> 1) & 1, p.err)) { ok = false; break; }
-                    if (!mbar_wait(&v_full[su], (gi >> 1) & 1, p.err)) { ok = false; break; }
+                    if (!mbar_wait(&v_full[su], (gi / kPfVStages) & 1, p.err)) { ok = false; break; }
                     G3_TRACE(1, gi);
                     // the first PV of a unit overwrites O: the previous unit's
                     // epilogue must have read it
@@ -1003,12 +1013,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     } else if (warp >= kPfWarpEpi) {
         // ------------------------------------------------ epilogue warps
         // O / (l_half0 + l_half1) -> out[t][2g+hh][:]: one warp per TMEM lane
-        // quadrant, thread = row, 32 columns at a time through this warp's
-        // staging rows, stored 128 contiguous bytes per 8 lanes.
+        // quadrant, thread = row, 32 columns at a time.
         const int quad = warp & 3;
         const int row = quad * 32 + lane;
         const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
-        float *stage = reinterpret_cast<float *>(sm + kPfOffOut) + (warp - kPfWarpEpi) * 32 * kPfOutRowF;
         bool ok = true;
         int gi = 0, uk = 0;
         for (int k = 0; ok && k < pf_unit_rounds(nunits); ++k) {
@@ -1024,7 +1032,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 break;
             }
             tc_fence_after();
-            const float lt = red[512 + (ukc & 1) * 256 + row] + red[512 + (ukc & 1) * 256 + 128 + row];
+            const float lt = reds[row] + reds[128 + row];
             const float inv = lt > 0.f ? 1.0f / lt : 0.f;
             const int nvalid = min(64, p.T - u.t0);
 #pragma unroll 1
@@ -1037,25 +1045,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     tc_fence_before();
                     mbar_arrive(o_free);
                 }
-                float *srow = stage + lane * kPfOutRowF;
+                // this thread's row: 128 contiguous bytes (off the critical path)
+                if ((row & 63) < nvalid) {
+                    float *dst = p.out + ((size_t)(u.t0 + (row & 63)) * kHeads + 2 * u.g + (row >> 6)) * kHeadDim + cc * 32;
 #pragma unroll
-                for (int k4 = 0; k4 < 32; k4 += 4)
-                    *reinterpret_cast<float4 *>(srow + k4) =
-                        make_float4(o[k4] * inv, o[k4 + 1] * inv, o[k4 + 2] * inv, o[k4 + 3] * inv);
-                __syncwarp();
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const int e = j * 32 + lane;
-                    const int rl = e >> 3, c4 = e & 7;  // row within the quadrant, float4 within 32 columns
-                    const int rr = quad * 32 + rl;      // tile row
-                    if ((rr & 63) < nvalid) {
-                        const float4 v4 = *reinterpret_cast<const float4 *>(stage + rl * kPfOutRowF + c4 * 4);
-                        float *dst = p.out + ((size_t)(u.t0 + (rr & 63)) * kHeads + 2 * u.g + (rr >> 6)) * kHeadDim +
-                                     cc * 32 + c4 * 4;
-                        *reinterpret_cast<float4 *>(dst) = v4;
-                    }
+                    for (int k4 = 0; k4 < 32; k4 += 4)
+                        *reinterpret_cast<float4 *>(dst + k4) =
+                            make_float4(o[k4] * inv, o[k4 + 1] * inv, o[k4 + 2] * inv, o[k4 + 3] * inv);
                 }
-                __syncwarp();
             }
         }
         if (!ok) *s_abort = 1;
@@ -1106,14 +1103,16 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 #pragma unroll
                     for (int k = 0; k < 32; ++k) mx = fmaxf(mx, x[k]);
                 }
-                mx *= kScaleLog2;
-                red[(pb * 2 + half) * 128 + row] = mx;
+                // exchanged in bf16 rounded up: both halves then use the same
+                // value, not below the true max (P stays <= 2^kRescaleLog2)
+                const __nv_bfloat16 mine = __float2bfloat16_ru(mx * kScaleLog2);
+                redm[(pb * 2 + half) * 128 + row] = mine;
                 mbar_arrive(&red_bar[pb]);
                 if (!__all_sync(0xffffffffu, mbar_wait(&red_bar[pb], (gi >> 1) & 1, p.err))) {
                     ok = false;
                     break;
                 }
-                mx = fmaxf(mx, red[(pb * 2 + (half ^ 1)) * 128 + row]);
+                mx = fmaxf(__bfloat162float(mine), __bfloat162float(redm[(pb * 2 + (half ^ 1)) * 128 + row]));
                 const bool raise = mx > m + kRescaleLog2;  // false while the row has no valid key
                 const float m_new = raise ? mx : m;
                 const float alpha = raise ? ex2_approx(m - m_new) : 1.f;
@@ -1170,15 +1169,15 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 mbar_arrive(&p_full[pb]);
             }
             if (!ok) break;
-            // ---- hand the unit to the epilogue warps: this half's row sum,
-            // double-buffered by unit parity.  Stay at most one unit ahead of
-            // the epilogue (its barriers count phases by parity).
+            // ---- hand the unit to the epilogue warps: this half's row sum.
+            // Stay at most one unit ahead of the epilogue: its barriers count
+            // phases by parity, and it reads the sums before releasing O.
             if (threadIdx.x == 0) G3_TRACE(5, ukc);
             if (ukc >= 1 && !__all_sync(0xffffffffu, mbar_wait(o_free, (ukc - 1) & 1, p.err))) {
                 ok = false;
                 break;
             }
-            red[512 + (ukc & 1) * 256 + half * 128 + row] = l;
+            reds[half * 128 + row] = l;  // read by the epilogue before it releases O
             mbar_arrive(fin_bar);
         }
         if (!ok) *s_abort = 1;
@@ -1189,10 +1188,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     if (warp == kPfWarpTma && lane == 0 && *s_abort) {
         // Let in-flight TMA copies land before the CTA's shared memory goes.
         mbar_wait(q_smem, 0, nullptr);
-        for (int s = 0; s < 2; ++s) {
-            mbar_wait(&k_full[s], 0, nullptr);
-            mbar_wait(&v_full[s], 0, nullptr);
-        }
+        for (int s = 0; s < kPfKStages; ++s) mbar_wait(&k_full[s], 0, nullptr);
+        for (int s = 0; s < kPfVStages; ++s) mbar_wait(&v_full[s], 0, nullptr);
     }
     __syncthreads();
     if (warp == kPfWarpMma) {
