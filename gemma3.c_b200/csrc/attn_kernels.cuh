@@ -855,6 +855,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     uint64_t *o_free = bars + 23;   // 128 arrivals: the epilogue warps have read O
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 24);
     volatile int *s_abort = reinterpret_cast<volatile int *>(bars + 25);
+    uint64_t *epi_bar = bars + 26;   // 128 arrivals: epilogue-internal steps (3 per unit)
+    uint64_t *epi_done = bars + 27;  // 128 arrivals: epilogue done with the Q staging
 
     if (threadIdx.x == 0) G3_TRACE(7, 0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -869,6 +871,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
         mbar_init(fin_bar, kPfSoftmaxThreads);
         mbar_init(o_free, 128);
+        mbar_init(epi_bar, 128);
+        mbar_init(epi_done, 128);
         *s_abort = 0;
         fence_mbar_init();
     }
@@ -922,8 +926,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     mbar_expect_tx(&v_full[sv], kPfKVStage);
                     for (int c = 0; c < 4; ++c)
                         tma_load_3d(sV + sv * kPfKVStage + c * 8192, &tmV, 64 * c, krow, u.g, &v_full[sv]);
-                    if (i == 0 && nxt >= 0) {
+                    // prefetch the next unit's Q into the staging once this
+                    // unit's Q is in TMEM and the previous unit's epilogue
+                    // has stopped using the staging for its output
+                    if (i == min(2, u.ntiles - 1) && nxt >= 0) {
                         if (!mbar_wait(q_tmem, ukc & 1, p.err)) { *s_abort = 1; break; }
+                        if (ukc >= 1 && !mbar_wait(epi_done, (ukc - 1) & 1, p.err)) { *s_abort = 1; break; }
                         load_q(nxt);
                     }
                 }
@@ -1012,13 +1020,30 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
     } else if (warp >= kPfWarpEpi) {
         // ------------------------------------------------ epilogue warps
-        // O / (l_half0 + l_half1) -> out[t][2g+hh][:]: one warp per TMEM lane
-        // quadrant, thread = row, 32 columns at a time.
+        // O / (l_half0 + l_half1) -> out[t][2g+hh][:], one warp per TMEM lane
+        // quadrant, thread = row.  Staged through the Q staging buffer (free
+        // once the next unit's Q is in TMEM) in two 128-column halves, so the
+        // stores are coalesced and O is released to the next unit right after
+        // the second half has been read from TMEM.  Staging: [128 rows][32
+        // 16-byte chunks], chunk c of row r at slot c ^ (r & 7).
         const int quad = warp & 3;
         const int row = quad * 32 + lane;
+        const int et = threadIdx.x - kPfWarpEpi * 32;  // 0..127
         const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
+        float4 *stage = reinterpret_cast<float4 *>(sQ);
+        auto next_unit = [&](int k) {
+            for (++k; k < pf_unit_rounds(nunits); ++k)
+                if (pf_unit_index(k, nunits) >= 0) return true;
+            return false;
+        };
         bool ok = true;
-        int gi = 0, uk = 0;
+        int gi = 0, uk = 0, eph = 0;
+        auto epi_sync = [&]() {
+            mbar_arrive(epi_bar);
+            const bool w = mbar_wait(epi_bar, eph & 1, p.err);
+            ++eph;
+            return __all_sync(0xffffffffu, w);
+        };
         for (int k = 0; ok && k < pf_unit_rounds(nunits); ++k) {
             const int idx = pf_unit_index(k, nunits);
             if (idx < 0) continue;
@@ -1026,34 +1051,52 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             const int ukc = uk++;
             gi += u.ntiles;
             const int gl = gi - 1;  // the unit's last tile
+            const bool more = next_unit(k);
+            // the staging still holds the next unit's Q until it is in TMEM
             if (!__all_sync(0xffffffffu, !*s_abort && mbar_wait(fin_bar, ukc & 1, p.err) &&
-                                             mbar_wait(&p_empty[gl & 1], (gl >> 1) & 1, p.err))) {
+                                             mbar_wait(&p_empty[gl & 1], (gl >> 1) & 1, p.err) &&
+                                             (!more || mbar_wait(q_tmem, (ukc + 1) & 1, p.err)))) {
                 ok = false;
                 break;
             }
             tc_fence_after();
+            fence_proxy_async_smem();  // the staging was last touched by TMA / tcgen05.cp
             const float lt = reds[row] + reds[128 + row];
             const float inv = lt > 0.f ? 1.0f / lt : 0.f;
             const int nvalid = min(64, p.T - u.t0);
+            for (int hc = 0; ok && hc < 2; ++hc) {
 #pragma unroll 1
-            for (int cc = 0; cc < 8; ++cc) {
-                float o[32];
-                tmem_ld32(lane_base + kTmemO + cc * 32, o);
-                tc_wait_ld();
-                if (cc == 7) {
-                    // all of O read from TMEM: the next unit's PV may overwrite it
-                    tc_fence_before();
-                    mbar_arrive(o_free);
-                }
-                // this thread's row: 128 contiguous bytes (off the critical path)
-                if ((row & 63) < nvalid) {
-                    float *dst = p.out + ((size_t)(u.t0 + (row & 63)) * kHeads + 2 * u.g + (row >> 6)) * kHeadDim + cc * 32;
+                for (int cc = 0; cc < 4; ++cc) {
+                    float o[32];
+                    tmem_ld32(lane_base + kTmemO + hc * 128 + cc * 32, o);
+                    tc_wait_ld();
+                    if (hc == 1 && cc == 3) {
+                        // all of O read from TMEM: the next unit's PV may overwrite it
+                        tc_fence_before();
+                        mbar_arrive(o_free);
+                    }
 #pragma unroll
-                    for (int k4 = 0; k4 < 32; k4 += 4)
-                        *reinterpret_cast<float4 *>(dst + k4) =
-                            make_float4(o[k4] * inv, o[k4 + 1] * inv, o[k4 + 2] * inv, o[k4 + 3] * inv);
+                    for (int k4 = 0; k4 < 8; ++k4) {
+                        const int c = cc * 8 + k4;
+                        stage[row * 32 + (c ^ (row & 7))] =
+                            make_float4(o[4 * k4] * inv, o[4 * k4 + 1] * inv, o[4 * k4 + 2] * inv, o[4 * k4 + 3] * inv);
+                    }
                 }
+                if (!epi_sync()) { ok = false; break; }
+                // 128 threads store 128 rows x 512 B; a warp covers one row's 512 contiguous bytes
+                for (int f = et; f < 128 * 32; f += 128) {
+                    const int r = f >> 5, c = f & 31;
+                    if ((r & 63) < nvalid) {
+                        float *dst = p.out + ((size_t)(u.t0 + (r & 63)) * kHeads + 2 * u.g + (r >> 6)) * kHeadDim +
+                                     hc * 128 + c * 4;
+                        *reinterpret_cast<float4 *>(dst) = stage[r * 32 + (c ^ (r & 7))];
+                    }
+                }
+                if (hc == 0 && !epi_sync()) { ok = false; break; }
             }
+            if (!ok) break;
+            fence_proxy_async_smem();  // our staging reads before the next Q's TMA write
+            mbar_arrive(epi_done);     // the staging is free for the next Q
         }
         if (!ok) *s_abort = 1;
     } else {
