@@ -273,6 +273,8 @@ __global__ void __launch_bounds__(512) prologue_decode(const float *__restrict__
                                                        const float *__restrict__ V, LayerDev L, float eps,
                                                        const __grid_constant__ DecodeRows rows,
                                                        float *__restrict__ qout) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int b = blockIdx.x, y = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pos = rows.pos[b], seq = rows.seq[b];
     const float *rope_row = L.rope + (size_t)pos * kHeadDim;
@@ -378,6 +380,9 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
     const KVT *Kp = plane<KVT>(p.L, seq, 0, g) + (size_t)r0 * kHeadDim;
     const KVT *Vp = plane<KVT>(p.L, seq, 1, g) + (size_t)r0 * kHeadDim;
 
+    // Dependent launch: the next kernel may start its set-up now; this one
+    // touches global memory only after the previous kernel has completed.
+    pdl_launch_dependents();
     if (threadIdx.x == 0) {
         s_abort = 0;
         for (int s = 0; s < NS; ++s) {
@@ -387,6 +392,7 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
         fence_mbar_init();
     }
     __syncthreads();
+    pdl_wait();
 
     // q and fresh-row buffers of the fused prologue live after the ring.
     float(*qsm)[kHeadDim] = reinterpret_cast<float(*)[kHeadDim]>(smem + 2 * NS * kPlaneTile);
@@ -674,6 +680,8 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
 __global__ void __launch_bounds__(256) merge_partials(const float *__restrict__ partials, int nparts, size_t bstride,
                                                       size_t hstride, size_t pstride, float *__restrict__ out,
                                                       float *__restrict__ emit) {
+    pdl_launch_dependents();
+    pdl_wait();
     const int b = blockIdx.x / kHeads, h = blockIdx.x % kHeads, d = threadIdx.x;
     const float *base = partials + (size_t)b * bstride + (size_t)h * hstride;
     float M = -INFINITY;

@@ -13,6 +13,7 @@
 #include <dlfcn.h>
 
 #include <mutex>
+#include <utility>
 
 #include <algorithm>
 #include <cmath>
@@ -113,6 +114,25 @@ static int make_map(CUtensorMap *m, const void *base, int rows, size_t plane_str
                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "cuTensorMapEncodeTiled failed (%d)", (int)r);
     return 0;
+}
+
+// Launch with programmatic stream serialization: the kernel may begin while
+// the previous kernel of the stream drains; the decode-path kernels call
+// griddepcontrol.wait before touching memory another kernel writes.
+template <typename... KArgs, typename... Args>
+static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 // ------------------------------------------------------------------ context
@@ -575,7 +595,8 @@ static int decode_impl(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_id
     const bool fused = pl.chunk < 2048;
     g3::DecodeParams p;
     if (!fused) {
-        g3::prologue_decode<KVT><<<B, 512, 0, ctx->stream>>>(Q, K, V, L, ctx->cfg.rmsnorm_eps, pl.rows, ctx->qdec);
+        launch_pdl(g3::prologue_decode<KVT>, dim3(B), dim3(512), 0, ctx->stream, Q, K, V, L, ctx->cfg.rmsnorm_eps,
+                   pl.rows, ctx->qdec);
         if (int r = check_launch(ctx, 1)) return r;
     }
     p.q = fused ? nullptr : ctx->qdec;
@@ -599,9 +620,11 @@ static int decode_impl(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_id
     size_t e0;
     prof_begin(ctx, &e0);
     if (fused)
-        g3::decode_splitkv<KVT, true><<<dim3(pl.nsplit, kKvHeads, B), 256, smem, ctx->stream>>>(p, pl.rows);
+        launch_pdl(g3::decode_splitkv<KVT, true>, dim3(pl.nsplit, kKvHeads, B), dim3(256), smem, ctx->stream, p,
+                   pl.rows);
     else
-        g3::decode_splitkv<KVT, false><<<dim3(pl.nsplit, kKvHeads, B), 256, smem, ctx->stream>>>(p, pl.rows);
+        launch_pdl(g3::decode_splitkv<KVT, false>, dim3(pl.nsplit, kKvHeads, B), dim3(256), smem, ctx->stream, p,
+                   pl.rows);
     if (ctx->prof) {
         // algorithmic bytes: every attended K and V row once
         double rows = 0;
@@ -611,8 +634,8 @@ static int decode_impl(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_id
     if (int r = check_launch(ctx, 1)) return r;
     if (p.write_partial && !p.tickets) {
         const size_t hs = (size_t)pl.nsplit * kPartialStride;
-        g3::merge_partials<<<B * kHeads, 256, 0, ctx->stream>>>(ctx->partial, pl.nsplit, kHeads * hs, hs,
-                                                                 kPartialStride, out, partial_out);
+        launch_pdl(g3::merge_partials, dim3(B * kHeads), dim3(256), 0, ctx->stream, (const float *)ctx->partial,
+                   pl.nsplit, (size_t)(kHeads * hs), hs, (size_t)kPartialStride, out, partial_out);
         if (int r = check_launch(ctx, 1)) return r;
     }
     return 0;

@@ -27,6 +27,14 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
     return t;
 }
 
+// Programmatic dependent launch: let the next kernel of the stream start
+// launching now / wait until the previous kernel of the stream has completed
+// and its memory is visible (a no-op when launched without the attribute).
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t smem_u32(const void *p) {
     return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
