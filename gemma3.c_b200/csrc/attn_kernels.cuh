@@ -1250,6 +1250,20 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 }
 
 // ------------------------------------------------------------------------
+// Self-test of the bounded-wait path: one thread waits on an mbarrier that
+// nothing ever arrives on.  The wait gives up after kWaitLimitNs, sets
+// kErrWaitTimeout in *err and the kernel returns normally.
+// ------------------------------------------------------------------------
+__global__ void wait_timeout_probe(unsigned *err) {
+    __shared__ uint64_t never;
+    if (threadIdx.x == 0) {
+        mbar_init(&never, 1);
+        fence_mbar_init();
+        mbar_wait(&never, 0, err);
+    }
+}
+
+// ------------------------------------------------------------------------
 // Utility kernels: seeded N(0,1) fill, host-layout import/export.
 // ------------------------------------------------------------------------
 __device__ __forceinline__ uint64_t splitmix64(uint64_t x) {

@@ -822,6 +822,15 @@ extern "C" int gemma3_cuda_fill_cache_random(gemma3_cuda_ctx *ctx, int layer, in
     return 0;
 }
 
+// ------------------------------------------------------------------ failure-path self-test
+extern "C" int gemma3_cuda_selftest_wait_timeout(gemma3_cuda_ctx *ctx) {
+    if (!ctx) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null context");
+    CU_TRY(cudaSetDevice(ctx->cfg.device));
+    g3::wait_timeout_probe<<<1, 32, 0, ctx->stream>>>(ctx->err);
+    if (int r = check_launch(ctx, 1)) return r;
+    return gemma3_cuda_synchronize(ctx);  // expected: GEMMA3_CUDA_ERR_GENERATION_FAILED
+}
+
 // ------------------------------------------------------------------ profiling
 extern "C" int gemma3_cuda_profile(gemma3_cuda_ctx *ctx, int enable) {
     if (!ctx) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null context");

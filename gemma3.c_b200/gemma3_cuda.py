@@ -101,6 +101,7 @@ SIGNATURES = {
     "gemma3_cuda_profile_read": (_I, [_P, _I, ctypes.POINTER(ctypes.c_longlong), ctypes.POINTER(ctypes.c_double),
                                       ctypes.POINTER(ctypes.c_double)]),
     "gemma3_cuda_gqa_decode_noalloc": (_I, [_P, _P, _I, _I, _I, _IP, _P, _P]),
+    "gemma3_cuda_selftest_wait_timeout": (_I, [_P]),
     "gemma3_cuda_last_error": (ctypes.c_char_p, []),
 }
 
@@ -210,6 +211,10 @@ class Context:
 
     def launch_count(self) -> int:
         return int(self.lib.gemma3_cuda_launch_count(self.h))
+
+    def selftest_wait_timeout(self) -> int:
+        """Runs the bounded-wait failure path; returns the C return code."""
+        return self.lib.gemma3_cuda_selftest_wait_timeout(self.h)
 
     def profile(self, enable: bool):
         self._chk(self.lib.gemma3_cuda_profile(self.h, int(enable)))

@@ -223,6 +223,14 @@ int gemma3_cuda_gqa_decode_noalloc(const float *q, const void *kv, int kv_dtype,
                                    int rows, int B, const int *nrows, float *out,
                                    void *stream);
 
+/* Test hook for failure detection (no counterpart in the reference, which
+ * has no device code): runs a kernel whose bounded wait can never complete.
+ * After the wait limit (about 2 s) the kernel sets the context's status word
+ * and returns; this call then reports GEMMA3_CUDA_ERR_GENERATION_FAILED
+ * ("bounded wait timed out"), clears the status, and the context remains
+ * usable for further calls. */
+int gemma3_cuda_selftest_wait_timeout(gemma3_cuda_ctx *ctx);
+
 /* Text of the last failure on this thread ("" if none). */
 const char *gemma3_cuda_last_error(void);
 

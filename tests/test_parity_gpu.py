@@ -264,3 +264,21 @@ def test_prefill_8192_many_units_per_cta(ropes, layer):
     want = want.view(T, 2048).cpu().numpy()
     assert np.isfinite(got).all()
     assert rel_err(got, want) <= TOL, rel_err(got, want)
+
+
+def test_bounded_wait_times_out_and_context_survives(ropes):
+    """A device wait that can never complete gives up after its limit, the
+    call reports GENERATION_FAILED with the timeout text, and the same
+    context then runs a normal decode correctly."""
+    import time
+    ctx = make_ctx(ropes, max_context=1024, max_prefill=64)
+    t0 = time.time()
+    rc = ctx.selftest_wait_timeout()
+    dt = time.time() - t0
+    assert rc == gc.ERR_GENERATION_FAILED
+    assert "timed out" in ctx.last_error()
+    assert 1.0 < dt < 30.0
+    Q, K, V = qkv(5, 1)
+    out = ctx.attn_decode(0, [0], [0], Q, K, V)  # position 0 attends only itself: out == v
+    assert np.allclose(out.reshape(8, 256), V.reshape(4, 256)[np.arange(8) // 2], atol=1e-5)
+    ctx.close()
