@@ -927,13 +927,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     const int sv = gi % kPfVStages, nv = gi / kPfVStages;
                     const int krow = (u.j0 + i) * 64;
                     if (nk >= 1 && !mbar_wait(&k_empty[sk], (nk - 1) & 1, p.err)) { *s_abort = 1; break; }
+                    // one 32 KB box per stage: [4 dim-blocks][64 keys][128 B] (a TMA
+                    // instruction has a near-fixed issue cost, so fewer larger boxes
+                    // stream faster than one box per 64-dim block)
                     mbar_expect_tx(&k_full[sk], kPfKVStage);
-                    for (int c = 0; c < 4; ++c)
-                        tma_load_3d(sK + sk * kPfKVStage + c * 8192, &tmK, 64 * c, krow, u.g, &k_full[sk]);
+                    tma_load_4d(sK + sk * kPfKVStage, &tmK, 0, krow, 0, u.g, &k_full[sk]);
                     if (nv >= 1 && !mbar_wait(&v_empty[sv], (nv - 1) & 1, p.err)) { *s_abort = 1; break; }
                     mbar_expect_tx(&v_full[sv], kPfKVStage);
-                    for (int c = 0; c < 4; ++c)
-                        tma_load_3d(sV + sv * kPfKVStage + c * 8192, &tmV, 64 * c, krow, u.g, &v_full[sv]);
+                    tma_load_4d(sV + sv * kPfKVStage, &tmV, 0, krow, 0, u.g, &v_full[sv]);
                     // prefetch the next unit's Q into the staging once this
                     // unit's Q is in TMEM and the previous unit's epilogue
                     // has stopped using the staging for its output

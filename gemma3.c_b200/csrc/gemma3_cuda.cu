@@ -116,6 +116,22 @@ static int make_map(CUtensorMap *m, const void *base, int rows, size_t plane_str
     return 0;
 }
 
+// The same fp16 planes viewed as 4-D {64 dims, rows, 4 dim-blocks, planes}:
+// one box of {64, box_rows, 4} lands in shared memory as [block][row][64
+// dims], each 128-byte row swizzled - the layout of the kernel's K/V stages.
+static int make_map4(CUtensorMap *m, const void *base, int rows, size_t plane_stride_elems, int planes,
+                     int box_rows) {
+    cuuint64_t dims[4] = {64, (cuuint64_t)rows, (cuuint64_t)(kHeadDim / 64), (cuuint64_t)planes};
+    cuuint64_t strides[3] = {(cuuint64_t)kHeadDim * 2, 128, (cuuint64_t)plane_stride_elems * 2};
+    cuuint32_t box[4] = {64, (cuuint32_t)box_rows, (cuuint32_t)(kHeadDim / 64), 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void *>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return 0;
+}
+
 // Launch with programmatic stream serialization: the kernel may begin while
 // the previous kernel of the stream drains; the decode-path kernels call
 // griddepcontrol.wait before touching memory another kernel writes.
@@ -451,8 +467,8 @@ static int prefill_impl(gemma3_cuda_ctx *ctx, int layer, int seq, const float *Q
     CUtensorMap tq, tk, tv;
     const size_t plane = (size_t)ctx->st_rows * kHeadDim;
     if (int r = make_map(&tq, ctx->qst, T, (size_t)T * kHeadDim, kHeads)) return r;
-    if (int r = make_map(&tk, ctx->kst, lrows, plane, kKvHeads)) return r;
-    if (int r = make_map(&tv, ctx->vst, lrows, plane, kKvHeads)) return r;
+    if (int r = make_map4(&tk, ctx->kst, lrows, plane, kKvHeads, 64)) return r;
+    if (int r = make_map4(&tv, ctx->vst, lrows, plane, kKvHeads, 64)) return r;
     g3::PrefillParams p;
     p.out = out;
     p.T = T;
