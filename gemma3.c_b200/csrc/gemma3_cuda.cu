@@ -25,6 +25,7 @@
 
 #include "../../include/gemma3_cuda.h"
 #include "attn_kernels.cuh"
+#include "proj_kernels.cuh"
 
 using g3::kHeadDim;
 using g3::kHeads;
@@ -158,6 +159,8 @@ struct LayerState {
     int is_global = 0;
     uint16_t *qn = nullptr, *kn = nullptr;
     int use_norm = 0;
+    __half *wqkv = nullptr;  // fp16 [4096][2560]: Wq rows 0-2047, Wk 2048-3071, Wv 3072-4095
+    __half *wo = nullptr;    // fp16 [2560][2048]
 };
 
 struct gemma3_cuda_ctx {
@@ -178,6 +181,15 @@ struct gemma3_cuda_ctx {
     float *partial = nullptr;  // [max_batch][8][kMaxSplit][258]
     float *emit = nullptr;     // [max_batch][8][258]
     float *gather = nullptr;   // [kv_ranks][max_batch][8][258]
+    // projection scratch (allocated on first use), rows = tokens
+    __half *xb = nullptr;  // [rows][2560] layer input in fp16
+    __half *ab = nullptr;  // [rows][2048] attention output in fp16
+    float *qkv = nullptr;         // q [rows][2048] | k [rows][1024] | v [rows][1024]
+    float *attn = nullptr;        // [rows][2048]
+    float *xio = nullptr;         // [rows][2560] x / out of the host-pointer layer calls
+    int proj_rows = 0;
+    float *pp = nullptr;          // split-K partials
+    size_t pp_floats = 0;
     // device copies for the host-pointer entry points
     float *io = nullptr;
     size_t io_rows = 0;
@@ -242,7 +254,15 @@ static void ctx_release(gemma3_cuda_ctx *c) {
         cudaFree(L.kv);
         cudaFree(L.qn);
         cudaFree(L.kn);
+        cudaFree(L.wqkv);
+        cudaFree(L.wo);
     }
+    cudaFree(c->xb);
+    cudaFree(c->ab);
+    cudaFree(c->qkv);
+    cudaFree(c->attn);
+    cudaFree(c->xio);
+    cudaFree(c->pp);
     cudaFree(c->rope_local);
     cudaFree(c->rope_global);
     cudaFree(c->qst);
@@ -298,6 +318,7 @@ static int ctx_alloc(gemma3_cuda_ctx *c) {
     CU_TRY(cudaMalloc(&c->err, sizeof(unsigned)));
     CU_TRY(cudaMemsetAsync(c->err, 0, sizeof(unsigned), c->stream));
     CU_TRY(cudaFuncSetAttribute(g3::prefill_fa_sm100, cudaFuncAttributeMaxDynamicSharedMemorySize, g3::kPfSmem));
+    CU_TRY(cudaFuncSetAttribute(g3::proj_gemm_sm100, cudaFuncAttributeMaxDynamicSharedMemorySize, g3::kProjSmem));
     const int dsm_bf = g3::DecodeCfg<__nv_bfloat16>::NS * 2 * g3::DecodeCfg<__nv_bfloat16>::TK * kHeadDim * 2;
     const int dsm_f = g3::DecodeCfg<float>::NS * 2 * g3::DecodeCfg<float>::TK * kHeadDim * 4;
     CU_TRY(cudaFuncSetAttribute(g3::decode_splitkv<__nv_bfloat16, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -715,6 +736,224 @@ extern "C" int gemma3_cuda_attn_decode(gemma3_cuda_ctx *ctx, int layer, int B, c
     CU_TRY(cudaMemcpyAsync(dv, V, (size_t)B * 1024 * 4, cudaMemcpyHostToDevice, ctx->stream));
     if (int r = gemma3_cuda_attn_decode_dev(ctx, layer, B, seq_ids, pos, dq, dk, dv, dout)) return r;
     CU_TRY(cudaMemcpyAsync(out, dout, (size_t)B * 2048 * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return gemma3_cuda_synchronize(ctx);
+}
+
+// ------------------------------------------------------------------ projections
+// Q/K/V and O projections of layer_attention (gemma3_transformer.c:290-292,
+// :355) and of the batched prefill (:614-639, :694-699) on the tensor cores:
+// BF16 weights resident in HBM, the activations rounded to BF16 once, fp32
+// accumulation (kernels in proj_kernels.cuh).
+static constexpr int kHidden = 2560;
+static constexpr int kQSize = kHeads * kHeadDim;     // 2048
+static constexpr int kKvSize = kKvHeads * kHeadDim;  // 1024
+static constexpr int kQkvRows = kQSize + 2 * kKvSize;
+
+static int proj_scratch(gemma3_cuda_ctx *c, int rows) {
+    if (c->proj_rows >= rows) return 0;
+    cudaFree(c->xb);
+    cudaFree(c->ab);
+    cudaFree(c->qkv);
+    cudaFree(c->attn);
+    cudaFree(c->xio);
+    c->xb = c->ab = nullptr;
+    c->qkv = c->attn = c->xio = nullptr;
+    c->proj_rows = 0;
+    CU_TRY(cudaMalloc(&c->xb, (size_t)rows * kHidden * 2));
+    CU_TRY(cudaMalloc(&c->ab, (size_t)rows * kQSize * 2));
+    CU_TRY(cudaMalloc(&c->qkv, (size_t)rows * kQkvRows * 4));
+    CU_TRY(cudaMalloc(&c->attn, (size_t)rows * kQSize * 4));
+    CU_TRY(cudaMalloc(&c->xio, (size_t)rows * kHidden * 4 * 2));
+    c->proj_rows = rows;
+    return 0;
+}
+
+// fp16 matrix [rows][cols] (row-major), box 64 columns x box_rows rows, 128-byte swizzle.
+static int make_map_f16(CUtensorMap *m, const void *base, int rows, int cols, int box_rows) {
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return 0;
+}
+
+// Y[T][N] = X[T][K] . W[N][K]^T, routed by `out`.  xb: fp16 [T][K] (device).
+static int proj_run(gemma3_cuda_ctx *ctx, const __half *W, int N, int K, const __half *xb, int T,
+                    const g3::ProjOut &out) {
+    const int nt = std::min(256, (T + 31) / 32 * 32);  // the epilogue reads 32 tokens per tcgen05.ld
+    const int ntile_tok = (T + nt - 1) / nt;
+    const int mtiles = N / 128, kchunks = K / 64;
+    const int tiles = mtiles * ntile_tok;
+    // too few tiles to keep every SM streaming weights: split K (each split
+    // at least two 64-wide chunks, none empty)
+    int splits = 1;
+    if (tiles < ctx->sm_count) {
+        splits = std::min((ctx->sm_count + tiles - 1) / tiles, std::max(1, kchunks / 2));
+        const int kper = (kchunks + splits - 1) / splits;
+        splits = (kchunks + kper - 1) / kper;
+    }
+    if (splits > 1) {
+        const size_t need = (size_t)splits * T * N;
+        if (ctx->pp_floats < need) {
+            cudaFree(ctx->pp);
+            ctx->pp = nullptr;
+            ctx->pp_floats = 0;
+            CU_TRY(cudaMalloc(&ctx->pp, need * 4));
+            ctx->pp_floats = need;
+        }
+    }
+    CUtensorMap tw, tx;
+    if (int r = make_map_f16(&tw, W, N, K, 128)) return r;
+    if (int r = make_map_f16(&tx, xb, T, K, nt)) return r;
+    g3::ProjParams p;
+    p.T = T;
+    p.N = N;
+    p.kchunks = kchunks;
+    p.nt = nt;
+    p.splits = splits;
+    p.ntile_tok = ntile_tok;
+    p.out = out;
+    p.partial = ctx->pp;
+    p.err = ctx->err;
+    const int grid = std::min(tiles * splits, ctx->sm_count);
+    size_t e0;
+    prof_begin(ctx, &e0);
+    g3::proj_gemm_sm100<<<grid, g3::kProjThreads, g3::kProjSmem, ctx->stream>>>(tw, tx, p);
+    if (int r = check_launch(ctx, 1)) return r;
+    if (splits > 1) {
+        const size_t n = (size_t)T * N;
+        const int blocks = (int)std::min<size_t>((n + 255) / 256, (size_t)ctx->sm_count * 8);
+        g3::proj_splitk_reduce<<<blocks, 256, 0, ctx->stream>>>(ctx->pp, splits, T, N, out);
+        if (int r = check_launch(ctx, 1)) return r;
+    }
+    prof_end(ctx, 2, e0, 2.0 * T * N * K);
+    return 0;
+}
+
+static int to_f16(gemma3_cuda_ctx *ctx, const float *x, __half *y, size_t n) {
+    const size_t n4 = n / 4;
+    const int blocks = (int)std::min<size_t>((n4 + 255) / 256, (size_t)ctx->sm_count * 8);
+    g3::to_f16_rows<<<blocks, 256, 0, ctx->stream>>>(x, y, n4, ctx->err);
+    return check_launch(ctx, 1);
+}
+
+static int proj_check(gemma3_cuda_ctx *ctx, int layer, int T) {
+    if (!ctx || layer < 0 || layer >= ctx->cfg.num_layers) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad layer");
+    const int maxT = std::max(ctx->cfg.max_prefill, ctx->cfg.max_batch);
+    if (T <= 0 || T > maxT) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad token count %d (max %d)", T, maxT);
+    if (!ctx->layers[layer].wqkv) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "projection weights of layer %d not set", layer);
+    CU_TRY(cudaSetDevice(ctx->cfg.device));
+    return proj_scratch(ctx, maxT);
+}
+
+// BF16 (the reference's stored weights) -> fp16 on the host: exact for
+// |w| >= 2^-14, subnormal below (absolute error < 2^-24); a weight beyond the
+// fp16 range is refused.
+static int bf16_rows_to_f16(const uint16_t *src, size_t n, std::vector<__half> &dst) {
+    dst.resize(n);
+    for (size_t i = 0; i < n; ++i) {
+        uint32_t u = (uint32_t)src[i] << 16;
+        float f;
+        memcpy(&f, &u, 4);
+        if (!(fabsf(f) <= 65504.f)) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "weight %g outside the fp16 range", f);
+        dst[i] = __float2half_rn(f);
+    }
+    return 0;
+}
+
+extern "C" int gemma3_cuda_set_proj_weights(gemma3_cuda_ctx *ctx, int layer, const uint16_t *wq, const uint16_t *wk,
+                                            const uint16_t *wv, const uint16_t *wo) {
+    if (!ctx || layer < 0 || layer >= ctx->cfg.num_layers) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad layer");
+    if (!wq || !wk || !wv || !wo) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null weight");
+    CU_TRY(cudaSetDevice(ctx->cfg.device));
+    std::vector<__half> h;
+    LayerState &L = ctx->layers[layer];
+    if (!L.wqkv) CU_TRY(cudaMalloc(&L.wqkv, (size_t)kQkvRows * kHidden * 2));
+    if (!L.wo) CU_TRY(cudaMalloc(&L.wo, (size_t)kHidden * kQSize * 2));
+    const struct { const uint16_t *src; size_t n; __half *dst; } parts[4] = {
+        {wq, (size_t)kQSize * kHidden, L.wqkv},
+        {wk, (size_t)kKvSize * kHidden, L.wqkv + (size_t)kQSize * kHidden},
+        {wv, (size_t)kKvSize * kHidden, L.wqkv + (size_t)(kQSize + kKvSize) * kHidden},
+        {wo, (size_t)kHidden * kQSize, L.wo},
+    };
+    for (const auto &pt : parts) {
+        if (int r = bf16_rows_to_f16(pt.src, pt.n, h)) return r;
+        CU_TRY(cudaMemcpy(pt.dst, h.data(), pt.n * 2, cudaMemcpyHostToDevice));
+    }
+    return 0;
+}
+
+extern "C" int gemma3_cuda_project_qkv_dev(gemma3_cuda_ctx *ctx, int layer, int T, const float *x, float *q, float *k,
+                                           float *v) {
+    if (int r = proj_check(ctx, layer, T)) return r;
+    if (!x || !q || !k || !v) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null buffer");
+    if (int r = to_f16(ctx, x, ctx->xb, (size_t)T * kHidden)) return r;
+    g3::ProjOut o;
+    o.ptr[0] = q;
+    o.ptr[1] = k;
+    o.ptr[2] = v;
+    o.ld[0] = kQSize;
+    o.ld[1] = o.ld[2] = kKvSize;
+    o.lo[0] = 0;
+    o.lo[1] = kQSize;
+    o.lo[2] = kQSize + kKvSize;
+    o.lo[3] = kQkvRows;
+    return proj_run(ctx, ctx->layers[layer].wqkv, kQkvRows, kHidden, ctx->xb, T, o);
+}
+
+extern "C" int gemma3_cuda_project_o_dev(gemma3_cuda_ctx *ctx, int layer, int T, const float *attn, float *out) {
+    if (int r = proj_check(ctx, layer, T)) return r;
+    if (!attn || !out) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null buffer");
+    if (int r = to_f16(ctx, attn, ctx->ab, (size_t)T * kQSize)) return r;
+    g3::ProjOut o;
+    o.ptr[0] = o.ptr[1] = o.ptr[2] = out;
+    o.ld[0] = o.ld[1] = o.ld[2] = kHidden;
+    o.lo[0] = 0;
+    o.lo[1] = o.lo[2] = o.lo[3] = kHidden;
+    return proj_run(ctx, ctx->layers[layer].wo, kHidden, kQSize, ctx->ab, T, o);
+}
+
+extern "C" int gemma3_cuda_layer_decode_dev(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_ids,
+                                            const int *pos, const float *x, float *out) {
+    if (int r = proj_check(ctx, layer, B)) return r;
+    float *q = ctx->qkv, *k = q + (size_t)ctx->proj_rows * kQSize, *v = k + (size_t)ctx->proj_rows * kKvSize;
+    if (int r = gemma3_cuda_project_qkv_dev(ctx, layer, B, x, q, k, v)) return r;
+    if (int r = gemma3_cuda_attn_decode_dev(ctx, layer, B, seq_ids, pos, q, k, v, ctx->attn)) return r;
+    return gemma3_cuda_project_o_dev(ctx, layer, B, ctx->attn, out);
+}
+
+extern "C" int gemma3_cuda_layer_decode(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_ids, const int *pos,
+                                        const float *x, float *out) {
+    if (int r = proj_check(ctx, layer, B)) return r;
+    if (!x || !out) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null buffer");
+    float *dx = ctx->xio, *dout = dx + (size_t)ctx->proj_rows * kHidden;
+    CU_TRY(cudaMemcpyAsync(dx, x, (size_t)B * kHidden * 4, cudaMemcpyHostToDevice, ctx->stream));
+    if (int r = gemma3_cuda_layer_decode_dev(ctx, layer, B, seq_ids, pos, dx, dout)) return r;
+    CU_TRY(cudaMemcpyAsync(out, dout, (size_t)B * kHidden * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return gemma3_cuda_synchronize(ctx);
+}
+
+extern "C" int gemma3_cuda_layer_prefill_dev(gemma3_cuda_ctx *ctx, int layer, int seq, const float *x, int T,
+                                             int start_pos, float *out) {
+    if (int r = proj_check(ctx, layer, T)) return r;
+    float *q = ctx->qkv, *k = q + (size_t)ctx->proj_rows * kQSize, *v = k + (size_t)ctx->proj_rows * kKvSize;
+    if (int r = gemma3_cuda_project_qkv_dev(ctx, layer, T, x, q, k, v)) return r;
+    if (int r = gemma3_cuda_attn_prefill_dev(ctx, layer, seq, q, k, v, T, start_pos, ctx->attn)) return r;
+    return gemma3_cuda_project_o_dev(ctx, layer, T, ctx->attn, out);
+}
+
+extern "C" int gemma3_cuda_layer_prefill(gemma3_cuda_ctx *ctx, int layer, int seq, const float *x, int T,
+                                         int start_pos, float *out) {
+    if (int r = proj_check(ctx, layer, T)) return r;
+    if (!x || !out) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null buffer");
+    float *dx = ctx->xio, *dout = dx + (size_t)ctx->proj_rows * kHidden;
+    CU_TRY(cudaMemcpyAsync(dx, x, (size_t)T * kHidden * 4, cudaMemcpyHostToDevice, ctx->stream));
+    if (int r = gemma3_cuda_layer_prefill_dev(ctx, layer, seq, dx, T, start_pos, dout)) return r;
+    CU_TRY(cudaMemcpyAsync(out, dout, (size_t)T * kHidden * 4, cudaMemcpyDeviceToHost, ctx->stream));
     return gemma3_cuda_synchronize(ctx);
 }
 

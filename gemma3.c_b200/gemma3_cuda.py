@@ -36,6 +36,7 @@ HEAD_DIM = 256
 WINDOW = 1024
 Q_SIZE = N_HEADS * HEAD_DIM
 KV_SIZE = N_KV * HEAD_DIM
+HIDDEN = 2560  # Gemma 3 4B hidden size (gemma3.h)
 PARTIAL_STRIDE = HEAD_DIM + 2
 
 
@@ -102,6 +103,13 @@ SIGNATURES = {
                                       ctypes.POINTER(ctypes.c_double)]),
     "gemma3_cuda_gqa_decode_noalloc": (_I, [_P, _P, _I, _I, _I, _IP, _P, _P]),
     "gemma3_cuda_selftest_wait_timeout": (_I, [_P]),
+    "gemma3_cuda_set_proj_weights": (_I, [_P, _I, _U16P, _U16P, _U16P, _U16P]),
+    "gemma3_cuda_project_qkv_dev": (_I, [_P, _I, _I, _P, _P, _P, _P]),
+    "gemma3_cuda_project_o_dev": (_I, [_P, _I, _I, _P, _P]),
+    "gemma3_cuda_layer_decode": (_I, [_P, _I, _I, _IP, _IP, _FP, _FP]),
+    "gemma3_cuda_layer_decode_dev": (_I, [_P, _I, _I, _IP, _IP, _P, _P]),
+    "gemma3_cuda_layer_prefill": (_I, [_P, _I, _I, _FP, _I, _I, _FP]),
+    "gemma3_cuda_layer_prefill_dev": (_I, [_P, _I, _I, _P, _I, _I, _P]),
     "gemma3_cuda_last_error": (ctypes.c_char_p, []),
 }
 
@@ -262,6 +270,48 @@ class Context:
             out = np.empty((B, Q_SIZE), dtype=np.float32)
         self._chk(self.lib.gemma3_cuda_attn_decode(self.h, layer, B, sp, pp, _fptr(Q), _fptr(K), _fptr(V), _fptr(out)))
         return out
+
+    # -- projections and whole-layer attention ----------------------------
+    def set_proj_weights(self, layer: int, wq, wk, wv, wo):
+        """BF16 (uint16) [2048][2560], [1024][2560], [1024][2560], [2560][2048]."""
+        ws = [np.ascontiguousarray(w, dtype=np.uint16) for w in (wq, wk, wv, wo)]
+        shapes = [(Q_SIZE, HIDDEN), (KV_SIZE, HIDDEN), (KV_SIZE, HIDDEN), (HIDDEN, Q_SIZE)]
+        for w, shp in zip(ws, shapes):
+            if w.shape != shp:
+                raise ValueError(f"weight shape {w.shape}, expected {shp}")
+        self._chk(self.lib.gemma3_cuda_set_proj_weights(self.h, layer, *[w.ctypes.data_as(_U16P) for w in ws]))
+
+    def project_qkv_dev(self, layer, T, x_ptr, q_ptr, k_ptr, v_ptr):
+        self._chk(self.lib.gemma3_cuda_project_qkv_dev(self.h, layer, T, x_ptr, q_ptr, k_ptr, v_ptr))
+
+    def project_o_dev(self, layer, T, attn_ptr, out_ptr):
+        self._chk(self.lib.gemma3_cuda_project_o_dev(self.h, layer, T, attn_ptr, out_ptr))
+
+    def layer_decode(self, layer, seq_ids, pos, x, out=None):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        B = len(seq_ids)
+        s, sp = _iarr(seq_ids)
+        p, pp = _iarr(pos)
+        if out is None:
+            out = np.empty((B, HIDDEN), dtype=np.float32)
+        self._chk(self.lib.gemma3_cuda_layer_decode(self.h, layer, B, sp, pp, _fptr(x), _fptr(out)))
+        return out
+
+    def layer_decode_dev(self, layer, seq_ids, pos, x_ptr, out_ptr):
+        s, sp = _iarr(seq_ids)
+        p, pp = _iarr(pos)
+        self._chk(self.lib.gemma3_cuda_layer_decode_dev(self.h, layer, len(s), sp, pp, x_ptr, out_ptr))
+
+    def layer_prefill(self, layer, seq, x, start_pos, out=None):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        T = x.shape[0]
+        if out is None:
+            out = np.empty((T, HIDDEN), dtype=np.float32)
+        self._chk(self.lib.gemma3_cuda_layer_prefill(self.h, layer, seq, _fptr(x), T, start_pos, _fptr(out)))
+        return out
+
+    def layer_prefill_dev(self, layer, seq, x_ptr, T, start_pos, out_ptr):
+        self._chk(self.lib.gemma3_cuda_layer_prefill_dev(self.h, layer, seq, x_ptr, T, start_pos, out_ptr))
 
     # -- hot path (device pointers, enqueue only) -------------------------
     def attn_prefill_dev(self, layer, seq, q_ptr, k_ptr, v_ptr, T, start_pos, out_ptr):

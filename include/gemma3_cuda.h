@@ -138,6 +138,52 @@ int gemma3_cuda_attn_decode_dev(gemma3_cuda_ctx *ctx, int layer, int B,
                                 const float *Q, const float *K, const float *V,
                                 float *out);
 
+/* ---- Q/K/V and O projections (BF16 weights on the tensor cores) -------- */
+
+/* Uploads one layer's projection weights, BF16 [out][in] row-major exactly
+ * as the reference stores them (gemma3_layer_weights.q_proj / k_proj /
+ * v_proj / o_proj, consumed by layer_attention, gemma3_transformer.c:258-356):
+ * wq [2048][2560], wk and wv [1024][2560], wo [2560][2048].  Host pointers;
+ * the device keeps its own copy (about 31 MB per layer). */
+int gemma3_cuda_set_proj_weights(gemma3_cuda_ctx *ctx, int layer,
+                                 const uint16_t *wq, const uint16_t *wk,
+                                 const uint16_t *wv, const uint16_t *wo);
+
+/* Projections of T tokens, all pointers in device memory (enqueues only).
+ * qkv: x [T][2560] (the normed layer input) -> q [T][2048], k [T][1024],
+ * v [T][1024]; replaces the three matvec_bf16_dispatch calls of
+ * gemma3_transformer.c:290-292 (decode) and the three cblas_sgemm calls of
+ * :614-639 (batched prefill).  o: attn [T][2048] -> out [T][2560]; replaces
+ * gemma3_transformer.c:355 and :694-699.  The activations are rounded to
+ * BF16 once, the weights are used as stored, sums accumulate in fp32.
+ * T <= max(max_prefill, max_batch). */
+int gemma3_cuda_project_qkv_dev(gemma3_cuda_ctx *ctx, int layer, int T,
+                                const float *x, float *q, float *k, float *v);
+int gemma3_cuda_project_o_dev(gemma3_cuda_ctx *ctx, int layer, int T,
+                              const float *attn, float *out);
+
+/* The whole of layer_attention (gemma3_transformer.c:258-356) for a batch of
+ * B decode tokens: x [B][2560] -> QKV projections -> QK-norm, RoPE, cache
+ * append, GQA -> O projection -> out [B][2560], without a host round trip
+ * between the steps.  seq_ids / pos as for gemma3_cuda_attn_decode.  The
+ * host-pointer form copies x in and out; _dev takes device pointers and
+ * enqueues only. */
+int gemma3_cuda_layer_decode(gemma3_cuda_ctx *ctx, int layer, int B,
+                             const int *seq_ids, const int *pos,
+                             const float *x, float *out);
+int gemma3_cuda_layer_decode_dev(gemma3_cuda_ctx *ctx, int layer, int B,
+                                 const int *seq_ids, const int *pos,
+                                 const float *x, float *out);
+
+/* Same for T prefill tokens of sequence slot `seq` at positions
+ * start_pos.. (the attention part of one layer of
+ * gemma3_transformer_prefill_batched, gemma3_transformer.c:613-699). */
+int gemma3_cuda_layer_prefill(gemma3_cuda_ctx *ctx, int layer, int seq,
+                              const float *x, int T, int start_pos, float *out);
+int gemma3_cuda_layer_prefill_dev(gemma3_cuda_ctx *ctx, int layer, int seq,
+                                  const float *x, int T, int start_pos,
+                                  float *out);
+
 /* Context-parallel decode on a global layer whose KV range is split across
  * kv_ranks contexts (one per GPU).  Step 1 runs on every rank and writes this
  * rank's log-sum-exp partial for each (sequence, q head) into `partial`
@@ -193,9 +239,10 @@ long long gemma3_cuda_launch_count(gemma3_cuda_ctx *ctx);
 /* Instrumentation (no counterpart in the reference, which has no timers).
  * gemma3_cuda_profile(ctx, 1) starts recording a CUDA event pair around
  * every launch of the two dominant kernels (and clears earlier records);
- * gemma3_cuda_profile_read sums, for kernel 0 = split-KV decode or
- * 1 = tensor-core prefill, the launches, their device time in ms and their
- * algorithmic work: K/V bytes read (decode) or FLOPs (prefill). */
+ * gemma3_cuda_profile_read sums, for kernel 0 = split-KV decode,
+ * 1 = tensor-core prefill or 2 = projection GEMM (with its split-K
+ * reduction), the launches, their device time in ms and their algorithmic
+ * work: K/V bytes read (decode) or FLOPs (prefill, projections). */
 int gemma3_cuda_profile(gemma3_cuda_ctx *ctx, int enable);
 int gemma3_cuda_profile_read(gemma3_cuda_ctx *ctx, int kernel, long long *launches,
                              double *ms, double *work);
