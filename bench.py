@@ -460,6 +460,65 @@ def secondary_decode1(args, torch, gc, pk, dev):
     return {"workload": "configs[1] global-layer decode, B=1, 8192 keys, L2 flushed between calls", **res}
 
 
+def secondary_projections(args, torch, gc, pk, dev):
+    """Q/K/V + O projections (fp16 tcgen05 GEMM): configs[2]'s T=8192 prefill
+    block (tensor-bound) and configs[3]'s B=64 decode batch (weight-streaming,
+    HBM-bound).  Eight layers of weights (252 MB, more than L2) are used in
+    turn so the decode figure streams weights from HBM."""
+    NL = 8
+    T = 8192
+    ctx = gc.Context(max_context=1024, max_batch=64, kv_dtype=gc.KV_BF16, device=dev, max_prefill=T, num_layers=NL)
+    gen = torch.Generator().manual_seed(5)
+
+    def w(shape):
+        return (torch.randn(*shape, generator=gen) * 0.02).to(torch.bfloat16).view(torch.int16).numpy().view("uint16")
+
+    for l in range(NL):
+        ctx.set_proj_weights(l, w((gc.Q_SIZE, gc.HIDDEN)), w((gc.KV_SIZE, gc.HIDDEN)), w((gc.KV_SIZE, gc.HIDDEN)),
+                             w((gc.HIDDEN, gc.Q_SIZE)))
+    d = f"cuda:{dev}"
+    x = torch.randn(T, gc.HIDDEN, device=d)
+    a = torch.randn(T, gc.Q_SIZE, device=d)
+    q = torch.empty(T, gc.Q_SIZE, device=d)
+    k = torch.empty(T, gc.KV_SIZE, device=d)
+    v = torch.empty(T, gc.KV_SIZE, device=d)
+    o = torch.empty(T, gc.HIDDEN, device=d)
+    stream = torch.cuda.ExternalStream(ctx.stream, device=d)
+    res = {}
+    for name, rows in (("prefill_T8192", T), ("decode_B64", 64)):
+        def step():
+            for l in range(NL):
+                ctx.project_qkv_dev(l, rows, x.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr())
+                ctx.project_o_dev(l, rows, a.data_ptr(), o.data_ptr())
+        for _ in range(3):
+            step()
+        ctx.synchronize()
+        reps = 3 if rows == T else 20
+        ctx.profile(True)
+        ms = ev_time(torch, stream, lambda: [step() for _ in range(reps)])
+        ctx.synchronize()
+        n, kms, flops = ctx.profile_read(2)
+        ctx.profile(False)
+        calls = reps * NL
+        wbytes = (gc.Q_SIZE + 2 * gc.KV_SIZE) * gc.HIDDEN * 2 + gc.HIDDEN * gc.Q_SIZE * 2
+        if rows == T:
+            tf = flops / (kms / 1e3) / 1e12
+            res[name] = {"gflop_per_layer": round(flops / calls / 1e9, 1), "us_per_layer": round(ms / calls * 1e3, 1),
+                         "roofline": {"bound": "tensor", "kernel": "proj_gemm_sm100 (fp16 tcgen05, fp32 acc)",
+                                      "achieved": round(tf, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                                      "frac": round(tf / pk["bf16_tflops"], 4)}}
+        else:
+            gbs = wbytes * calls / (kms / 1e3) / 1e9
+            res[name] = {"weight_mb_per_layer": round(wbytes / 1e6, 1), "us_per_layer": round(ms / calls * 1e3, 2),
+                         "roofline": {"bound": "hbm", "kernel": "proj_gemm_sm100 + split-K reduce",
+                                      "achieved": round(gbs, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                                      "frac": round(gbs / pk["hbm_gbs"], 4)}}
+    ctx.close()
+    del x, a, q, k, v, o
+    torch.cuda.empty_cache()
+    return {"workload": "Q/K/V + O projections, 8 layers of fp16 weights in turn", **res}
+
+
 def secondary_context_parallel(args, dist, torch, gc, pk):
     """B=4 sequences at 131,072 keys, BF16 KV; the 5 global layers'
     KV range is split over the N ranks (partials merged with an NCCL
@@ -623,7 +682,8 @@ def main():
     if dist.rank == 0 and dist.world == 1:
         if not args.no_secondary:
             line["secondary"] = {"prefill": secondary_prefill(args, torch, gc, pk, dist.local),
-                                 "decode_b1": secondary_decode1(args, torch, gc, pk, dist.local)}
+                                 "decode_b1": secondary_decode1(args, torch, gc, pk, dist.local),
+                                 "projections": secondary_projections(args, torch, gc, pk, dist.local)}
     if not args.no_secondary:
         line.setdefault("secondary", {})["context_parallel"] = cp
         if not args.no_cpu_baseline:

@@ -788,13 +788,22 @@ static int proj_run(gemma3_cuda_ctx *ctx, const __half *W, int N, int K, const _
     const int ntile_tok = (T + nt - 1) / nt;
     const int mtiles = N / 128, kchunks = K / 64;
     const int tiles = mtiles * ntile_tok;
-    // too few tiles to keep every SM streaming weights: split K (each split
-    // at least two 64-wide chunks, none empty)
+    // Too few tiles to keep every SM busy (decode): split K.  The split count
+    // minimises the busiest SM's work in 64-wide K chunks, (tiles per SM) x
+    // (chunks per tile + 2 for writing and reducing a tile's partial sums),
+    // preferring fewer splits on ties; no split is empty.
     int splits = 1;
     if (tiles < ctx->sm_count) {
-        splits = std::min((ctx->sm_count + tiles - 1) / tiles, std::max(1, kchunks / 2));
-        const int kper = (kchunks + splits - 1) / splits;
-        splits = (kchunks + kper - 1) / kper;
+        long best = kchunks;  // one split: every tile does all chunks
+        for (int sp = 2; sp <= kchunks; ++sp) {
+            const int kper = (kchunks + sp - 1) / sp;
+            const int eff = (kchunks + kper - 1) / kper;
+            const long cost = (long)((tiles * eff + ctx->sm_count - 1) / ctx->sm_count) * (kper + 2);
+            if (cost < best) {
+                best = cost;
+                splits = eff;
+            }
+        }
     }
     if (splits > 1) {
         const size_t need = (size_t)splits * T * N;

@@ -61,8 +61,9 @@ struct ProjParams {
 };
 
 __device__ __forceinline__ float *proj_dst(const ProjOut &o, int t, int f) {
-    const int s = f < o.lo[1] ? 0 : (f < o.lo[2] ? 1 : 2);
-    return o.ptr[s] + (size_t)t * o.ld[s] + (f - o.lo[s]);
+    if (f < o.lo[1]) return o.ptr[0] + (size_t)t * o.ld[0] + (f - o.lo[0]);
+    if (f < o.lo[2]) return o.ptr[1] + (size_t)t * o.ld[1] + (f - o.lo[1]);
+    return o.ptr[2] + (size_t)t * o.ld[2] + (f - o.lo[2]);
 }
 
 __global__ void __launch_bounds__(kProjThreads, 1)
@@ -192,22 +193,34 @@ __global__ void __launch_bounds__(kProjThreads, 1)
                 break;
             }
             tc_fence_after();
-            const int f = m * 128 + row;
+            // destination of this tile (a 128-feature tile never straddles the
+            // Q / K / V segments): column f of a row-major [T][ld] array
+            const int f0 = m * 128;
+            float *base;
+            int ld;
+            if (p.splits > 1) {
+                base = p.partial + (size_t)s * p.T * p.N + f0;
+                ld = p.N;
+            } else if (f0 < p.out.lo[1]) {
+                base = p.out.ptr[0] + (f0 - p.out.lo[0]);
+                ld = p.out.ld[0];
+            } else if (f0 < p.out.lo[2]) {
+                base = p.out.ptr[1] + (f0 - p.out.lo[1]);
+                ld = p.out.ld[1];
+            } else {
+                base = p.out.ptr[2] + (f0 - p.out.lo[2]);
+                ld = p.out.ld[2];
+            }
+            float *col = base + row;
             const int t0 = n * p.nt;
             for (int c = 0; c < p.nt / 32; ++c) {
                 float v[32];
                 tmem_ld32(lane_base + b * 256 + c * 32, v);
                 tc_wait_ld();
+                const int tc = t0 + c * 32;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int t = t0 + c * 32 + j;
-                    if (t < p.T) {
-                        if (p.splits > 1)
-                            p.partial[((size_t)s * p.T + t) * p.N + f] = v[j];
-                        else
-                            *proj_dst(p.out, t, f) = v[j];
-                    }
-                }
+                for (int j = 0; j < 32; ++j)
+                    if (tc + j < p.T) col[(size_t)(tc + j) * ld] = v[j];
             }
             tc_fence_before();
             mbar_arrive(&acc_empty[b]);
