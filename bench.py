@@ -57,7 +57,7 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true", help="skip the configs[1]/[2] figures")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile-case", choices=["decode", "prefill"],
+    ap.add_argument("--profile-case", choices=["decode", "prefill", "proj"],
                     help="tiny workload for ncu captures: 3 launches of the kernel, ~1-2 GB on the device")
     ap.add_argument("--seqs", type=int, default=B_TOTAL,
                     help="override the 64 sequences (small cases for ncu captures only)")
@@ -590,7 +590,8 @@ def profile_case(args):
     """Few-launch cases for `ncu --set full` (one GPU, about 1-2 GB resident,
     inputs still larger than L2): decode = global layer, 8 sequences x 32769
     rows (1.07 GB of BF16 KV); prefill = one global and one local layer at
-    T=8192."""
+    T=8192; proj = the Q/K/V projection of a T=8192 block, twice (a
+    302 MB fp16 input / output set)."""
     import torch
     import gemma3_cuda as gc
     import synth
@@ -606,6 +607,22 @@ def profile_case(args):
         o = torch.empty(B, 2048, device="cuda")
         for _ in range(3):
             ctx.attn_decode_dev(5, list(range(B)), [POS] * B, q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr())
+    elif args.profile_case == "proj":
+        T = 8192
+        ctx = gc.Context(max_context=1024, max_batch=1, kv_dtype=gc.KV_BF16, max_prefill=T, num_layers=1)
+        gen = torch.Generator().manual_seed(5)
+
+        def w(shape):
+            return (torch.randn(*shape, generator=gen) * 0.02).to(torch.bfloat16).view(torch.int16).numpy().view(
+                "uint16")
+
+        ctx.set_proj_weights(0, w((2048, 2560)), w((1024, 2560)), w((1024, 2560)), w((2560, 2048)))
+        x = torch.randn(T, 2560, device="cuda")
+        q = torch.empty(T, 2048, device="cuda")
+        k = torch.empty(T, 1024, device="cuda")
+        v = torch.empty(T, 1024, device="cuda")
+        for _ in range(2):
+            ctx.project_qkv_dev(0, T, x.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr())
     else:
         T = 8192
         ctx = gc.Context(max_context=T, max_batch=1, kv_dtype=gc.KV_BF16, max_prefill=T, num_layers=6)

@@ -607,8 +607,10 @@ static void plan_decode(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_i
     // least 4 tiles per CTA; never more than kMaxSplit splits.
     const long long target = 148LL * 8;
     const long long one_wave = 148LL * 2;
-    long long chunk = std::max<long long>(4 * TK, (total + target - 1) / target);
-    chunk = std::max<long long>(chunk, std::min<long long>(512, (total + one_wave - 1) / one_wave));
+    const long long min_rows = 512;
+    const int min_tiles = 4;
+    long long chunk = std::max<long long>((long long)min_tiles * TK, (total + target - 1) / target);
+    chunk = std::max<long long>(chunk, std::min<long long>(min_rows, (total + one_wave - 1) / one_wave));
     chunk = std::max<long long>(chunk, (maxrows + kMaxSplit - 1) / kMaxSplit);
     chunk = (chunk + TK - 1) / TK * TK;
     pl.chunk = (int)chunk;
