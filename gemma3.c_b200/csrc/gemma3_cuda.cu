@@ -26,6 +26,7 @@
 #include "../../include/gemma3_cuda.h"
 #include "attn_kernels.cuh"
 #include "proj_kernels.cuh"
+#include "layer_kernels.cuh"
 
 using g3::kHeadDim;
 using g3::kHeads;
@@ -161,6 +162,12 @@ struct LayerState {
     int use_norm = 0;
     __half *wqkv = nullptr;  // fp16 [4096][2560]: Wq rows 0-2047, Wk 2048-3071, Wv 3072-4095
     __half *wo = nullptr;    // fp16 [2560][2048]
+    // the rest of the transformer block (gemma3_cuda_set_layer_weights)
+    __half *wgu = nullptr;    // fp16 [20480][2560]: gate rows 0-10239, up 10240-20479
+    __half *wdown = nullptr;  // fp16 [2560][10240]
+    uint16_t *ln = nullptr;   // BF16 [4][2560]: input, post-attention, pre-FFN, post-FFN norm gains
+    int ln_set[4] = {0, 0, 0, 0};
+    int block_ready = 0;
 };
 
 struct gemma3_cuda_ctx {
@@ -190,6 +197,14 @@ struct gemma3_cuda_ctx {
     int proj_rows = 0;
     float *pp = nullptr;          // split-K partials
     size_t pp_floats = 0;
+    // transformer-block scratch (allocated on first use)
+    float *gu = nullptr;          // gate [rows][10240] | up [rows][10240]
+    __half *hb = nullptr;         // [rows][10240] gelu(gate) * up
+    float *delta = nullptr;       // [rows][2560] attention / MLP output before its norm
+    float *xfwd = nullptr;        // [rows][2560] residual stream of the host-pointer forward calls
+    int blk_rows = 0;
+    uint16_t *wstage = nullptr;   // BF16 weight staging for the device-side fp16 conversion
+    size_t wstage_elems = 0;
     // device copies for the host-pointer entry points
     float *io = nullptr;
     size_t io_rows = 0;
@@ -256,7 +271,15 @@ static void ctx_release(gemma3_cuda_ctx *c) {
         cudaFree(L.kn);
         cudaFree(L.wqkv);
         cudaFree(L.wo);
+        cudaFree(L.wgu);
+        cudaFree(L.wdown);
+        cudaFree(L.ln);
     }
+    cudaFree(c->gu);
+    cudaFree(c->hb);
+    cudaFree(c->delta);
+    cudaFree(c->xfwd);
+    cudaFree(c->wstage);
     cudaFree(c->xb);
     cudaFree(c->ab);
     cudaFree(c->qkv);
@@ -861,19 +884,20 @@ static int proj_check(gemma3_cuda_ctx *ctx, int layer, int T) {
     return proj_scratch(ctx, maxT);
 }
 
-// BF16 (the reference's stored weights) -> fp16 on the host: exact for
-// |w| >= 2^-14, subnormal below (absolute error < 2^-24); a weight beyond the
-// fp16 range is refused.
-static int bf16_rows_to_f16(const uint16_t *src, size_t n, std::vector<__half> &dst) {
-    dst.resize(n);
-    for (size_t i = 0; i < n; ++i) {
-        uint32_t u = (uint32_t)src[i] << 16;
-        float f;
-        memcpy(&f, &u, 4);
-        if (!(fabsf(f) <= 65504.f)) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "weight %g outside the fp16 range", f);
-        dst[i] = __float2half_rn(f);
+// Host BF16 matrix -> device fp16 (through a staging buffer; the conversion
+// runs on the device, see bf16_to_f16).
+static int upload_f16(gemma3_cuda_ctx *ctx, __half *dst, const uint16_t *src, size_t n) {
+    if (ctx->wstage_elems < n) {
+        cudaFree(ctx->wstage);
+        ctx->wstage = nullptr;
+        ctx->wstage_elems = 0;
+        CU_TRY(cudaMalloc(&ctx->wstage, n * 2));
+        ctx->wstage_elems = n;
     }
-    return 0;
+    CU_TRY(cudaMemcpyAsync(ctx->wstage, src, n * 2, cudaMemcpyHostToDevice, ctx->stream));
+    const int blocks = (int)std::min<size_t>((n + 255) / 256, (size_t)ctx->sm_count * 16);
+    g3::bf16_to_f16<<<blocks, 256, 0, ctx->stream>>>(ctx->wstage, dst, n, ctx->err);
+    return check_launch(ctx, 1);
 }
 
 extern "C" int gemma3_cuda_set_proj_weights(gemma3_cuda_ctx *ctx, int layer, const uint16_t *wq, const uint16_t *wk,
@@ -881,21 +905,15 @@ extern "C" int gemma3_cuda_set_proj_weights(gemma3_cuda_ctx *ctx, int layer, con
     if (!ctx || layer < 0 || layer >= ctx->cfg.num_layers) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad layer");
     if (!wq || !wk || !wv || !wo) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null weight");
     CU_TRY(cudaSetDevice(ctx->cfg.device));
-    std::vector<__half> h;
     LayerState &L = ctx->layers[layer];
     if (!L.wqkv) CU_TRY(cudaMalloc(&L.wqkv, (size_t)kQkvRows * kHidden * 2));
     if (!L.wo) CU_TRY(cudaMalloc(&L.wo, (size_t)kHidden * kQSize * 2));
-    const struct { const uint16_t *src; size_t n; __half *dst; } parts[4] = {
-        {wq, (size_t)kQSize * kHidden, L.wqkv},
-        {wk, (size_t)kKvSize * kHidden, L.wqkv + (size_t)kQSize * kHidden},
-        {wv, (size_t)kKvSize * kHidden, L.wqkv + (size_t)(kQSize + kKvSize) * kHidden},
-        {wo, (size_t)kHidden * kQSize, L.wo},
-    };
-    for (const auto &pt : parts) {
-        if (int r = bf16_rows_to_f16(pt.src, pt.n, h)) return r;
-        CU_TRY(cudaMemcpy(pt.dst, h.data(), pt.n * 2, cudaMemcpyHostToDevice));
-    }
-    return 0;
+    if (int r = upload_f16(ctx, L.wqkv, wq, (size_t)kQSize * kHidden)) return r;
+    if (int r = upload_f16(ctx, L.wqkv + (size_t)kQSize * kHidden, wk, (size_t)kKvSize * kHidden)) return r;
+    if (int r = upload_f16(ctx, L.wqkv + (size_t)(kQSize + kKvSize) * kHidden, wv, (size_t)kKvSize * kHidden))
+        return r;
+    if (int r = upload_f16(ctx, L.wo, wo, (size_t)kHidden * kQSize)) return r;
+    return gemma3_cuda_synchronize(ctx);  // a weight outside the fp16 range fails here
 }
 
 extern "C" int gemma3_cuda_project_qkv_dev(gemma3_cuda_ctx *ctx, int layer, int T, const float *x, float *q, float *k,
@@ -965,6 +983,171 @@ extern "C" int gemma3_cuda_layer_prefill(gemma3_cuda_ctx *ctx, int layer, int se
     CU_TRY(cudaMemcpyAsync(dx, x, (size_t)T * kHidden * 4, cudaMemcpyHostToDevice, ctx->stream));
     if (int r = gemma3_cuda_layer_prefill_dev(ctx, layer, seq, dx, T, start_pos, dout)) return r;
     CU_TRY(cudaMemcpyAsync(out, dout, (size_t)T * kHidden * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return gemma3_cuda_synchronize(ctx);
+}
+
+// ------------------------------------------------------------------ transformer block
+// The whole Gemma 3 block on the device (gemma3_transformer_forward,
+// gemma3_transformer.c:427-499): input norm, attention (projections
+// included), post-attention norm + residual, pre-FFN norm, gated GELU MLP
+// (layer_mlp, :362-398), post-FFN norm + residual; the residual stream stays
+// in device memory across all layers.
+static constexpr int kInter = 10240;  // intermediate_size of Gemma 3 4B
+
+static int block_scratch(gemma3_cuda_ctx *c, int rows) {
+    if (c->blk_rows >= rows) return 0;
+    cudaFree(c->gu);
+    cudaFree(c->hb);
+    cudaFree(c->delta);
+    cudaFree(c->xfwd);
+    c->gu = nullptr;
+    c->hb = nullptr;
+    c->delta = c->xfwd = nullptr;
+    c->blk_rows = 0;
+    CU_TRY(cudaMalloc(&c->gu, (size_t)rows * 2 * kInter * 4));
+    CU_TRY(cudaMalloc(&c->hb, (size_t)rows * kInter * 2));
+    CU_TRY(cudaMalloc(&c->delta, (size_t)rows * kHidden * 4));
+    CU_TRY(cudaMalloc(&c->xfwd, (size_t)rows * kHidden * 4));
+    c->blk_rows = rows;
+    return 0;
+}
+
+extern "C" int gemma3_cuda_set_layer_weights(gemma3_cuda_ctx *ctx, int layer, const gemma3_cuda_layer_weights *w) {
+    if (!ctx || !w || layer < 0 || layer >= ctx->cfg.num_layers) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad layer");
+    if (!w->gate_proj || !w->up_proj || !w->down_proj || !w->input_layernorm)
+        return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null weight");
+    if (int r = gemma3_cuda_set_proj_weights(ctx, layer, w->q_proj, w->k_proj, w->v_proj, w->o_proj)) return r;
+    if (int r = gemma3_cuda_set_qk_norm(ctx, layer, w->q_norm, w->k_norm)) return r;
+    LayerState &L = ctx->layers[layer];
+    L.block_ready = 0;
+    if (!L.wgu) CU_TRY(cudaMalloc(&L.wgu, (size_t)2 * kInter * kHidden * 2));
+    if (!L.wdown) CU_TRY(cudaMalloc(&L.wdown, (size_t)kHidden * kInter * 2));
+    if (!L.ln) CU_TRY(cudaMalloc(&L.ln, (size_t)4 * kHidden * 2));
+    if (int r = upload_f16(ctx, L.wgu, w->gate_proj, (size_t)kInter * kHidden)) return r;
+    if (int r = upload_f16(ctx, L.wgu + (size_t)kInter * kHidden, w->up_proj, (size_t)kInter * kHidden)) return r;
+    if (int r = upload_f16(ctx, L.wdown, w->down_proj, (size_t)kHidden * kInter)) return r;
+    const uint16_t *lns[4] = {w->input_layernorm, w->post_attention_layernorm, w->pre_feedforward_layernorm,
+                              w->post_feedforward_layernorm};
+    for (int i = 0; i < 4; ++i) {
+        L.ln_set[i] = lns[i] ? 1 : 0;  // a missing post / pre-FFN norm is skipped, as the reference does
+        if (lns[i])
+            CU_TRY(cudaMemcpyAsync(L.ln + (size_t)i * kHidden, lns[i], kHidden * 2, cudaMemcpyHostToDevice,
+                                   ctx->stream));
+    }
+    if (int r = gemma3_cuda_synchronize(ctx)) return r;
+    L.block_ready = 1;
+    return 0;
+}
+
+static const uint16_t *ln_of(const LayerState &L, int i) { return L.ln_set[i] ? L.ln + (size_t)i * kHidden : nullptr; }
+
+// x [T][2560] (device, fp32) <- all layers applied to T rows.  attn(l, q, k,
+// v, out) runs the attention core of layer l on the rows.
+template <typename AttnFn>
+static int forward_layers(gemma3_cuda_ctx *ctx, int T, float *x, AttnFn attn) {
+    for (int l = 0; l < ctx->cfg.num_layers; ++l)
+        if (!ctx->layers[l].block_ready)
+            return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "block weights of layer %d not set", l);
+    if (int r = proj_check(ctx, 0, T)) return r;
+    if (int r = block_scratch(ctx, ctx->proj_rows)) return r;
+    const float eps = ctx->cfg.rmsnorm_eps;
+    const int R = ctx->proj_rows;
+    float *q = ctx->qkv, *k = q + (size_t)R * kQSize, *v = k + (size_t)R * kKvSize;
+    float *gate = ctx->gu, *up = ctx->gu + (size_t)R * kInter;
+    // pre-attention norm of layer 0; every later one comes out of the
+    // previous layer's last residual step
+    g3::rms_norm_rows_f16<<<T, g3::kNormThreads, 0, ctx->stream>>>(x, ln_of(ctx->layers[0], 0), ctx->xb, eps,
+                                                                    ctx->err);
+    if (int r = check_launch(ctx, 1)) return r;
+    for (int l = 0; l < ctx->cfg.num_layers; ++l) {
+        const LayerState &L = ctx->layers[l];
+        g3::ProjOut o;
+        o.ptr[0] = q;
+        o.ptr[1] = k;
+        o.ptr[2] = v;
+        o.ld[0] = kQSize;
+        o.ld[1] = o.ld[2] = kKvSize;
+        o.lo[0] = 0;
+        o.lo[1] = kQSize;
+        o.lo[2] = kQSize + kKvSize;
+        o.lo[3] = kQkvRows;
+        if (int r = proj_run(ctx, L.wqkv, kQkvRows, kHidden, ctx->xb, T, o)) return r;
+        if (int r = attn(l, q, k, v, ctx->attn)) return r;
+        if (int r = to_f16(ctx, ctx->attn, ctx->ab, (size_t)T * kQSize)) return r;
+        o.ptr[0] = o.ptr[1] = o.ptr[2] = ctx->delta;
+        o.ld[0] = o.ld[1] = o.ld[2] = kHidden;
+        o.lo[0] = 0;
+        o.lo[1] = o.lo[2] = o.lo[3] = kHidden;
+        if (int r = proj_run(ctx, L.wo, kHidden, kQSize, ctx->ab, T, o)) return r;
+        // x += post_attn_norm(o_proj); xn = pre_ffn_norm(x)
+        g3::residual_norm_rows<<<T, g3::kNormThreads, 0, ctx->stream>>>(ctx->delta, ln_of(L, 1), x, ln_of(L, 2),
+                                                                         ctx->xb, eps, ctx->err);
+        if (int r = check_launch(ctx, 1)) return r;
+        o.ptr[0] = gate;
+        o.ptr[1] = o.ptr[2] = up;
+        o.ld[0] = o.ld[1] = o.ld[2] = kInter;
+        o.lo[0] = 0;
+        o.lo[1] = o.lo[2] = kInter;
+        o.lo[3] = 2 * kInter;
+        if (int r = proj_run(ctx, L.wgu, 2 * kInter, kHidden, ctx->xb, T, o)) return r;
+        {
+            const size_t n = (size_t)T * kInter;
+            // gate and up rows are [T][10240] each, contiguous
+            const int blocks = (int)std::min<size_t>((n + 255) / 256, (size_t)ctx->sm_count * 8);
+            g3::gelu_mul_f16<<<blocks, 256, 0, ctx->stream>>>(gate, up, ctx->hb, n, ctx->err);
+            if (int r = check_launch(ctx, 1)) return r;
+        }
+        o.ptr[0] = o.ptr[1] = o.ptr[2] = ctx->delta;
+        o.ld[0] = o.ld[1] = o.ld[2] = kHidden;
+        o.lo[0] = 0;
+        o.lo[1] = o.lo[2] = o.lo[3] = kHidden;
+        if (int r = proj_run(ctx, L.wdown, kHidden, kInter, ctx->hb, T, o)) return r;
+        // x += post_ffn_norm(mlp); xn = next layer's pre-attention norm(x)
+        const bool last = l + 1 == ctx->cfg.num_layers;
+        g3::residual_norm_rows<<<T, g3::kNormThreads, 0, ctx->stream>>>(
+            ctx->delta, ln_of(L, 3), x, last ? nullptr : ln_of(ctx->layers[l + 1], 0), last ? nullptr : ctx->xb,
+            eps, ctx->err);
+        if (int r = check_launch(ctx, 1)) return r;
+    }
+    return 0;
+}
+
+extern "C" int gemma3_cuda_forward_dev(gemma3_cuda_ctx *ctx, int B, const int *seq_ids, const int *pos, float *x) {
+    if (int r = decode_check(ctx, 0, B, seq_ids, pos)) return r;
+    if (!x) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null buffer");
+    return forward_layers(ctx, B, x, [&](int l, const float *q, const float *k, const float *v, float *out) {
+        return gemma3_cuda_attn_decode_dev(ctx, l, B, seq_ids, pos, q, k, v, out);
+    });
+}
+
+extern "C" int gemma3_cuda_forward(gemma3_cuda_ctx *ctx, int B, const int *seq_ids, const int *pos, float *x) {
+    if (int r = decode_check(ctx, 0, B, seq_ids, pos)) return r;
+    if (!x) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null buffer");
+    if (int r = proj_check(ctx, 0, B)) return r;
+    if (int r = block_scratch(ctx, ctx->proj_rows)) return r;
+    CU_TRY(cudaMemcpyAsync(ctx->xfwd, x, (size_t)B * kHidden * 4, cudaMemcpyHostToDevice, ctx->stream));
+    if (int r = gemma3_cuda_forward_dev(ctx, B, seq_ids, pos, ctx->xfwd)) return r;
+    CU_TRY(cudaMemcpyAsync(x, ctx->xfwd, (size_t)B * kHidden * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return gemma3_cuda_synchronize(ctx);
+}
+
+extern "C" int gemma3_cuda_prefill_forward_dev(gemma3_cuda_ctx *ctx, int seq, float *x, int T, int start_pos) {
+    for (int l = 0; l < ctx->cfg.num_layers; ++l)
+        if (int r = prefill_check(ctx, l, seq, T, start_pos)) return r;
+    if (!x) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null buffer");
+    return forward_layers(ctx, T, x, [&](int l, const float *q, const float *k, const float *v, float *out) {
+        return gemma3_cuda_attn_prefill_dev(ctx, l, seq, q, k, v, T, start_pos, out);
+    });
+}
+
+extern "C" int gemma3_cuda_prefill_forward(gemma3_cuda_ctx *ctx, int seq, float *x, int T, int start_pos) {
+    if (!ctx) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null context");
+    if (!x) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null buffer");
+    if (int r = proj_check(ctx, 0, T)) return r;
+    if (int r = block_scratch(ctx, ctx->proj_rows)) return r;
+    CU_TRY(cudaMemcpyAsync(ctx->xfwd, x, (size_t)T * kHidden * 4, cudaMemcpyHostToDevice, ctx->stream));
+    if (int r = gemma3_cuda_prefill_forward_dev(ctx, seq, ctx->xfwd, T, start_pos)) return r;
+    CU_TRY(cudaMemcpyAsync(x, ctx->xfwd, (size_t)T * kHidden * 4, cudaMemcpyDeviceToHost, ctx->stream));
     return gemma3_cuda_synchronize(ctx);
 }
 

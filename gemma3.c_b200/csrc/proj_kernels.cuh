@@ -261,4 +261,16 @@ __global__ void __launch_bounds__(256) to_f16_rows(const float *__restrict__ x, 
     }
 }
 
+// BF16 weights (as the reference stores them) -> fp16: exact for |w| >= 2^-14,
+// subnormal below (absolute error < 2^-24); a weight beyond the fp16 range
+// sets kErrRange.
+__global__ void __launch_bounds__(256) bf16_to_f16(const uint16_t *__restrict__ src, __half *__restrict__ dst, size_t n,
+                                                   unsigned *err) {
+    for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const float f = __uint_as_float((uint32_t)src[i] << 16);
+        if (!(fabsf(f) <= 65504.f)) atomicOr(err, kErrRange);
+        dst[i] = __float2half_rn(f);
+    }
+}
+
 }  // namespace g3

@@ -76,6 +76,14 @@ _IP = ctypes.POINTER(ctypes.c_int)
 _U16P = ctypes.POINTER(ctypes.c_uint16)
 
 # name -> (restype, argtypes); must cover every function in the header.
+class LayerWeights(ctypes.Structure):
+    """gemma3_cuda_layer_weights: BF16 (uint16) arrays as gemma3_layer_weights holds them."""
+    _fields_ = [(n, ctypes.c_void_p) for n in (
+        "input_layernorm", "q_proj", "k_proj", "v_proj", "o_proj", "q_norm", "k_norm",
+        "post_attention_layernorm", "gate_proj", "up_proj", "down_proj",
+        "pre_feedforward_layernorm", "post_feedforward_layernorm")]
+
+
 SIGNATURES = {
     "gemma3_cuda_config_default": (None, [ctypes.POINTER(Config)]),
     "gemma3_cuda_init": (_P, [ctypes.POINTER(Config)]),
@@ -110,6 +118,11 @@ SIGNATURES = {
     "gemma3_cuda_layer_decode_dev": (_I, [_P, _I, _I, _IP, _IP, _P, _P]),
     "gemma3_cuda_layer_prefill": (_I, [_P, _I, _I, _FP, _I, _I, _FP]),
     "gemma3_cuda_layer_prefill_dev": (_I, [_P, _I, _I, _P, _I, _I, _P]),
+    "gemma3_cuda_set_layer_weights": (_I, [_P, _I, ctypes.POINTER(LayerWeights)]),
+    "gemma3_cuda_forward": (_I, [_P, _I, _IP, _IP, _FP]),
+    "gemma3_cuda_forward_dev": (_I, [_P, _I, _IP, _IP, _P]),
+    "gemma3_cuda_prefill_forward": (_I, [_P, _I, _FP, _I, _I]),
+    "gemma3_cuda_prefill_forward_dev": (_I, [_P, _I, _P, _I, _I]),
     "gemma3_cuda_last_error": (ctypes.c_char_p, []),
 }
 
@@ -312,6 +325,35 @@ class Context:
 
     def layer_prefill_dev(self, layer, seq, x_ptr, T, start_pos, out_ptr):
         self._chk(self.lib.gemma3_cuda_layer_prefill_dev(self.h, layer, seq, x_ptr, T, start_pos, out_ptr))
+
+    # -- whole transformer blocks ---------------------------------------------
+    def set_layer_weights(self, layer: int, **w):
+        """BF16 (uint16) arrays keyed by LayerWeights field name; the three
+        optional norms may be omitted or None."""
+        keep = {k: np.ascontiguousarray(v, dtype=np.uint16) for k, v in w.items() if v is not None}
+        lw = LayerWeights(**{k: v.ctypes.data for k, v in keep.items()})
+        self._chk(self.lib.gemma3_cuda_set_layer_weights(self.h, layer, ctypes.byref(lw)))
+
+    def forward(self, seq_ids, pos, x):
+        """x [B][2560] fp32 residual stream, updated in place (returned)."""
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        s, sp = _iarr(seq_ids)
+        p, pp = _iarr(pos)
+        self._chk(self.lib.gemma3_cuda_forward(self.h, len(s), sp, pp, _fptr(x)))
+        return x
+
+    def prefill_forward(self, seq, x, start_pos):
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        self._chk(self.lib.gemma3_cuda_prefill_forward(self.h, seq, _fptr(x), x.shape[0], start_pos))
+        return x
+
+    def forward_dev(self, seq_ids, pos, x_ptr):
+        s, sp = _iarr(seq_ids)
+        p, pp = _iarr(pos)
+        self._chk(self.lib.gemma3_cuda_forward_dev(self.h, len(s), sp, pp, x_ptr))
+
+    def prefill_forward_dev(self, seq, x_ptr, T, start_pos):
+        self._chk(self.lib.gemma3_cuda_prefill_forward_dev(self.h, seq, x_ptr, T, start_pos))
 
     # -- hot path (device pointers, enqueue only) -------------------------
     def attn_prefill_dev(self, layer, seq, q_ptr, k_ptr, v_ptr, T, start_pos, out_ptr):

@@ -184,6 +184,46 @@ int gemma3_cuda_layer_prefill_dev(gemma3_cuda_ctx *ctx, int layer, int seq,
                                   const float *x, int T, int start_pos,
                                   float *out);
 
+/* ---- Whole transformer blocks on the device ------------------------------ */
+
+/* One layer's weights exactly as gemma3_layer_weights holds them (BF16,
+ * gemma3.h): norm gains [2560] (q_norm / k_norm [256]), projections
+ * [out][in] row-major: q [2048][2560], k / v [1024][2560], o [2560][2048],
+ * gate / up [10240][2560], down [2560][10240].  post_attention_layernorm,
+ * pre_feedforward_layernorm and post_feedforward_layernorm may be NULL (the
+ * reference then skips that norm, gemma3_transformer.c:463,473,492). */
+typedef struct {
+    const uint16_t *input_layernorm;
+    const uint16_t *q_proj, *k_proj, *v_proj, *o_proj;
+    const uint16_t *q_norm, *k_norm;
+    const uint16_t *post_attention_layernorm;
+    const uint16_t *gate_proj, *up_proj, *down_proj;
+    const uint16_t *pre_feedforward_layernorm, *post_feedforward_layernorm;
+} gemma3_cuda_layer_weights;
+
+/* Uploads one layer's weights (about 190 MB of device memory per layer). */
+int gemma3_cuda_set_layer_weights(gemma3_cuda_ctx *ctx, int layer,
+                                  const gemma3_cuda_layer_weights *w);
+
+/* All num_layers blocks of gemma3_transformer_forward (gemma3_transformer.c:
+ * 427-499) for a batch of B decode tokens: x [B][2560] is the residual stream
+ * (the scaled embeddings on entry, the last block's output on return: the
+ * caller applies the final norm and the vocabulary projection).  seq_ids /
+ * pos as for gemma3_cuda_attn_decode.  Host pointer (copied in and out) or,
+ * for _dev, device pointer updated in place (enqueues only). */
+int gemma3_cuda_forward(gemma3_cuda_ctx *ctx, int B, const int *seq_ids,
+                        const int *pos, float *x);
+int gemma3_cuda_forward_dev(gemma3_cuda_ctx *ctx, int B, const int *seq_ids,
+                            const int *pos, float *x);
+
+/* Same for T prompt tokens of sequence slot `seq` at positions
+ * start_pos.. (the layer loop of gemma3_transformer_prefill_batched,
+ * gemma3_transformer.c:601-740): x [T][2560] in / out. */
+int gemma3_cuda_prefill_forward(gemma3_cuda_ctx *ctx, int seq, float *x, int T,
+                                int start_pos);
+int gemma3_cuda_prefill_forward_dev(gemma3_cuda_ctx *ctx, int seq, float *x,
+                                    int T, int start_pos);
+
 /* Context-parallel decode on a global layer whose KV range is split across
  * kv_ranks contexts (one per GPU).  Step 1 runs on every rank and writes this
  * rank's log-sum-exp partial for each (sequence, q head) into `partial`

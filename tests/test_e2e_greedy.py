@@ -1,8 +1,9 @@
 """End-to-end greedy decoding on the random-init 34-layer Gemma-3-4B: the
 reference's own forward pass vs the same model with the attention core on the
 B200 (prompt through gemma3_cuda_attn_prefill, 32 generated tokens through
-gemma3_cuda_attn_decode).  The first 32 tokens must match; the top-1 logits of
-every step must agree within 1e-2 relative (the margins are logged).
+gemma3_cuda_attn_decode), and with every transformer block on the B200.  The
+first 32 tokens must match; the top-1 logits of every step must agree within
+1e-2 relative (the margins are logged).
 Harness: oracle/e2e_harness.c (test infrastructure)."""
 import ctypes
 import os
@@ -38,5 +39,26 @@ def test_greedy_32_steps_match():
     print("reference tokens", ref_t.tolist())
     print("device tokens   ", dev_t.tolist())
     print("min margin", float(ref_m.min()))
+    assert np.array_equal(ref_t, dev_t)
+    assert np.max(np.abs(dev_top - ref_top) / np.abs(ref_top)) <= 1e-2
+
+
+def test_greedy_32_steps_all_blocks_on_device():
+    """The same 32 steps with every transformer block on the device
+    (gemma3_cuda_prefill_forward / gemma3_cuda_forward: projections, norms,
+    residuals, GELU MLP and attention), the host keeping only the embedding
+    lookup, the final norm and the logits."""
+    if not os.path.exists(SO):
+        pytest.skip("e2e harness not built (needs the reference sources at build time)")
+    os.environ.setdefault("OPENBLAS_NUM_THREADS", "1")
+    lib = ctypes.CDLL(SO)
+    lib.e2e_greedy.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_uint64, ctypes.c_int, ctypes.c_int,
+                               ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    ref_t, ref_m, ref_top = _arm(lib, 0)
+    dev_t, dev_m, dev_top = _arm(lib, 2, 0)
+    print("reference tokens", ref_t.tolist())
+    print("device tokens   ", dev_t.tolist())
+    print("min margin", float(ref_m.min()), "max top-1 rel diff",
+          float(np.max(np.abs(dev_top - ref_top) / np.abs(ref_top))))
     assert np.array_equal(ref_t, dev_t)
     assert np.max(np.abs(dev_top - ref_top) / np.abs(ref_top)) <= 1e-2
