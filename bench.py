@@ -519,6 +519,87 @@ def secondary_projections(args, torch, gc, pk, dev):
     return {"workload": "Q/K/V + O projections, 8 layers of fp16 weights in turn", **res}
 
 
+def secondary_model(args, torch, gc, pk, dev):
+    """All 34 transformer blocks on the device (gemma3_cuda_prefill_forward_dev /
+    gemma3_cuda_forward_dev): a T=8192 prompt (configs[2]'s length) and a B=64
+    decode step at 4,096 cached positions per sequence.  One layer's random
+    BF16 weights (N(0, 0.02), norm gains N(0, 0.1)) are uploaded to all 34
+    layers; the embeddings, final norm and logits are outside the timed calls."""
+    T, B, CTXD = 8192, 64, 4096
+    d = f"cuda:{dev}"
+    gen = torch.Generator().manual_seed(11)
+
+    def w(shape, std=0.02):
+        return (torch.randn(*shape, generator=gen) * std).to(torch.bfloat16).view(torch.int16).numpy().view("uint16")
+
+    H, I = gc.HIDDEN, 10240
+    lw = dict(input_layernorm=w((H,), 0.1), q_proj=w((gc.Q_SIZE, H)), k_proj=w((gc.KV_SIZE, H)),
+              v_proj=w((gc.KV_SIZE, H)), o_proj=w((H, gc.Q_SIZE)), q_norm=w((256,), 0.1), k_norm=w((256,), 0.1),
+              post_attention_layernorm=w((H,), 0.1), gate_proj=w((I, H)), up_proj=w((I, H)), down_proj=w((H, I)),
+              pre_feedforward_layernorm=w((H,), 0.1), post_feedforward_layernorm=w((H,), 0.1))
+    ctx = gc.Context(max_context=T, max_batch=B, kv_dtype=gc.KV_BF16, device=dev, max_prefill=T)
+    ctx.upload_rope(gc.rope_table(T, 10000.0), gc.rope_table(T, 1000000.0))
+    for l in range(N_LAYERS):
+        ctx.set_layer_weights(l, **lw)
+    stream = torch.cuda.ExternalStream(ctx.stream, device=d)
+    res = {}
+    # prefill: 34 blocks over 8192 tokens
+    x0 = torch.randn(T, H, device=d)
+    x = torch.empty_like(x0)
+
+    def pstep():
+        x.copy_(x0)
+        ctx.prefill_forward_dev(0, x.data_ptr(), T, 0)
+
+    with torch.cuda.stream(stream):
+        pstep()
+    ctx.synchronize()
+    reps = 2
+    with torch.cuda.stream(stream):
+        ms = ev_time(torch, stream, lambda: [pstep() for _ in range(reps)])
+    ctx.synchronize()
+    attn_flops = 3.243e12
+    proj_flops = N_LAYERS * 2.0 * T * H * (gc.Q_SIZE + 2 * gc.KV_SIZE + gc.Q_SIZE)
+    mlp_flops = N_LAYERS * 2.0 * T * H * 3 * I
+    tot = attn_flops + proj_flops + mlp_flops
+    res["prefill_T8192"] = {"ms": round(ms / reps, 2), "tok_per_s": round(T * reps / (ms / 1e3), 1),
+                            "tflop_per_prompt": round(tot / 1e12, 2),
+                            "tflops": round(tot * reps / (ms / 1e3) / 1e12, 1),
+                            "frac_of_peak": round(tot * reps / (ms / 1e3) / 1e12 / pk["bf16_tflops"], 4)}
+    del x0, x
+    # decode: B=64 tokens at position CTXD over random caches
+    ctx.reset()
+    for l in range(N_LAYERS):
+        for s_ in range(B):
+            ctx.fill_cache_random(l, s_, CTXD if gc.is_global_layer(l) else 1024, 1000 + 97 * l + s_)
+    xd0 = torch.randn(B, H, device=d)
+    xd = torch.empty_like(xd0)
+    seqs, poss = list(range(B)), [CTXD] * B
+
+    def dstep():
+        xd.copy_(xd0)
+        ctx.forward_dev(seqs, poss, xd.data_ptr())
+
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            dstep()
+    ctx.synchronize()
+    reps = 10
+    with torch.cuda.stream(stream):
+        ms = ev_time(torch, stream, lambda: [dstep() for _ in range(reps)])
+    ctx.synchronize()
+    wbytes = N_LAYERS * 2 * (H * (gc.Q_SIZE + 2 * gc.KV_SIZE) + H * gc.Q_SIZE + 3 * H * I)
+    kvbytes = B * (5 * (CTXD + 1) + 29 * 1024) * 4096
+    gbs = (wbytes + kvbytes) * reps / (ms / 1e3) / 1e9
+    res["decode_B64_ctx4096"] = {"ms_per_step": round(ms / reps, 3), "tok_per_s": round(B * reps / (ms / 1e3), 1),
+                                 "weight_gb": round(wbytes / 1e9, 2), "kv_gb": round(kvbytes / 1e9, 2),
+                                 "gbs": round(gbs, 1), "frac_hbm": round(gbs / pk["hbm_gbs"], 4)}
+    ctx.close()
+    del xd0, xd
+    torch.cuda.empty_cache()
+    return {"workload": "34 Gemma-3-4B blocks on the device (attention, projections, norms, GELU MLP)", **res}
+
+
 def secondary_context_parallel(args, dist, torch, gc, pk):
     """B=4 sequences at 131,072 keys, BF16 KV; the 5 global layers'
     KV range is split over the N ranks (partials merged with an NCCL
@@ -700,7 +781,8 @@ def main():
         if not args.no_secondary:
             line["secondary"] = {"prefill": secondary_prefill(args, torch, gc, pk, dist.local),
                                  "decode_b1": secondary_decode1(args, torch, gc, pk, dist.local),
-                                 "projections": secondary_projections(args, torch, gc, pk, dist.local)}
+                                 "projections": secondary_projections(args, torch, gc, pk, dist.local),
+                                 "model": secondary_model(args, torch, gc, pk, dist.local)}
     if not args.no_secondary:
         line.setdefault("secondary", {})["context_parallel"] = cp
         if not args.no_cpu_baseline:

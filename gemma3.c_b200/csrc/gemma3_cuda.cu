@@ -856,12 +856,13 @@ static int proj_run(gemma3_cuda_ctx *ctx, const __half *W, int N, int K, const _
     const int grid = std::min(tiles * splits, ctx->sm_count);
     size_t e0;
     prof_begin(ctx, &e0);
-    g3::proj_gemm_sm100<<<grid, g3::kProjThreads, g3::kProjSmem, ctx->stream>>>(tw, tx, p);
+    CU_TRY(launch_pdl(g3::proj_gemm_sm100, dim3(grid), dim3(g3::kProjThreads), g3::kProjSmem, ctx->stream, tw, tx, p));
     if (int r = check_launch(ctx, 1)) return r;
     if (splits > 1) {
         const size_t n = (size_t)T * N;
         const int blocks = (int)std::min<size_t>((n + 255) / 256, (size_t)ctx->sm_count * 8);
-        g3::proj_splitk_reduce<<<blocks, 256, 0, ctx->stream>>>(ctx->pp, splits, T, N, out);
+        CU_TRY(launch_pdl(g3::proj_splitk_reduce, dim3(blocks), dim3(256), 0, ctx->stream, (const float *)ctx->pp,
+                          splits, T, N, out));
         if (int r = check_launch(ctx, 1)) return r;
     }
     prof_end(ctx, 2, e0, 2.0 * T * N * K);
@@ -871,7 +872,7 @@ static int proj_run(gemma3_cuda_ctx *ctx, const __half *W, int N, int K, const _
 static int to_f16(gemma3_cuda_ctx *ctx, const float *x, __half *y, size_t n) {
     const size_t n4 = n / 4;
     const int blocks = (int)std::min<size_t>((n4 + 255) / 256, (size_t)ctx->sm_count * 8);
-    g3::to_f16_rows<<<blocks, 256, 0, ctx->stream>>>(x, y, n4, ctx->err);
+    CU_TRY(launch_pdl(g3::to_f16_rows, dim3(blocks), dim3(256), 0, ctx->stream, x, y, n4, ctx->err));
     return check_launch(ctx, 1);
 }
 
@@ -1056,8 +1057,8 @@ static int forward_layers(gemma3_cuda_ctx *ctx, int T, float *x, AttnFn attn) {
     float *gate = ctx->gu, *up = ctx->gu + (size_t)R * kInter;
     // pre-attention norm of layer 0; every later one comes out of the
     // previous layer's last residual step
-    g3::rms_norm_rows_f16<<<T, g3::kNormThreads, 0, ctx->stream>>>(x, ln_of(ctx->layers[0], 0), ctx->xb, eps,
-                                                                    ctx->err);
+    CU_TRY(launch_pdl(g3::rms_norm_rows_f16, dim3(T), dim3(g3::kNormThreads), 0, ctx->stream, (const float *)x,
+                      ln_of(ctx->layers[0], 0), ctx->xb, eps, ctx->err));
     if (int r = check_launch(ctx, 1)) return r;
     for (int l = 0; l < ctx->cfg.num_layers; ++l) {
         const LayerState &L = ctx->layers[l];
@@ -1080,8 +1081,8 @@ static int forward_layers(gemma3_cuda_ctx *ctx, int T, float *x, AttnFn attn) {
         o.lo[1] = o.lo[2] = o.lo[3] = kHidden;
         if (int r = proj_run(ctx, L.wo, kHidden, kQSize, ctx->ab, T, o)) return r;
         // x += post_attn_norm(o_proj); xn = pre_ffn_norm(x)
-        g3::residual_norm_rows<<<T, g3::kNormThreads, 0, ctx->stream>>>(ctx->delta, ln_of(L, 1), x, ln_of(L, 2),
-                                                                         ctx->xb, eps, ctx->err);
+        CU_TRY(launch_pdl(g3::residual_norm_rows, dim3(T), dim3(g3::kNormThreads), 0, ctx->stream,
+                          (const float *)ctx->delta, ln_of(L, 1), x, ln_of(L, 2), ctx->xb, eps, ctx->err));
         if (int r = check_launch(ctx, 1)) return r;
         o.ptr[0] = gate;
         o.ptr[1] = o.ptr[2] = up;
@@ -1094,7 +1095,8 @@ static int forward_layers(gemma3_cuda_ctx *ctx, int T, float *x, AttnFn attn) {
             const size_t n = (size_t)T * kInter;
             // gate and up rows are [T][10240] each, contiguous
             const int blocks = (int)std::min<size_t>((n + 255) / 256, (size_t)ctx->sm_count * 8);
-            g3::gelu_mul_f16<<<blocks, 256, 0, ctx->stream>>>(gate, up, ctx->hb, n, ctx->err);
+            CU_TRY(launch_pdl(g3::gelu_mul_f16, dim3(blocks), dim3(256), 0, ctx->stream, (const float *)gate,
+                              (const float *)up, ctx->hb, n, ctx->err));
             if (int r = check_launch(ctx, 1)) return r;
         }
         o.ptr[0] = o.ptr[1] = o.ptr[2] = ctx->delta;
@@ -1104,9 +1106,10 @@ static int forward_layers(gemma3_cuda_ctx *ctx, int T, float *x, AttnFn attn) {
         if (int r = proj_run(ctx, L.wdown, kHidden, kInter, ctx->hb, T, o)) return r;
         // x += post_ffn_norm(mlp); xn = next layer's pre-attention norm(x)
         const bool last = l + 1 == ctx->cfg.num_layers;
-        g3::residual_norm_rows<<<T, g3::kNormThreads, 0, ctx->stream>>>(
-            ctx->delta, ln_of(L, 3), x, last ? nullptr : ln_of(ctx->layers[l + 1], 0), last ? nullptr : ctx->xb,
-            eps, ctx->err);
+        CU_TRY(launch_pdl(g3::residual_norm_rows, dim3(T), dim3(g3::kNormThreads), 0, ctx->stream,
+                          (const float *)ctx->delta, ln_of(L, 3), x,
+                          last ? (const uint16_t *)nullptr : ln_of(ctx->layers[l + 1], 0),
+                          last ? (__half *)nullptr : ctx->xb, eps, ctx->err));
         if (int r = check_launch(ctx, 1)) return r;
     }
     return 0;

@@ -8,6 +8,7 @@
 // gemma3_gelu_tanh_inplace (:348-358), gemma3_vec_mul / gemma3_vec_add.
 // Every row of the residual stream is fp32 [2560]; the inputs of the next
 // matrix product are written as fp16 (range-checked, see proj_kernels.cuh).
+// Launched with programmatic dependent launch (griddepcontrol.wait first).
 #pragma once
 #include "proj_kernels.cuh"
 
@@ -56,6 +57,8 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_rows_f16(const float *_
                                                                   const uint16_t *__restrict__ w, __half *__restrict__ xn,
                                                                   float eps, unsigned *err) {
     __shared__ float red[8];
+    pdl_launch_dependents();
+    pdl_wait();
     const size_t base = (size_t)blockIdx.x * kHiddenDim;
     float v[kNormPer];
 #pragma unroll
@@ -77,6 +80,8 @@ __global__ void __launch_bounds__(kNormThreads) residual_norm_rows(const float *
                                                                    const uint16_t *__restrict__ w_pre,
                                                                    __half *__restrict__ xn, float eps, unsigned *err) {
     __shared__ float red[8];
+    pdl_launch_dependents();
+    pdl_wait();
     const size_t base = (size_t)blockIdx.x * kHiddenDim;
     float d[kNormPer];
 #pragma unroll
@@ -99,6 +104,8 @@ __global__ void __launch_bounds__(kNormThreads) residual_norm_rows(const float *
 // gate and up are [rows][inter] each, at gu and gu + rows * inter.
 __global__ void __launch_bounds__(256) gelu_mul_f16(const float *__restrict__ gate, const float *__restrict__ up,
                                                     __half *__restrict__ h, size_t n, unsigned *err) {
+    pdl_launch_dependents();
+    pdl_wait();
     const float k0 = 0.7978845608028654f, k1 = 0.044715f;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         const float g = gate[i];

@@ -1,5 +1,7 @@
 // proj_kernels.cuh - BF16 Q/K/V and O projections of the attention layer on
-// the tensor cores (sm_100a).
+// the tensor cores (sm_100a).  Every kernel here is launched with
+// programmatic dependent launch: it begins while the previous kernel of the
+// stream drains and calls griddepcontrol.wait before touching memory.
 //
 // The reference computes every projection as y = W x with W stored BF16
 // [out][in] row-major and x fp32 (gemma3_matvec_bf16, gemma3_kernels.c:195-225,
@@ -103,6 +105,7 @@ __global__ void __launch_bounds__(kProjThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    pdl_launch_dependents();
 
     // tile index -> (feature tile, token tile, K split)
     auto tile_of = [&](int idx, int &m, int &n, int &s) {
@@ -115,6 +118,17 @@ __global__ void __launch_bounds__(kProjThreads, 1)
         k0 = s * kper;
         k1 = min(p.kchunks, k0 + kper);
     };
+    // The weights do not depend on the previous kernel of the stream: warm L2
+    // with this CTA's first weight tiles while that kernel drains, then wait
+    // for it (programmatic dependent launch) before touching anything else.
+    if (warp == 0 && lane == 0 && blockIdx.x < ntiles) {
+        prefetch_tmap(&tmW);
+        int m, n, s, k0, k1;
+        tile_of(blockIdx.x, m, n, s);
+        k_range(s, k0, k1);
+        for (int kc = k0; kc < min(k1, k0 + 2 * kProjStages); ++kc) tma_prefetch_2d(&tmW, kc * 64, m * 128);
+    }
+    pdl_wait();
 
     if (warp == 0) {
         // ---------------------------------------------------- TMA producer
@@ -238,6 +252,8 @@ __global__ void __launch_bounds__(kProjThreads, 1)
 // out[t][f] = sum over s (in order) of partial[s][t][f], routed as ProjOut.
 __global__ void __launch_bounds__(256) proj_splitk_reduce(const float *__restrict__ partial, int splits, int T, int N,
                                                           const ProjOut out) {
+    pdl_launch_dependents();
+    pdl_wait();
     const size_t n = (size_t)T * N;
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         float acc = partial[i];
@@ -250,6 +266,8 @@ __global__ void __launch_bounds__(256) proj_splitk_reduce(const float *__restric
 // value outside the fp16 range sets kErrRange.
 __global__ void __launch_bounds__(256) to_f16_rows(const float *__restrict__ x, __half *__restrict__ y, size_t n4,
                                                    unsigned *err) {
+    pdl_launch_dependents();
+    pdl_wait();
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
         const float4 v = reinterpret_cast<const float4 *>(x)[i];
         const float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
