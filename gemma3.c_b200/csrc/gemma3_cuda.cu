@@ -205,6 +205,15 @@ struct gemma3_cuda_ctx {
     int blk_rows = 0;
     uint16_t *wstage = nullptr;   // BF16 weight staging for the device-side fp16 conversion
     size_t wstage_elems = 0;
+    // tied embedding (gemma3_cuda_set_embeddings)
+    uint16_t *embed = nullptr;    // BF16 [vocab][2560]: exact lookups
+    __half *embed16 = nullptr;    // fp16 [vocab_pad][2560], zero rows past vocab: the logits GEMM
+    uint16_t *final_ln = nullptr; // BF16 [2560]
+    int vocab = 0, vocab_pad = 0;
+    float *logits = nullptr;      // [rows][vocab_pad]
+    int logit_rows = 0;
+    int *tok_dev = nullptr;       // [rows] token ids in, [rows] argmax out (after)
+    float *top_dev = nullptr;     // [rows] top-1 logits
     // device copies for the host-pointer entry points
     float *io = nullptr;
     size_t io_rows = 0;
@@ -280,6 +289,12 @@ static void ctx_release(gemma3_cuda_ctx *c) {
     cudaFree(c->delta);
     cudaFree(c->xfwd);
     cudaFree(c->wstage);
+    cudaFree(c->embed);
+    cudaFree(c->embed16);
+    cudaFree(c->final_ln);
+    cudaFree(c->logits);
+    cudaFree(c->tok_dev);
+    cudaFree(c->top_dev);
     cudaFree(c->xb);
     cudaFree(c->ab);
     cudaFree(c->qkv);
@@ -1151,6 +1166,111 @@ extern "C" int gemma3_cuda_prefill_forward(gemma3_cuda_ctx *ctx, int seq, float 
     CU_TRY(cudaMemcpyAsync(ctx->xfwd, x, (size_t)T * kHidden * 4, cudaMemcpyHostToDevice, ctx->stream));
     if (int r = gemma3_cuda_prefill_forward_dev(ctx, seq, ctx->xfwd, T, start_pos)) return r;
     CU_TRY(cudaMemcpyAsync(x, ctx->xfwd, (size_t)T * kHidden * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return gemma3_cuda_synchronize(ctx);
+}
+
+// ------------------------------------------------------------------ greedy decoding
+// Embedding lookup (gemma3_embed_bf16 + the sqrt(hidden) scale), the 34
+// blocks, the final norm and the tied-embedding logits (gemma3_transformer.c:
+// 502-509) with the greedy argmax (gemma3_argmax) on the device.
+extern "C" int gemma3_cuda_set_embeddings(gemma3_cuda_ctx *ctx, const uint16_t *embed, int vocab,
+                                          const uint16_t *final_norm) {
+    if (!ctx || !embed || !final_norm || vocab <= 0) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad embedding arguments");
+    CU_TRY(cudaSetDevice(ctx->cfg.device));
+    cudaFree(ctx->embed);
+    cudaFree(ctx->embed16);
+    cudaFree(ctx->logits);
+    ctx->embed = nullptr;
+    ctx->embed16 = nullptr;
+    ctx->logits = nullptr;
+    ctx->logit_rows = 0;
+    ctx->vocab = ctx->vocab_pad = 0;
+    const int pad = (vocab + 127) / 128 * 128;
+    CU_TRY(cudaMalloc(&ctx->embed, (size_t)vocab * kHidden * 2));
+    CU_TRY(cudaMalloc(&ctx->embed16, (size_t)pad * kHidden * 2));
+    if (!ctx->final_ln) CU_TRY(cudaMalloc(&ctx->final_ln, kHidden * 2));
+    CU_TRY(cudaMemcpyAsync(ctx->embed, embed, (size_t)vocab * kHidden * 2, cudaMemcpyHostToDevice, ctx->stream));
+    CU_TRY(cudaMemcpyAsync(ctx->final_ln, final_norm, kHidden * 2, cudaMemcpyHostToDevice, ctx->stream));
+    CU_TRY(cudaMemsetAsync(ctx->embed16 + (size_t)vocab * kHidden, 0, (size_t)(pad - vocab) * kHidden * 2, ctx->stream));
+    {
+        const size_t n = (size_t)vocab * kHidden;
+        const int blocks = (int)std::min<size_t>((n + 255) / 256, (size_t)ctx->sm_count * 16);
+        g3::bf16_to_f16<<<blocks, 256, 0, ctx->stream>>>(ctx->embed, ctx->embed16, n, ctx->err);
+        if (int r = check_launch(ctx, 1)) return r;
+    }
+    if (int r = gemma3_cuda_synchronize(ctx)) return r;
+    ctx->vocab = vocab;
+    ctx->vocab_pad = pad;
+    return 0;
+}
+
+// tokens (device [T]) -> x (device [T][2560]) scaled embeddings
+static int embed_tokens(gemma3_cuda_ctx *ctx, const int *tokens, int T, float *x) {
+    const float scale = sqrtf((float)kHidden);
+    CU_TRY(launch_pdl(g3::embed_rows, dim3(T), dim3(g3::kNormThreads), 0, ctx->stream, tokens,
+                      (const uint16_t *)ctx->embed, ctx->vocab, scale, x, ctx->err));
+    return check_launch(ctx, 1);
+}
+
+// rows of x (device [rows][2560]) -> next tokens into ctx->tok_dev, top-1 logits into ctx->top_dev
+static int logits_argmax(gemma3_cuda_ctx *ctx, const float *x, int rows) {
+    if (ctx->logit_rows < rows) {
+        cudaFree(ctx->logits);
+        ctx->logits = nullptr;
+        ctx->logit_rows = 0;
+        CU_TRY(cudaMalloc(&ctx->logits, (size_t)rows * ctx->vocab_pad * 4));
+        ctx->logit_rows = rows;
+    }
+    CU_TRY(launch_pdl(g3::rms_norm_rows_f16, dim3(rows), dim3(g3::kNormThreads), 0, ctx->stream, x,
+                      (const uint16_t *)ctx->final_ln, ctx->xb, ctx->cfg.rmsnorm_eps, ctx->err));
+    if (int r = check_launch(ctx, 1)) return r;
+    g3::ProjOut o;
+    o.ptr[0] = o.ptr[1] = o.ptr[2] = ctx->logits;
+    o.ld[0] = o.ld[1] = o.ld[2] = ctx->vocab_pad;
+    o.lo[0] = 0;
+    o.lo[1] = o.lo[2] = o.lo[3] = ctx->vocab_pad;
+    if (int r = proj_run(ctx, ctx->embed16, ctx->vocab_pad, kHidden, ctx->xb, rows, o)) return r;
+    CU_TRY(launch_pdl(g3::argmax_rows, dim3(rows), dim3(g3::kArgmaxThreads), 0, ctx->stream,
+                      (const float *)ctx->logits, (size_t)ctx->vocab_pad, ctx->vocab, ctx->tok_dev, ctx->top_dev));
+    return check_launch(ctx, 1);
+}
+
+static int greedy_check(gemma3_cuda_ctx *ctx, int rows) {
+    if (!ctx) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null context");
+    if (!ctx->vocab) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "embeddings not set");
+    if (int r = proj_check(ctx, 0, rows)) return r;
+    if (int r = block_scratch(ctx, ctx->proj_rows)) return r;
+    if (!ctx->tok_dev) {
+        CU_TRY(cudaMalloc(&ctx->tok_dev, (size_t)ctx->proj_rows * 4));
+        CU_TRY(cudaMalloc(&ctx->top_dev, (size_t)ctx->proj_rows * 4));
+    }
+    return 0;
+}
+
+extern "C" int gemma3_cuda_prefill_greedy(gemma3_cuda_ctx *ctx, int seq, const int *tokens, int T, int start_pos,
+                                          int *next_token, float *top_logit) {
+    if (int r = greedy_check(ctx, T)) return r;
+    if (!tokens || !next_token) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null buffer");
+    CU_TRY(cudaMemcpyAsync(ctx->tok_dev, tokens, (size_t)T * 4, cudaMemcpyHostToDevice, ctx->stream));
+    if (int r = embed_tokens(ctx, ctx->tok_dev, T, ctx->xfwd)) return r;
+    if (int r = gemma3_cuda_prefill_forward_dev(ctx, seq, ctx->xfwd, T, start_pos)) return r;
+    if (int r = logits_argmax(ctx, ctx->xfwd + (size_t)(T - 1) * kHidden, 1)) return r;  // the last prompt token
+    CU_TRY(cudaMemcpyAsync(next_token, ctx->tok_dev, 4, cudaMemcpyDeviceToHost, ctx->stream));
+    if (top_logit) CU_TRY(cudaMemcpyAsync(top_logit, ctx->top_dev, 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return gemma3_cuda_synchronize(ctx);
+}
+
+extern "C" int gemma3_cuda_greedy_step(gemma3_cuda_ctx *ctx, int B, const int *seq_ids, const int *pos,
+                                       const int *tokens, int *next_tokens, float *top_logits) {
+    if (int r = greedy_check(ctx, B)) return r;
+    if (int r = decode_check(ctx, 0, B, seq_ids, pos)) return r;
+    if (!tokens || !next_tokens) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null buffer");
+    CU_TRY(cudaMemcpyAsync(ctx->tok_dev, tokens, (size_t)B * 4, cudaMemcpyHostToDevice, ctx->stream));
+    if (int r = embed_tokens(ctx, ctx->tok_dev, B, ctx->xfwd)) return r;
+    if (int r = gemma3_cuda_forward_dev(ctx, B, seq_ids, pos, ctx->xfwd)) return r;
+    if (int r = logits_argmax(ctx, ctx->xfwd, B)) return r;
+    CU_TRY(cudaMemcpyAsync(next_tokens, ctx->tok_dev, (size_t)B * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    if (top_logits) CU_TRY(cudaMemcpyAsync(top_logits, ctx->top_dev, (size_t)B * 4, cudaMemcpyDeviceToHost, ctx->stream));
     return gemma3_cuda_synchronize(ctx);
 }
 

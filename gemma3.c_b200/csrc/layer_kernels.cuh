@@ -114,4 +114,86 @@ __global__ void __launch_bounds__(256) gelu_mul_f16(const float *__restrict__ ga
     }
 }
 
+// x[row] = embed[tokens[row]] * scale in fp32 (gemma3_embed_bf16,
+// gemma3_kernels.c:322-328, then the sqrt(hidden_size) scale of
+// gemma3_transformer.c:411-418).  A token id outside [0, vocab) writes zeros
+// and raises kErrBadIndex.
+__global__ void __launch_bounds__(kNormThreads) embed_rows(const int *__restrict__ tokens,
+                                                           const uint16_t *__restrict__ embed, int vocab, float scale,
+                                                           float *__restrict__ x, unsigned *err) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int tok = tokens[blockIdx.x];
+    const bool ok = tok >= 0 && tok < vocab;
+    if (!ok && threadIdx.x == 0) atomicOr(err, kErrBadIndex);
+    const uint16_t *row = embed + (size_t)(ok ? tok : 0) * kHiddenDim;
+#pragma unroll
+    for (int i = 0; i < kNormPer; ++i) {
+        const int c = threadIdx.x + i * kNormThreads;
+        x[(size_t)blockIdx.x * kHiddenDim + c] = ok ? bf16_bits_to_f(row[c]) * scale : 0.f;
+    }
+}
+
+// Per row: the first index of the largest of n logits and its value, as
+// gemma3_argmax (gemma3_kernels.c:799-811: strict ">" scanning from index 0,
+// so the lowest index wins a tie).  A NaN ranks below every number here.
+// One CTA of 1024 threads per row.
+constexpr int kArgmaxThreads = 1024;
+__device__ __forceinline__ bool arg_gt(float a, float b) { return a > b || (b != b && a == a); }
+// candidate (va, ia) beats (vb, ib): ia < 0 marks "no candidate"
+__device__ __forceinline__ bool arg_better(float va, int ia, float vb, int ib) {
+    if (ib < 0) return ia >= 0;
+    if (ia < 0) return false;
+    return arg_gt(va, vb) || (!arg_gt(vb, va) && ia < ib);
+}
+__global__ void __launch_bounds__(kArgmaxThreads) argmax_rows(const float *__restrict__ logits, size_t ld, int n,
+                                                               int *__restrict__ idx_out, float *__restrict__ val_out) {
+    __shared__ float sv[32];
+    __shared__ int si[32];
+    pdl_launch_dependents();
+    pdl_wait();
+    const float *row = logits + (size_t)blockIdx.x * ld;
+    float best = 0.f;
+    int bi = -1;
+    for (int i = threadIdx.x; i < n; i += kArgmaxThreads) {
+        const float v = row[i];
+        if (bi < 0 || arg_gt(v, best)) {
+            best = v;
+            bi = i;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (arg_better(ov, oi, best, bi)) {
+            best = ov;
+            bi = oi;
+        }
+    }
+    const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (l == 0) {
+        sv[w] = best;
+        si[w] = bi;
+    }
+    __syncthreads();
+    if (w == 0) {
+        best = sv[l];
+        bi = si[l];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (arg_better(ov, oi, best, bi)) {
+                best = ov;
+                bi = oi;
+            }
+        }
+        if (l == 0) {
+            idx_out[blockIdx.x] = bi < 0 ? 0 : bi;
+            if (val_out) val_out[blockIdx.x] = best;
+        }
+    }
+}
+
 }  // namespace g3

@@ -123,6 +123,9 @@ SIGNATURES = {
     "gemma3_cuda_forward_dev": (_I, [_P, _I, _IP, _IP, _P]),
     "gemma3_cuda_prefill_forward": (_I, [_P, _I, _FP, _I, _I]),
     "gemma3_cuda_prefill_forward_dev": (_I, [_P, _I, _P, _I, _I]),
+    "gemma3_cuda_set_embeddings": (_I, [_P, _U16P, _I, _U16P]),
+    "gemma3_cuda_prefill_greedy": (_I, [_P, _I, _IP, _I, _I, _IP, _FP]),
+    "gemma3_cuda_greedy_step": (_I, [_P, _I, _IP, _IP, _IP, _IP, _FP]),
     "gemma3_cuda_last_error": (ctypes.c_char_p, []),
 }
 
@@ -354,6 +357,30 @@ class Context:
 
     def prefill_forward_dev(self, seq, x_ptr, T, start_pos):
         self._chk(self.lib.gemma3_cuda_prefill_forward_dev(self.h, seq, x_ptr, T, start_pos))
+
+    # -- greedy decoding ------------------------------------------------------
+    def set_embeddings(self, embed, final_norm):
+        e = np.ascontiguousarray(embed, dtype=np.uint16)
+        n = np.ascontiguousarray(final_norm, dtype=np.uint16)
+        self._chk(self.lib.gemma3_cuda_set_embeddings(self.h, e.ctypes.data_as(_U16P), e.shape[0],
+                                                      n.ctypes.data_as(_U16P)))
+
+    def prefill_greedy(self, seq, tokens, start_pos):
+        t, tp = _iarr(tokens)
+        nxt = np.zeros(1, np.int32)
+        top = np.zeros(1, np.float32)
+        self._chk(self.lib.gemma3_cuda_prefill_greedy(self.h, seq, tp, len(t), start_pos,
+                                                      nxt.ctypes.data_as(_IP), _fptr(top)))
+        return int(nxt[0]), float(top[0])
+
+    def greedy_step(self, seq_ids, pos, tokens):
+        s, sp = _iarr(seq_ids)
+        p, pp = _iarr(pos)
+        t, tp = _iarr(tokens)
+        nxt = np.zeros(len(s), np.int32)
+        top = np.zeros(len(s), np.float32)
+        self._chk(self.lib.gemma3_cuda_greedy_step(self.h, len(s), sp, pp, tp, nxt.ctypes.data_as(_IP), _fptr(top)))
+        return nxt, top
 
     # -- hot path (device pointers, enqueue only) -------------------------
     def attn_prefill_dev(self, layer, seq, q_ptr, k_ptr, v_ptr, T, start_pos, out_ptr):

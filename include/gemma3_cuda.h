@@ -224,6 +224,32 @@ int gemma3_cuda_prefill_forward(gemma3_cuda_ctx *ctx, int seq, float *x, int T,
 int gemma3_cuda_prefill_forward_dev(gemma3_cuda_ctx *ctx, int seq, float *x,
                                     int T, int start_pos);
 
+/* ---- Greedy decoding on the device ---------------------------------------- */
+
+/* Uploads the tied embedding table (BF16 [vocab][2560], gemma3_weights_t.
+ * embed_tokens) and the final norm gains (BF16 [2560], .norm).  Lookups use
+ * the BF16 table exactly; the vocabulary projection uses an fp16 copy.
+ * About 2.7 GB of device memory at vocab = 262208. */
+int gemma3_cuda_set_embeddings(gemma3_cuda_ctx *ctx, const uint16_t *embed,
+                               int vocab, const uint16_t *final_norm);
+
+/* A prompt of T token ids (host) for sequence slot `seq` at positions
+ * start_pos..: embedding lookup and scale (gemma3_transformer.c:411-418),
+ * all blocks, then for the last token the final norm, the tied-embedding
+ * logits (:502-509) and the greedy choice (gemma3_argmax: the first index of
+ * the largest logit).  Writes the next token id and (top_logit, may be
+ * NULL) its logit.  Needs gemma3_cuda_set_layer_weights for every layer. */
+int gemma3_cuda_prefill_greedy(gemma3_cuda_ctx *ctx, int seq, const int *tokens,
+                               int T, int start_pos, int *next_token,
+                               float *top_logit);
+
+/* One greedy decode step for B sequences: token ids (host) at positions
+ * pos[b] in slots seq_ids[b] -> next token ids (host) and (top_logits, may
+ * be NULL) their logits.  Only the ids cross the host boundary. */
+int gemma3_cuda_greedy_step(gemma3_cuda_ctx *ctx, int B, const int *seq_ids,
+                            const int *pos, const int *tokens,
+                            int *next_tokens, float *top_logits);
+
 /* Context-parallel decode on a global layer whose KV range is split across
  * kv_ranks contexts (one per GPU).  Step 1 runs on every rank and writes this
  * rank's log-sum-exp partial for each (sequence, q head) into `partial`

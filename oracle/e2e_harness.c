@@ -17,7 +17,8 @@
  * Arm "cuda, all blocks" (use_cuda 2): every transformer block on the device
  * through gemma3_cuda_prefill_forward / gemma3_cuda_forward (projections,
  * norms, residuals and MLP included); embeddings, final norm and logits stay
- * on the host.
+ * on the host.  Arm "cuda, greedy" (use_cuda 3): token ids in, token ids out
+ * through gemma3_cuda_prefill_greedy / gemma3_cuda_greedy_step.
  *
  * Weights are random BF16 (truncated fp32 draws): projections and
  * embeddings ~N(0, 0.02), norm weights ~N(0, 0.1) (gain 1+w), drawn with a
@@ -159,8 +160,8 @@ static void logits_of(float *logits, const float *x, const gemma3_weights_t *w, 
 
 /*
  * Runs one arm.  use_cuda: 0 = reference forward, 1 = device attention path,
- * 2 = all transformer blocks on the device (kv_dtype GEMMA3_CUDA_KV_F32 /
- * _BF16).  Prompt = n_prompt uniform token ids
+ * 2 = all transformer blocks on the device, 3 = greedy decoding on the device
+ * (kv_dtype GEMMA3_CUDA_KV_F32 / _BF16).  Prompt = n_prompt uniform token ids
  * in [0, vocab) from `seed`; then n_steps greedy tokens.  Writes the generated
  * tokens, the top-1 minus top-2 logit margin and (top_out, may be NULL) the
  * top-1 logit of each step.  Returns 0, or a negative gemma3_error.
@@ -210,8 +211,9 @@ int e2e_greedy(int n_prompt, int n_steps, uint64_t seed, int use_cuda, int kv_dt
         }
         for (int l = 0; l < cfg->num_layers; l++)
             gemma3_cuda_set_qk_norm(ctx, l, w->layers[l].q_norm, w->layers[l].k_norm);
-        if (use_cuda == 2) {
-            /* every block on the device; embeddings, final norm and logits on the host */
+        if (use_cuda >= 2) {
+            /* every block on the device; embeddings, final norm and logits on the host
+             * (use_cuda 2) or on the device too (use_cuda 3) */
             for (int l = 0; l < cfg->num_layers && !rc; l++) {
                 const gemma3_cuda_layer_weights lw = {
                     w->layers[l].input_layernorm, w->layers[l].q_proj, w->layers[l].k_proj, w->layers[l].v_proj,
@@ -227,17 +229,31 @@ int e2e_greedy(int n_prompt, int n_steps, uint64_t seed, int use_cuda, int kv_dt
                 gemma3_embed_bf16(X + (size_t)i * H, w->embed_tokens, prompt[i], H);
                 for (int j = 0; j < H; j++) X[(size_t)i * H + j] *= es;
             }
-            if (!rc) rc = gemma3_cuda_prefill_forward(ctx, 0, X, n_prompt, 0);
-            if (!rc) logits_of(logits, X + (size_t)(n_prompt - 1) * H, w, buf, cfg, pool);
-            int pos = n_prompt, tok = 0, seq = 0;
-            for (int s = 0; s < n_steps && !rc; s++, pos++) {
-                top2(logits, cfg->vocab_size, &tok, &margins_out[s]);
-                tokens_out[s] = tok;
-                float *x = buf->x;
-                gemma3_embed_bf16(x, w->embed_tokens, tok, H);
-                for (int j = 0; j < H; j++) x[j] *= es;
-                rc = gemma3_cuda_forward(ctx, 1, &seq, &pos, x);
-                if (!rc) logits_of(logits, x, w, buf, cfg, pool);
+            if (use_cuda == 3) {
+                /* token ids in, token ids out: embedding, blocks, final norm, logits and argmax on the device */
+                if (!rc) rc = gemma3_cuda_set_embeddings(ctx, w->embed_tokens, cfg->vocab_size, w->norm);
+                int tok = 0, seq = 0, pos = n_prompt;
+                float top = 0.f;
+                if (!rc) rc = gemma3_cuda_prefill_greedy(ctx, 0, prompt, n_prompt, 0, &tok, &top);
+                for (int s = 0; s < n_steps && !rc; s++, pos++) {
+                    tokens_out[s] = tok;
+                    margins_out[s] = 0.f;
+                    if (g_top_out) *g_top_out++ = top;
+                    rc = gemma3_cuda_greedy_step(ctx, 1, &seq, &pos, &tok, &tok, &top);
+                }
+            } else {
+                if (!rc) rc = gemma3_cuda_prefill_forward(ctx, 0, X, n_prompt, 0);
+                if (!rc) logits_of(logits, X + (size_t)(n_prompt - 1) * H, w, buf, cfg, pool);
+                int pos = n_prompt, tok = 0, seq = 0;
+                for (int s = 0; s < n_steps && !rc; s++, pos++) {
+                    top2(logits, cfg->vocab_size, &tok, &margins_out[s]);
+                    tokens_out[s] = tok;
+                    float *x = buf->x;
+                    gemma3_embed_bf16(x, w->embed_tokens, tok, H);
+                    for (int j = 0; j < H; j++) x[j] *= es;
+                    rc = gemma3_cuda_forward(ctx, 1, &seq, &pos, x);
+                    if (!rc) logits_of(logits, x, w, buf, cfg, pool);
+                }
             }
             if (rc) fprintf(stderr, "e2e: %s\n", gemma3_cuda_last_error());
             free(X);

@@ -62,3 +62,22 @@ def test_greedy_32_steps_all_blocks_on_device():
           float(np.max(np.abs(dev_top - ref_top) / np.abs(ref_top))))
     assert np.array_equal(ref_t, dev_t)
     assert np.max(np.abs(dev_top - ref_top) / np.abs(ref_top)) <= 1e-2
+
+
+def test_greedy_32_steps_token_ids_on_device():
+    """Token ids in, token ids out: embedding lookup, all blocks, final norm,
+    the tied-embedding logits and the greedy argmax on the device
+    (gemma3_cuda_prefill_greedy / gemma3_cuda_greedy_step)."""
+    if not os.path.exists(SO):
+        pytest.skip("e2e harness not built (needs the reference sources at build time)")
+    os.environ.setdefault("OPENBLAS_NUM_THREADS", "1")
+    lib = ctypes.CDLL(SO)
+    lib.e2e_greedy.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.c_uint64, ctypes.c_int, ctypes.c_int,
+                               ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    ref_t, ref_m, ref_top = _arm(lib, 0)
+    dev_t, _, dev_top = _arm(lib, 3, 0)
+    print("reference tokens", ref_t.tolist())
+    print("device tokens   ", dev_t.tolist())
+    print("max top-1 rel diff", float(np.max(np.abs(dev_top - ref_top) / np.abs(ref_top))))
+    assert np.array_equal(ref_t, dev_t)
+    assert np.max(np.abs(dev_top - ref_top) / np.abs(ref_top)) <= 1e-2
