@@ -594,6 +594,22 @@ def secondary_model(args, torch, gc, pk, dev):
     res["decode_B64_ctx4096"] = {"ms_per_step": round(ms / reps, 3), "tok_per_s": round(B * reps / (ms / 1e3), 1),
                                  "weight_gb": round(wbytes / 1e9, 2), "kv_gb": round(kvbytes / 1e9, 2),
                                  "gbs": round(gbs, 1), "frac_hbm": round(gbs / pk["hbm_gbs"], 4)}
+    # greedy step: token ids in, ids out (embedding, 34 blocks, final norm,
+    # 262,208-way tied-embedding logits, argmax), same caches and positions
+    emb = w((262208, H))
+    ctx.set_embeddings(emb, w((H,), 0.1))
+    del emb
+    toks = list(range(1000, 1000 + B))
+    for _ in range(2):
+        ctx.greedy_step(seqs, poss, toks)
+    reps = 5
+    import time as _t
+    t0 = _t.perf_counter()
+    for _ in range(reps):
+        ctx.greedy_step(seqs, poss, toks)  # synchronous: ids back on the host each step
+    wall = (_t.perf_counter() - t0) / reps
+    res["greedy_step_B64_ctx4096"] = {"ms_per_step_wall": round(wall * 1e3, 3), "tok_per_s": round(B / wall, 1),
+                                      "note": "host-synchronous call incl. 1.34 GB logits GEMM and argmax"}
     ctx.close()
     del xd0, xd
     torch.cuda.empty_cache()
