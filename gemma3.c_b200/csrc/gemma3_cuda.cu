@@ -27,6 +27,7 @@
 #include "attn_kernels.cuh"
 #include "proj_kernels.cuh"
 #include "layer_kernels.cuh"
+#include "safetensors.hpp"
 
 using g3::kHeadDim;
 using g3::kHeads;
@@ -1272,6 +1273,105 @@ extern "C" int gemma3_cuda_greedy_step(gemma3_cuda_ctx *ctx, int B, const int *s
     CU_TRY(cudaMemcpyAsync(next_tokens, ctx->tok_dev, (size_t)B * 4, cudaMemcpyDeviceToHost, ctx->stream));
     if (top_logits) CU_TRY(cudaMemcpyAsync(top_logits, ctx->top_dev, (size_t)B * 4, cudaMemcpyDeviceToHost, ctx->stream));
     return gemma3_cuda_synchronize(ctx);
+}
+
+// ------------------------------------------------------------------ SafeTensors upload
+// The weight names and the BF16 expectation of gemma3_load_weights
+// (gemma3_safetensors.c:651-713), checked here (presence, dtype, shape)
+// before anything is uploaded; text-only checkpoints without the
+// "language_model." prefix are accepted too.
+struct StModel {
+    std::string prefix;
+    std::vector<gemma3_cuda_layer_weights> layers;
+    const uint16_t *embed = nullptr, *norm = nullptr;
+    int vocab = 0;
+};
+
+static std::string shape_str(const std::vector<int64_t> &v) {
+    std::string r = "[";
+    for (size_t i = 0; i < v.size(); ++i) r += (i ? ", " : "") + std::to_string(v[i]);
+    return r + "]";
+}
+
+static int st_get(const g3st::Index &ix, const std::string &name, const std::vector<int64_t> &shape, bool required,
+                  const uint16_t **out) {
+    *out = nullptr;
+    const g3st::Tensor *t = ix.find(name);
+    if (!t) return required ? fail(GEMMA3_CUDA_ERR_INVALID_ARG, "tensor %s not found", name.c_str()) : 0;
+    if (t->dtype != "BF16")
+        return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "tensor %s is %s, not BF16", name.c_str(), t->dtype.c_str());
+    if (t->shape != shape)
+        return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "tensor %s has shape %s, expected %s", name.c_str(),
+                    shape_str(t->shape).c_str(), shape_str(shape).c_str());
+    int64_t n = 1;
+    for (auto d : shape) n *= d;
+    if (t->bytes != (size_t)n * 2)
+        return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "tensor %s: %zu bytes for %lld BF16 values", name.c_str(), t->bytes,
+                    (long long)n);
+    *out = reinterpret_cast<const uint16_t *>(t->data);
+    return 0;
+}
+
+static int st_collect(const g3st::Index &ix, int num_layers, StModel &m) {
+    m.prefix.clear();
+    for (const char *pre : {"language_model.model.", "model."})
+        if (ix.find(std::string(pre) + "embed_tokens.weight")) {
+            m.prefix = pre;
+            break;
+        }
+    if (m.prefix.empty()) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "tensor language_model.model.embed_tokens.weight not found");
+    const g3st::Tensor *e = ix.find(m.prefix + "embed_tokens.weight");
+    if (e->shape.size() != 2 || e->shape[1] != kHidden || e->shape[0] <= 0 || e->shape[0] > INT32_MAX)
+        return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "embed_tokens has shape %s", shape_str(e->shape).c_str());
+    m.vocab = (int)e->shape[0];
+    if (int r = st_get(ix, m.prefix + "embed_tokens.weight", {m.vocab, kHidden}, true, &m.embed)) return r;
+    if (int r = st_get(ix, m.prefix + "norm.weight", {kHidden}, true, &m.norm)) return r;
+    m.layers.assign(num_layers, gemma3_cuda_layer_weights{});
+    for (int l = 0; l < num_layers; ++l) {
+        const std::string p = m.prefix + "layers." + std::to_string(l) + ".";
+        gemma3_cuda_layer_weights &w = m.layers[l];
+        const struct { const char *name; std::vector<int64_t> shape; bool req; const uint16_t **dst; } items[] = {
+            {"input_layernorm.weight", {kHidden}, true, &w.input_layernorm},
+            {"self_attn.q_proj.weight", {kQSize, kHidden}, true, &w.q_proj},
+            {"self_attn.k_proj.weight", {kKvSize, kHidden}, true, &w.k_proj},
+            {"self_attn.v_proj.weight", {kKvSize, kHidden}, true, &w.v_proj},
+            {"self_attn.o_proj.weight", {kHidden, kQSize}, true, &w.o_proj},
+            {"self_attn.q_norm.weight", {kHeadDim}, false, &w.q_norm},
+            {"self_attn.k_norm.weight", {kHeadDim}, false, &w.k_norm},
+            {"post_attention_layernorm.weight", {kHidden}, false, &w.post_attention_layernorm},
+            {"mlp.gate_proj.weight", {kInter, kHidden}, true, &w.gate_proj},
+            {"mlp.up_proj.weight", {kInter, kHidden}, true, &w.up_proj},
+            {"mlp.down_proj.weight", {kHidden, kInter}, true, &w.down_proj},
+            {"pre_feedforward_layernorm.weight", {kHidden}, false, &w.pre_feedforward_layernorm},
+            {"post_feedforward_layernorm.weight", {kHidden}, false, &w.post_feedforward_layernorm},
+        };
+        for (const auto &it : items)
+            if (int r = st_get(ix, p + it.name, it.shape, it.req, it.dst)) return r;
+    }
+    return 0;
+}
+
+extern "C" int gemma3_cuda_safetensors_check(const char *model_dir, int num_layers, int *vocab_out) {
+    if (!model_dir || num_layers <= 0) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad arguments");
+    g3st::Index ix;
+    std::string err;
+    if (!ix.open(model_dir, err)) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "%s", err.c_str());
+    StModel m;
+    if (int r = st_collect(ix, num_layers, m)) return r;
+    if (vocab_out) *vocab_out = m.vocab;
+    return 0;
+}
+
+extern "C" int gemma3_cuda_load_safetensors(gemma3_cuda_ctx *ctx, const char *model_dir) {
+    if (!ctx || !model_dir) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad arguments");
+    g3st::Index ix;
+    std::string err;
+    if (!ix.open(model_dir, err)) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "%s", err.c_str());
+    StModel m;
+    if (int r = st_collect(ix, ctx->cfg.num_layers, m)) return r;  // everything checked before any upload
+    for (int l = 0; l < ctx->cfg.num_layers; ++l)
+        if (int r = gemma3_cuda_set_layer_weights(ctx, l, &m.layers[l])) return r;
+    return gemma3_cuda_set_embeddings(ctx, m.embed, m.vocab, m.norm);
 }
 
 // ------------------------------------------------------------------ NCCL

@@ -126,6 +126,8 @@ SIGNATURES = {
     "gemma3_cuda_set_embeddings": (_I, [_P, _U16P, _I, _U16P]),
     "gemma3_cuda_prefill_greedy": (_I, [_P, _I, _IP, _I, _I, _IP, _FP]),
     "gemma3_cuda_greedy_step": (_I, [_P, _I, _IP, _IP, _IP, _IP, _FP]),
+    "gemma3_cuda_safetensors_check": (_I, [ctypes.c_char_p, _I, _IP]),
+    "gemma3_cuda_load_safetensors": (_I, [_P, ctypes.c_char_p]),
     "gemma3_cuda_last_error": (ctypes.c_char_p, []),
 }
 
@@ -162,6 +164,17 @@ def _fptr(a: np.ndarray):
 def _iarr(xs):
     a = np.ascontiguousarray(np.asarray(xs, dtype=np.int32))
     return a, a.ctypes.data_as(_IP)
+
+
+def safetensors_check(model_dir: str, num_layers: int = N_LAYERS) -> int:
+    """Host-only check of a checkpoint directory; returns the vocabulary size,
+    raises Gemma3CudaError with the reason otherwise."""
+    lib = load_library()
+    v = np.zeros(1, np.int32)
+    rc = lib.gemma3_cuda_safetensors_check(model_dir.encode(), num_layers, v.ctypes.data_as(_IP))
+    if rc != 0:
+        raise Gemma3CudaError(rc, (lib.gemma3_cuda_last_error() or b"").decode())
+    return int(v[0])
 
 
 def rope_table(max_pos: int, theta: float) -> np.ndarray:
@@ -357,6 +370,10 @@ class Context:
 
     def prefill_forward_dev(self, seq, x_ptr, T, start_pos):
         self._chk(self.lib.gemma3_cuda_prefill_forward_dev(self.h, seq, x_ptr, T, start_pos))
+
+    # -- checkpoints -----------------------------------------------------------
+    def load_safetensors(self, model_dir: str):
+        self._chk(self.lib.gemma3_cuda_load_safetensors(self.h, model_dir.encode()))
 
     # -- greedy decoding ------------------------------------------------------
     def set_embeddings(self, embed, final_norm):

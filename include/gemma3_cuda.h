@@ -250,6 +250,22 @@ int gemma3_cuda_greedy_step(gemma3_cuda_ctx *ctx, int B, const int *seq_ids,
                             const int *pos, const int *tokens,
                             int *next_tokens, float *top_logits);
 
+/* ---- SafeTensors checkpoints ----------------------------------------------- */
+
+/* Checks a checkpoint directory the way gemma3_load_weights reads it
+ * (gemma3_safetensors.c:393-486, :651-713): every *.safetensors file, the
+ * tensor names "language_model.model.layers.<l>.<...>.weight" (or
+ * "model.layers..." for text-only checkpoints), BF16, and the Gemma 3 4B
+ * shapes for num_layers layers.  Host only (no device needed); writes the
+ * vocabulary size (rows of embed_tokens) to vocab_out when not NULL. */
+int gemma3_cuda_safetensors_check(const char *model_dir, int num_layers,
+                                  int *vocab_out);
+
+/* Checks, then uploads every layer (gemma3_cuda_set_layer_weights) and the
+ * embeddings / final norm (gemma3_cuda_set_embeddings) straight from the
+ * memory-mapped files.  Nothing is uploaded if the check fails. */
+int gemma3_cuda_load_safetensors(gemma3_cuda_ctx *ctx, const char *model_dir);
+
 /* Context-parallel decode on a global layer whose KV range is split across
  * kv_ranks contexts (one per GPU).  Step 1 runs on every rank and writes this
  * rank's log-sum-exp partial for each (sequence, q head) into `partial`
