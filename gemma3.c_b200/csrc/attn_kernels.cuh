@@ -356,6 +356,21 @@ __device__ __forceinline__ void load_row8<float>(const float *row, int lane, flo
 // (DecodeParams::qraw) and the in-kernel merge (DecodeParams::tickets); the
 // plain form is compiled without that code, which measurably slows the long
 // streaming loop even when it is not executed.
+// Development-only per-CTA phase timestamps of the decode kernel (build with
+// -DG3_DEC_TRACE); compiled out of the library.
+#ifdef G3_DEC_TRACE
+__device__ unsigned long long g3_dec_trace[1024][6];
+#define G3_DTRACE(k)                                                                                  \
+    do {                                                                                              \
+        const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);          \
+        if (threadIdx.x == 0 && cta < 1024) g3_dec_trace[cta][k] = globaltimer_ns();                  \
+    } while (0)
+#else
+#define G3_DTRACE(k) \
+    do {             \
+    } while (0)
+#endif
+
 template <typename KVT, bool kFused>
 __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, const __grid_constant__ DecodeRows rows) {
     constexpr int TK = DecodeCfg<KVT>::TK;
@@ -382,6 +397,7 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
 
     // Dependent launch: the next kernel may start its set-up now; this one
     // touches global memory only after the previous kernel has completed.
+    G3_DTRACE(0);
     pdl_launch_dependents();
     if (threadIdx.x == 0) {
         s_abort = 0;
@@ -393,6 +409,7 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
     }
     __syncthreads();
     pdl_wait();
+    G3_DTRACE(1);
 
     // q and fresh-row buffers of the fused prologue live after the ring.
     float(*qsm)[kHeadDim] = reinterpret_cast<float(*)[kHeadDim]>(smem + 2 * NS * kPlaneTile);
@@ -471,6 +488,7 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
             store4<KVT>(&newkv[sel][128 + 4 * lane], r.b);
         }
         __syncthreads();
+        G3_DTRACE(2);
         if (threadIdx.x == 0 && owner)
             for (int i = 0; i < NS && i < ntiles; ++i) issue(i);
     }
@@ -497,6 +515,7 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
             s_abort = 1;
             break;
         }
+        if (i == 0) G3_DTRACE(3);
         if (s_abort) break;
         const int nr = min(TK, r1 - (r0 + i * TK));
         const KVT *kt = kbuf + (size_t)s * TK * kHeadDim;
@@ -628,6 +647,7 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
             // to finish merges all partials; no CTA ever waits for another.
             __threadfence();
             __syncthreads();
+            G3_DTRACE(4);
             if (threadIdx.x == 0) s_last = atomicAdd(&p.tickets[b * kKvHeads + g], 1u) == (unsigned)(p.nsplit - 1);
             __syncthreads();
             if (!s_last) return;
@@ -662,6 +682,7 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
             *reinterpret_cast<float2 *>(p.out + (size_t)b * kHeads * kHeadDim + h * kHeadDim + d) =
                 make_float2(At * inv, Bt * inv);
             if (threadIdx.x == 0) p.tickets[b * kKvHeads + g] = 0u;
+            G3_DTRACE(5);
         }
     } else {
         const float inv = Ls > 0.f ? 1.0f / Ls : 0.f;

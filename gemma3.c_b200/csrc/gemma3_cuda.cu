@@ -1659,6 +1659,11 @@ extern "C" int gemma3_cuda_gqa_decode_noalloc(const float *q, const void *kv, in
     return 0;
 }
 
+#ifdef G3_DEC_TRACE
+extern "C" int g3_debug_read_dec_trace(unsigned long long *host) {
+    return (int)cudaMemcpyFromSymbol(host, g3::g3_dec_trace, sizeof(g3::g3_dec_trace));
+}
+#endif
 #ifdef G3_PF_TRACE
 extern "C" int g3_debug_read_trace(long long *host) {
     return (int)cudaMemcpyFromSymbol(host, g3::g3_pf_trace, sizeof(g3::g3_pf_trace));
