@@ -371,11 +371,181 @@ __device__ unsigned long long g3_dec_trace[1024][6];
     } while (0)
 #endif
 
+
+// Running online-softmax state of one warp for the two query heads of a GQA
+// group: max m and sum l (log2 domain) and the lane's 8 dims of O.
+struct DecAcc {
+    float m0, m1, l0, l1;
+    float o0[8], o1[8];
+    __device__ __forceinline__ void reset() {
+        m0 = m1 = -INFINITY;
+        l0 = l1 = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) o0[j] = o1[j] = 0.f;
+    }
+};
+
+// One tile of rows [0, nr) of K (kt) and V (vt) in shared memory: warp w
+// scores rows w, w+8, ... against both query heads, rescales its state to
+// the new running max and accumulates P.V.
+template <typename KVT>
+__device__ __forceinline__ void decode_tile(const KVT *kt, const KVT *vt, int nr, int warp, int lane,
+                                            const float (&q0)[8], const float (&q1)[8], DecAcc &a) {
+    constexpr int RW = DecodeCfg<KVT>::TK / 8;  // rows per warp per tile
+    float sc0[RW], sc1[RW];
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+        const int row = warp + 8 * r;
+        float k[8];
+        if (row < nr) {
+            load_row8<KVT>(kt + (size_t)row * kHeadDim, lane, k);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) k[j] = 0.f;
+        }
+        float x = 0.f, c = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            x = fmaf(q0[j], k[j], x);
+            c = fmaf(q1[j], k[j], c);
+        }
+        sc0[r] = x;
+        sc1[r] = c;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+        for (int r = 0; r < RW; ++r) {
+            sc0[r] += __shfl_xor_sync(0xffffffffu, sc0[r], o);
+            sc1[r] += __shfl_xor_sync(0xffffffffu, sc1[r], o);
+        }
+    }
+    float mx0 = a.m0, mx1 = a.m1;
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+        if (warp + 8 * r < nr) {
+            mx0 = fmaxf(mx0, sc0[r]);
+            mx1 = fmaxf(mx1, sc1[r]);
+        }
+    }
+    // A warp with no valid row in this tile keeps mx == m == -inf; its
+    // rescale factor must then be 1, not 2^(-inf - -inf) = NaN.
+    const float al0 = mx0 == -INFINITY ? 1.f : ex2_approx(a.m0 - mx0);
+    const float al1 = mx1 == -INFINITY ? 1.f : ex2_approx(a.m1 - mx1);
+    a.m0 = mx0;
+    a.m1 = mx1;
+    a.l0 *= al0;
+    a.l1 *= al1;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        a.o0[j] *= al0;
+        a.o1[j] *= al1;
+    }
+#pragma unroll
+    for (int r = 0; r < RW; ++r) {
+        const int row = warp + 8 * r;
+        if (row < nr) {
+            const float p0 = ex2_approx(sc0[r] - a.m0), p1 = ex2_approx(sc1[r] - a.m1);
+            a.l0 += p0;
+            a.l1 += p1;
+            float v[8];
+            load_row8<KVT>(vt + (size_t)row * kHeadDim, lane, v);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                a.o0[j] = fmaf(p0, v[j], a.o0[j]);
+                a.o1[j] = fmaf(p1, v[j], a.o1[j]);
+            }
+        }
+    }
+}
+
+// Combines the 8 warps' states through shared memory: acc (16 KB,
+// [warp][head][256]) and wm / wl.  Thread t gets, for head hh = t / 128 of
+// the group and dims d, d + 1 (d = 2 (t % 128)), the CTA's max M, sum Ls and
+// unnormalised O (A, Bv).  The caller synchronises before reusing acc.
+template <typename KVT>
+__device__ __forceinline__ void combine_warps(const DecAcc &a, float *acc, float (*wm)[2], float (*wl)[2], int warp,
+                                              int lane, float &M, float &Ls, float &A, float &Bv) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        acc[(warp * 2 + 0) * kHeadDim + lane_dim<KVT>(lane, j)] = a.o0[j];
+        acc[(warp * 2 + 1) * kHeadDim + lane_dim<KVT>(lane, j)] = a.o1[j];
+    }
+    if (lane == 0) {
+        wm[warp][0] = a.m0;
+        wm[warp][1] = a.m1;
+        wl[warp][0] = a.l0;
+        wl[warp][1] = a.l1;
+    }
+    __syncthreads();
+    const int hh = threadIdx.x >> 7;
+    const int d = (threadIdx.x & 127) * 2;
+    M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) M = fmaxf(M, wm[w][hh]);
+    Ls = 0.f;
+    A = 0.f;
+    Bv = 0.f;
+    if (M != -INFINITY) {
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+            if (wm[w][hh] == -INFINITY) continue;  // warp saw no row
+            const float f = ex2_approx(wm[w][hh] - M);
+            Ls += wl[w][hh] * f;
+            A += acc[(w * 2 + hh) * kHeadDim + d] * f;
+            Bv += acc[(w * 2 + hh) * kHeadDim + d + 1] * f;
+        }
+    }
+}
+
+// Log-sum-exp merge of n partials [m, l, O[256]] of the two heads of a group
+// (partial i of head 2g + th at base + th * hstride + i * 258, read through
+// L2: other CTAs wrote them).  Thread t writes the normalised O of head
+// hh = t / 128, dims d, d + 1 into out_g (the group's 512 outputs).  One
+// online pass, 16 partials (32 loads) in flight per thread.
+__device__ __forceinline__ void merge_group(const float *base, size_t hstride, int n, float *out_g) {
+    constexpr int C = 16;
+    const int hh = threadIdx.x >> 7, d = (threadIdx.x & 127) * 2;
+    const float *bh = base + hh * hstride;
+    float Mx = -INFINITY, Lt = 0.f, At = 0.f, Bt = 0.f;
+    for (int i0 = 0; i0 < n; i0 += C) {
+        float2 ml[C], o[C];
+#pragma unroll
+        for (int j = 0; j < C; ++j) {
+            if (i0 + j < n) {
+                const float *pp = bh + (size_t)(i0 + j) * (kHeadDim + 2);
+                ml[j] = __ldcg(reinterpret_cast<const float2 *>(pp));
+                o[j] = __ldcg(reinterpret_cast<const float2 *>(pp + 2 + d));
+            } else {
+                ml[j] = make_float2(-INFINITY, 0.f);
+                o[j] = make_float2(0.f, 0.f);
+            }
+        }
+        float cm = Mx;
+#pragma unroll
+        for (int j = 0; j < C; ++j) cm = fmaxf(cm, ml[j].x);
+        if (cm == -INFINITY) continue;  // no rows so far
+        const float sc = Mx == -INFINITY ? 0.f : ex2_approx(Mx - cm);
+        Lt *= sc;
+        At *= sc;
+        Bt *= sc;
+#pragma unroll
+        for (int j = 0; j < C; ++j) {
+            const float f = ml[j].x == -INFINITY ? 0.f : ex2_approx(ml[j].x - cm);
+            Lt += ml[j].y * f;
+            At += o[j].x * f;
+            Bt += o[j].y * f;
+        }
+        Mx = cm;
+    }
+    const float inv = Lt > 0.f ? 1.0f / Lt : 0.f;
+    *reinterpret_cast<float2 *>(out_g + hh * kHeadDim + d) = make_float2(At * inv, Bt * inv);
+}
+
 template <typename KVT, bool kFused>
 __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, const __grid_constant__ DecodeRows rows) {
     constexpr int TK = DecodeCfg<KVT>::TK;
     constexpr int NS = DecodeCfg<KVT>::NS;
-    constexpr int RW = TK / 8;  // rows per warp per tile
     constexpr uint32_t kPlaneTile = TK * kHeadDim * sizeof(KVT);
     extern __shared__ __align__(128) unsigned char smem[];
     KVT *kbuf = reinterpret_cast<KVT *>(smem);
@@ -452,10 +622,15 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
         bulk_g2s(ks, kg, nr * row_b, &full[s]);
         bulk_g2s(vs, vg, nr * row_b, &full[s]);
     };
-    // The owner CTA (one per sequence and kv head) starts copying after its
-    // prologue has built the fresh row; every other CTA right away.
-    if (threadIdx.x == 0 && !(kFused && owner))
-        for (int i = 0; i < NS && i < ntiles; ++i) issue(i);
+    // Tiles ahead of the one holding the new token's row (owner CTA only)
+    // go out right away; that tile and the rest of the first fill after the
+    // prologue has built the row.
+    int early = 0;
+    if (threadIdx.x == 0) {
+        while (early < NS && early < ntiles &&
+               !(kFused && owner && slot >= r0 + early * TK && slot < r0 + (early + 1) * TK))
+            issue(early++);
+    }
 
     // Fused prologue (gemma3_transformer.c:294-316): while the first tiles
     // are in flight, warps 0-1 normalise + rotate the two query heads of the
@@ -489,8 +664,8 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
         }
         __syncthreads();
         G3_DTRACE(2);
-        if (threadIdx.x == 0 && owner)
-            for (int i = 0; i < NS && i < ntiles; ++i) issue(i);
+        if (threadIdx.x == 0)
+            for (int i = early; i < NS && i < ntiles; ++i) issue(i);
     }
 
     // Query rows of the two heads sharing kv head g, the lane's 8 dims.
@@ -504,10 +679,8 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
             q1[j] = qb[lane_dim<KVT>(lane, j)];
         }
     }
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-    float o0[8], o1[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) o0[j] = o1[j] = 0.f;
+    DecAcc acc_st;
+    acc_st.reset();
 
     for (int i = 0; i < ntiles; ++i) {
         const int s = i % NS;
@@ -518,73 +691,8 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
         if (i == 0) G3_DTRACE(3);
         if (s_abort) break;
         const int nr = min(TK, r1 - (r0 + i * TK));
-        const KVT *kt = kbuf + (size_t)s * TK * kHeadDim;
-        const KVT *vt = vbuf + (size_t)s * TK * kHeadDim;
-        float sc0[RW], sc1[RW];
-#pragma unroll
-        for (int r = 0; r < RW; ++r) {
-            const int row = warp + 8 * r;
-            float k[8];
-            if (row < nr) {
-                load_row8<KVT>(kt + (size_t)row * kHeadDim, lane, k);
-            } else {
-#pragma unroll
-                for (int j = 0; j < 8; ++j) k[j] = 0.f;
-            }
-            float a = 0.f, c = 0.f;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-                a = fmaf(q0[j], k[j], a);
-                c = fmaf(q1[j], k[j], c);
-            }
-            sc0[r] = a;
-            sc1[r] = c;
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-#pragma unroll
-            for (int r = 0; r < RW; ++r) {
-                sc0[r] += __shfl_xor_sync(0xffffffffu, sc0[r], o);
-                sc1[r] += __shfl_xor_sync(0xffffffffu, sc1[r], o);
-            }
-        }
-        float mx0 = m0, mx1 = m1;
-#pragma unroll
-        for (int r = 0; r < RW; ++r) {
-            if (warp + 8 * r < nr) {
-                mx0 = fmaxf(mx0, sc0[r]);
-                mx1 = fmaxf(mx1, sc1[r]);
-            }
-        }
-        // A warp with no valid row in this tile keeps mx == m == -inf; its
-        // rescale factor must then be 1, not 2^(-inf - -inf) = NaN.
-        const float al0 = mx0 == -INFINITY ? 1.f : ex2_approx(m0 - mx0);
-        const float al1 = mx1 == -INFINITY ? 1.f : ex2_approx(m1 - mx1);
-        m0 = mx0;
-        m1 = mx1;
-        l0 *= al0;
-        l1 *= al1;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            o0[j] *= al0;
-            o1[j] *= al1;
-        }
-#pragma unroll
-        for (int r = 0; r < RW; ++r) {
-            const int row = warp + 8 * r;
-            if (row < nr) {
-                const float p0 = ex2_approx(sc0[r] - m0), p1 = ex2_approx(sc1[r] - m1);
-                l0 += p0;
-                l1 += p1;
-                float v[8];
-                load_row8<KVT>(vt + (size_t)row * kHeadDim, lane, v);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    o0[j] = fmaf(p0, v[j], o0[j]);
-                    o1[j] = fmaf(p1, v[j], o1[j]);
-                }
-            }
-        }
+        decode_tile<KVT>(kbuf + (size_t)s * TK * kHeadDim, vbuf + (size_t)s * TK * kHeadDim, nr, warp, lane, q0, q1,
+                         acc_st);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
         if (threadIdx.x == 0 && i + NS < ntiles) {
@@ -603,36 +711,12 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
     __syncthreads();
 
     // Combine the 8 warps' (m, l, o) through shared memory (the K ring is
-    // free now): acc[warp][head][256].
+    // free now).
     float *acc = reinterpret_cast<float *>(smem);
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        acc[(warp * 2 + 0) * kHeadDim + lane_dim<KVT>(lane, j)] = o0[j];
-        acc[(warp * 2 + 1) * kHeadDim + lane_dim<KVT>(lane, j)] = o1[j];
-    }
-    if (lane == 0) {
-        wm[warp][0] = m0;
-        wm[warp][1] = m1;
-        wl[warp][0] = l0;
-        wl[warp][1] = l1;
-    }
-    __syncthreads();
-    const int hh = threadIdx.x >> 7;         // head within the group
-    const int d = (threadIdx.x & 127) * 2;   // two dims per thread
-    float M = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < 8; ++w) M = fmaxf(M, wm[w][hh]);
-    float Ls = 0.f, A = 0.f, Bv = 0.f;
-    if (M != -INFINITY) {
-#pragma unroll
-        for (int w = 0; w < 8; ++w) {
-            if (wm[w][hh] == -INFINITY) continue;  // warp saw no row
-            const float f = ex2_approx(wm[w][hh] - M);
-            Ls += wl[w][hh] * f;
-            A += acc[(w * 2 + hh) * kHeadDim + d] * f;
-            Bv += acc[(w * 2 + hh) * kHeadDim + d + 1] * f;
-        }
-    }
+    float M, Ls, A, Bv;
+    combine_warps<KVT>(acc_st, acc, wm, wl, warp, lane, M, Ls, A, Bv);
+    const int hh = threadIdx.x >> 7;
+    const int d = (threadIdx.x & 127) * 2;
     const int h = 2 * g + hh;
     if (p.write_partial) {
         float *dst = p.partial + (((size_t)b * kHeads + h) * p.nsplit + split) * (kHeadDim + 2);
@@ -645,42 +729,14 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
         if (kFused && p.tickets) {
             // Split-K style completion: the last split of this (seq, kv head)
             // to finish merges all partials; no CTA ever waits for another.
-            __threadfence();
             __syncthreads();
             G3_DTRACE(4);
-            if (threadIdx.x == 0) s_last = atomicAdd(&p.tickets[b * kKvHeads + g], 1u) == (unsigned)(p.nsplit - 1);
+            if (threadIdx.x == 0)
+                s_last = atom_add_acqrel_gpu(&p.tickets[b * kKvHeads + g], 1u) == (unsigned)(p.nsplit - 1);
             __syncthreads();
             if (!s_last) return;
-            __threadfence();
-            // (m, l) of every split and head in one parallel round of loads,
-            // then the O sums with eight independent loads in flight.
-            float *sm_m = reinterpret_cast<float *>(smem);          // [2][nsplit]
-            float *sm_l = sm_m + 2 * kMaxSplitFused;                 // [2][nsplit]
-            for (int t = threadIdx.x; t < 2 * p.nsplit; t += 256) {
-                const int th = t / p.nsplit, ts = t % p.nsplit;
-                const float *pp = p.partial + (((size_t)b * kHeads + 2 * g + th) * p.nsplit + ts) * (kHeadDim + 2);
-                sm_m[th * kMaxSplitFused + ts] = __ldcg(pp);
-                sm_l[th * kMaxSplitFused + ts] = __ldcg(pp + 1);
-            }
-            __syncthreads();
-            const float *mh = sm_m + hh * kMaxSplitFused, *lh = sm_l + hh * kMaxSplitFused;
-            float Mx = -INFINITY;
-            for (int i = 0; i < p.nsplit; ++i) Mx = fmaxf(Mx, mh[i]);
-            const float *base = p.partial + ((size_t)b * kHeads + h) * p.nsplit * (kHeadDim + 2);
-            float Lt = 0.f, At = 0.f, Bt = 0.f;
-            if (Mx != -INFINITY) {
-#pragma unroll 8
-                for (int i = 0; i < p.nsplit; ++i) {
-                    const float f = mh[i] == -INFINITY ? 0.f : ex2_approx(mh[i] - Mx);
-                    const float2 o = __ldcg(reinterpret_cast<const float2 *>(base + (size_t)i * (kHeadDim + 2) + 2 + d));
-                    Lt += lh[i] * f;
-                    At += o.x * f;
-                    Bt += o.y * f;
-                }
-            }
-            const float inv = Lt > 0.f ? 1.0f / Lt : 0.f;
-            *reinterpret_cast<float2 *>(p.out + (size_t)b * kHeads * kHeadDim + h * kHeadDim + d) =
-                make_float2(At * inv, Bt * inv);
+            merge_group(p.partial + ((size_t)b * kHeads + 2 * g) * p.nsplit * (kHeadDim + 2),
+                        (size_t)p.nsplit * (kHeadDim + 2), p.nsplit, p.out + (size_t)b * kHeads * kHeadDim + 2 * g * kHeadDim);
             if (threadIdx.x == 0) p.tickets[b * kKvHeads + g] = 0u;
             G3_DTRACE(5);
         }
@@ -1133,7 +1189,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         // ------------------------------------------------ softmax warps 0-7
         const int row = threadIdx.x & 127;  // TMEM lane == S/O row
         const int half = threadIdx.x >> 7;  // keys [32*half, +32), O cols [128*half, +128)
-        const int tr = row & 63, hh = row >> 6;
+        const int tr = row & 63;
         const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
         bool ok = true;
         int gi = 0, uk = 0;

@@ -623,7 +623,6 @@ static void plan_decode(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_i
     const LayerState &L = ctx->layers[layer];
     constexpr int TK = g3::DecodeCfg<KVT>::TK;
     pl.rows.B = B;
-    long long total = 0;
     int maxrows = 0;
     for (int b = 0; b < B; ++b) {
         pl.rows.seq[b] = seq_ids[b];
@@ -636,22 +635,46 @@ static void plan_decode(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_i
             n = std::min(pos[b] + 1, kWindow);
         }
         pl.rows.nrows[b] = n;
-        total += (long long)n * kKvHeads;
         maxrows = std::max(maxrows, n);
     }
-    // Aim for ~8 CTAs per SM over the call (2 resident x 4 waves), but give
-    // every CTA at least 512 rows when there is work for a full wave of
-    // those (each CTA pays a fixed start -- barrier set-up, its q prologue,
-    // the first copies' latency -- that short CTAs cannot amortise); at
-    // least 4 tiles per CTA; never more than kMaxSplit splits.
-    const long long target = 148LL * 8;
-    const long long one_wave = 148LL * 2;
-    const long long min_rows = 512;
-    const int min_tiles = 4;
-    long long chunk = std::max<long long>((long long)min_tiles * TK, (total + target - 1) / target);
-    chunk = std::max<long long>(chunk, std::min<long long>(min_rows, (total + one_wave - 1) / one_wave));
-    chunk = std::max<long long>(chunk, (maxrows + kMaxSplit - 1) / kMaxSplit);
-    chunk = (chunk + TK - 1) / TK * TK;
+    // Rows per split from a cost model of the split kernel, calibrated on
+    // B200 measurements.  Two CTAs are resident per SM; each streams its K/V
+    // rows at ~22.6 GB/s (all 2 x SMs slots together saturate HBM) and pays
+    // a fixed ~4 us (launch, first-copy latency, prologue) plus ~2 us when
+    // its result is a partial to merge.  Splits of one call are near equal,
+    // so they run in waves: a call of N CTAs takes ceil(N / slots) CTA
+    // times, where a unit's last split shorter than a quarter split is not
+    // counted (it ends within its wave).  The model picks, e.g., B=8 x 1024
+    // local rows: 8 splits of 128 (one wave); B=64 x 1024: one split each;
+    // B=64 x 32K global rows: splits of ~4K rows (7 full waves).  Splits hold
+    // at least 2 tiles, and a unit at most kMaxSplit.
+    const int units = B * kKvHeads;
+    const int slots = 2 * ctx->sm_count;
+    const double row_bytes = 2.0 * kHeadDim * sizeof(KVT);
+    constexpr double kRate = 22.6e3;  // bytes per us per CTA
+    constexpr double kFixed = 4.0, kMergeCost = 2.0;
+    long long chunk = 0;
+    double best = 1e300;
+    for (int s = 1; s <= kMaxSplit; ++s) {
+        long long c = (maxrows + s - 1) / s;
+        c = std::max<long long>(c, 2 * TK);
+        c = (c + TK - 1) / TK * TK;
+        const long long ns = (maxrows + c - 1) / c;
+        if (ns > kMaxSplit) continue;
+        const long long last = maxrows - (ns - 1) * c;
+        const long long big = (long long)units * (ns - (ns > 1 && 4 * last < c ? 1 : 0));
+        const long long waves = std::max<long long>(1, (big + slots - 1) / slots);
+        const double t = waves * (c * row_bytes / kRate + kFixed + (ns > 1 ? kMergeCost : 0.0));
+        if (t < best * (1.0 - 1e-9)) {
+            best = t;
+            chunk = c;
+        }
+        if (c == 2 * TK) break;  // smaller splits only repeat this one
+    }
+#ifdef G3_PLAN_ENV  // development-only planner override, compiled out of the library
+    if (const char *e = getenv(L.is_global ? "G3_CHUNK_GLOBAL" : "G3_CHUNK_LOCAL"))
+        if (atoi(e) > 0) chunk = std::max<long long>(atoi(e), (maxrows + kMaxSplit - 1) / kMaxSplit);
+#endif
     pl.chunk = (int)chunk;
     pl.nsplit = std::max(1, (int)((maxrows + chunk - 1) / chunk));
 }

@@ -21,6 +21,17 @@ enum : unsigned {
 // A bounded wait gives up after this much wall-clock time (globaltimer ns).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
+// Atomic add with acquire-release semantics at GPU scope.  After a CTA
+// barrier, one thread's release covers the stores every thread of the CTA
+// made before the barrier (fence cumulativity), so a split that publishes a
+// partial needs no per-thread fence; its acquire side likewise covers the
+// whole CTA after the next barrier.
+__device__ __forceinline__ unsigned atom_add_acqrel_gpu(unsigned *p, unsigned v) {
+    unsigned old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));

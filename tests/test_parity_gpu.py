@@ -282,3 +282,62 @@ def test_bounded_wait_times_out_and_context_survives(ropes):
     out = ctx.attn_decode(0, [0], [0], Q, K, V)  # position 0 attends only itself: out == v
     assert np.allclose(out.reshape(8, 256), V.reshape(4, 256)[np.arange(8) // 2], atol=1e-5)
     ctx.close()
+
+
+def _bf16_cache(kr, vr, rows):
+    import torch
+    kr[:rows] = torch.from_numpy(kr[:rows]).bfloat16().float().numpy()
+    vr[:rows] = torch.from_numpy(vr[:rows]).bfloat16().float().numpy()
+
+
+@pytest.mark.parametrize("kv", [gc.KV_F32, gc.KV_BF16])
+@pytest.mark.parametrize("layer,positions", [
+    # local: units of 172..1024 rows, runs of ~167 rows straddling units
+    (0, [170, 171, 255, 300, 511, 700, 1022, 1023, 1024, 1500, 2047, 2048, 3000, 4000, 5000, 8190]),
+    # local: one 128-row unit per run (a segment is the whole unit)
+    (0, [127]),
+    # global: long units, many runs per unit
+    (5, [600, 700, 1000, 1500, 2000, 3000, 4095, 8190]),
+])
+def test_decode_streamk_runs(oracle, ropes, kv, layer, positions):
+    """Short decode calls run as equal row runs over (seq, kv head) units
+    (stream-K), the last run of a unit merging its partials: two consecutive
+    steps per sequence (the second reads the row the first appended) against
+    the reference, for mixed lengths, runs covering two units and units
+    covered by a single run."""
+    glob = gc.is_global_layer(layer)
+    rope = ropes[1] if glob else ropes[0]
+    qn, kn = synth.qk_norm_gains(500 + layer)
+    B = len(positions)
+    ctx = make_ctx(ropes, kv, max_batch=B)
+    ctx.set_qk_norm(layer, qn, kn)
+    caches, toks, wants = [], [], []
+    for s, p in enumerate(positions):
+        c = oracle.new_cache(glob, 8192)
+        kr, vr = oracle.cache_arrays(c)
+        rows = p if glob else min(p, 1024)
+        kr[:rows] = synth.normal(600 + 3 * s, (rows, 4, 256))
+        vr[:rows] = synth.normal(601 + 3 * s, (rows, 4, 256))
+        if kv == gc.KV_BF16:
+            _bf16_cache(kr, vr, rows)
+        ctx.import_cache(layer, s, kr[:rows].copy(), vr[:rows].copy())
+        Q, K, V = qkv(700 + 5 * s, 2)
+        wants.append(oracle.attn_core_tokens(c, Q, K, V, qn, kn, rope, p))
+        toks.append((Q, K, V))
+        caches.append(c)
+    seqs = list(range(B))
+    for step in range(2):
+        got = ctx.attn_decode(layer, seqs, [p + step for p in positions], np.stack([t[0][step] for t in toks]),
+                              np.stack([t[1][step] for t in toks]), np.stack([t[2][step] for t in toks]))
+        for b in range(B):
+            assert rel_err(got[b], wants[b][step]) <= TOL, (step, b, rel_err(got[b], wants[b][step]))
+    if kv == gc.KV_F32:
+        for s, p in enumerate(positions):
+            kd, vd = ctx.export_cache(layer, s)
+            _, vr = oracle.cache_arrays(caches[s])
+            for q in (p, p + 1):
+                slot = q if glob else q % 1024
+                assert np.array_equal(vd[slot], vr[slot]), (s, q)
+    for c in caches:
+        oracle.free_cache(c)
+    ctx.close()
