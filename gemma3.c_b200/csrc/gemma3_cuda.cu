@@ -1559,9 +1559,10 @@ extern "C" int gemma3_cuda_profile_read(gemma3_cuda_ctx *ctx, int kernel, long l
 }
 
 // ------------------------------------------------------------------ decode without allocation
-// For callers that cannot allocate device memory: code that runs while a
-// CUDA graph is being captured, hosts whose memory budget is fixed when the
-// process starts, and embedders that hand every device buffer in themselves.
+// For callers that cannot allocate device memory: serving loops that may not
+// stall on cudaMalloc's implicit device synchronisation, hosts whose memory
+// budget is fixed when the process starts, and embedders that hand every
+// device buffer in themselves.
 // The split-KV decode needs scratch (the scaled queries and the per-split
 // (m, l, O) partials); here it lives in one file-scope device array that
 // every GPU which loads this library holds until the process exits.

@@ -330,9 +330,10 @@ int gemma3_cuda_profile_read(gemma3_cuda_ctx *ctx, int kernel, long long *launch
                              double *ms, double *work);
 
 /* GQA decode that allocates no memory.  No counterpart in the reference: it
- * exists for callers that cannot allocate device memory -- code running while
- * a CUDA graph is captured, processes whose device memory budget is fixed up
- * front, embedders that supply every buffer themselves.  It runs the same
+ * exists for callers that cannot allocate device memory -- hosts that may not
+ * stall on cudaMalloc's implicit device synchronisation inside a serving
+ * loop, processes whose device memory budget is fixed up front, embedders
+ * that supply every buffer themselves.  It runs the same
  * split-KV kernels as gemma3_cuda_attn_decode_dev on a cache the caller owns,
  * keeping its scratch (scaled queries and split partials) in a static device
  * array of 4.6 MB that every GPU loading this library holds until exit.

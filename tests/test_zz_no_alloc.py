@@ -1,9 +1,9 @@
 """The no-allocation decode entry point (gemma3_cuda_gqa_decode_noalloc),
 called through the C-ABI, against the context path gemma3_cuda_attn_decode.
 
-This entry point serves callers that cannot allocate device memory (code
-running under CUDA graph capture, fixed-budget processes, embedders owning
-all buffers); its scratch is a static device array.  The test drives the
+This entry point serves callers that cannot allocate device memory (serving
+loops that may not stall on cudaMalloc's device synchronisation, fixed-budget
+processes, embedders owning all buffers); its scratch is a static device array.  The test drives the
 existing entry point with QK-norm off and identity RoPE tables, so the raw Q
 is exactly the query both paths attend with, exports the cache the existing
 path built, and checks two consecutive no-allocation calls against it within
