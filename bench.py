@@ -363,9 +363,16 @@ def headline(args, dist, torch, gc, synth, pk):
     vh = v.cpu().pin_memory().numpy()
     oh = torch.empty(N_LAYERS, Bl, 2048).pin_memory().numpy()
 
+    # the host-pointer entry point called per layer as a C host calls it:
+    # host pointers converted once, outside the timed loop
+    fn_h = ctx.lib.gemma3_cuda_attn_decode
+    hptrs = [tuple(a[l].ctypes.data_as(ctypes.POINTER(ctypes.c_float)) for a in (qh, kh, vh, oh))
+             for l in range(N_LAYERS)]
+
     def step_e2e():
         for l in range(N_LAYERS):
-            ctx.attn_decode(l, seqs, pos, qh[l], kh[l], vh[l], out=oh[l])
+            if fn_h(h, l, Bl, sp, pp, *hptrs[l]) != 0:
+                raise RuntimeError(ctx.last_error())
 
     step_e2e()
     dist.barrier()

@@ -219,6 +219,7 @@ struct gemma3_cuda_ctx {
     float *io = nullptr;
     size_t io_rows = 0;
     unsigned *err = nullptr;
+    unsigned *err_host = nullptr;  // pinned copy of *err, read back on the stream
     long long launches = 0;
     int sm_count = 148;
     g3NcclComm comm = nullptr;
@@ -285,6 +286,7 @@ static void ctx_release(gemma3_cuda_ctx *c) {
         cudaFree(L.wdown);
         cudaFree(L.ln);
     }
+    if (c->err_host) cudaFreeHost(c->err_host);
     cudaFree(c->gu);
     cudaFree(c->hb);
     cudaFree(c->delta);
@@ -356,6 +358,8 @@ static int ctx_alloc(gemma3_cuda_ctx *c) {
     CU_TRY(cudaMalloc(&c->io, c->io_rows * (2048 + 1024 + 1024 + 2048) * sizeof(float)));
     CU_TRY(cudaMalloc(&c->err, sizeof(unsigned)));
     CU_TRY(cudaMemsetAsync(c->err, 0, sizeof(unsigned), c->stream));
+    CU_TRY(cudaHostAlloc((void **)&c->err_host, sizeof(unsigned), cudaHostAllocDefault));
+    *c->err_host = 0;
     CU_TRY(cudaFuncSetAttribute(g3::prefill_fa_sm100, cudaFuncAttributeMaxDynamicSharedMemorySize, g3::kPfSmem));
     CU_TRY(cudaFuncSetAttribute(g3::proj_gemm_sm100, cudaFuncAttributeMaxDynamicSharedMemorySize, g3::kProjSmem));
     const int dsm_bf = g3::DecodeCfg<__nv_bfloat16>::NS * 2 * g3::DecodeCfg<__nv_bfloat16>::TK * kHeadDim * 2;
@@ -409,9 +413,11 @@ extern "C" long long gemma3_cuda_launch_count(gemma3_cuda_ctx *ctx) { return ctx
 extern "C" int gemma3_cuda_synchronize(gemma3_cuda_ctx *ctx) {
     if (!ctx) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null context");
     CU_TRY(cudaSetDevice(ctx->cfg.device));
+    // The status word comes back on the stream behind the call's own work,
+    // so one stream synchronisation covers both (no second blocking copy).
+    CU_TRY(cudaMemcpyAsync(ctx->err_host, ctx->err, sizeof(unsigned), cudaMemcpyDeviceToHost, ctx->stream));
     CU_TRY(cudaStreamSynchronize(ctx->stream));
-    unsigned e = 0;
-    CU_TRY(cudaMemcpy(&e, ctx->err, sizeof e, cudaMemcpyDeviceToHost));
+    const unsigned e = *ctx->err_host;
     if (e) {
         // an aborted launch may leave split tickets counted: start clean
         cudaMemsetAsync(ctx->tickets, 0, (size_t)ctx->cfg.max_batch * kKvHeads * sizeof(unsigned), ctx->stream);
