@@ -673,22 +673,39 @@ def secondary_context_parallel(args, dist, torch, gc, pk):
         for l in range(N_LAYERS):
             c.attn_decode_dev(l, seqs, poss, q[l].data_ptr(), k[l].data_ptr(), v[l].data_ptr(), out[l].data_ptr())
 
-    for _ in range(args.warmup):
-        step()
-    c.synchronize()
-    dist.barrier()
     steps = max(args.steps, 10)
-    ms = dist.max(ev_time(torch, stream, lambda: [step() for _ in range(steps)]))
-    c.synchronize()
+
+    def timed():
+        for _ in range(args.warmup):
+            step()
+        c.synchronize()
+        dist.barrier()
+        t = dist.max(ev_time(torch, stream, lambda: [step() for _ in range(steps)]))
+        c.synchronize()
+        return t
+
+    ms = ms_nccl = timed()
+    if dist.world > 1:
+        # fused exchange: merged partials stored into the peers' buffers over
+        # NVLink by the merge kernel, flags instead of a library collective
+        c.peer_init()
+        ms = timed()
+    dist.barrier()
     c.close()
     del q, k, v, out
     torch.cuda.empty_cache()
     byts = (len(GLOBAL_LAYERS) * ctxlen + (N_LAYERS - len(GLOBAL_LAYERS)) * 1024) * B * ROW_BYTES_BF16
     gbs = byts * steps / (ms / 1e3) / 1e9
-    return {"workload": "configs[4] long-context decode, B=4 @ 131072 keys, global-layer KV split over "
-                        f"{dist.world} GPU(s), NCCL all-gather + LSE merge; local layers on every rank",
-            "value": round(gbs, 1), "unit": "GB/s", "ms_per_step": round(ms / steps, 3),
-            "algorithmic_bytes_per_step": byts, "frac_of_n_x_hbm": round(gbs / (pk["hbm_gbs"] * dist.world), 4)}
+    xchg = ("merge kernel stores partials into peers' buffers over NVLink + flag wait + LSE merge"
+            if dist.world > 1 else "no exchange")
+    res = {"workload": "configs[4] long-context decode, B=4 @ 131072 keys, global-layer KV split over "
+                       f"{dist.world} GPU(s), {xchg}; local layers on every rank",
+           "value": round(gbs, 1), "unit": "GB/s", "ms_per_step": round(ms / steps, 3),
+           "algorithmic_bytes_per_step": byts, "frac_of_n_x_hbm": round(gbs / (pk["hbm_gbs"] * dist.world), 4)}
+    if dist.world > 1:
+        res["nccl_allgather"] = {"value": round(byts * steps / (ms_nccl / 1e3) / 1e9, 1),
+                                 "ms_per_step": round(ms_nccl / steps, 3)}
+    return res
 
 
 def ncu_traffic(kernel, bytes_per_launch):
@@ -824,7 +841,7 @@ def main():
                                  "model": secondary_model(args, torch, gc, pk, dist.local)}
     if not args.no_secondary:
         line.setdefault("secondary", {})["context_parallel"] = cp
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and dist.rank == 0 and dist.world == 1:
             try:
                 line["cpu_baseline"] = cpu_baseline_sample()
             except Exception as e:  # reported, never silently replaced

@@ -786,6 +786,122 @@ __global__ void __launch_bounds__(256) merge_partials(const float *__restrict__ 
 }
 
 // ------------------------------------------------------------------------
+// Context-parallel exchange over peer memory (global layers split across
+// GPUs).  Every rank owns a receive buffer [2 parity][R ranks][B][8][258]
+// and flags [2 parity][8]; each rank maps all ranks' buffers (CUDA IPC).
+// merge_partials_push merges this rank's split partials and stores the
+// merged (m, l, O) of each (seq, head) straight into slot `me` of every
+// rank's receive buffer over NVLink; its last CTA (grid ticket) then raises
+// flag `me` of every rank to the exchange's epoch.  merge_peer_partials
+// waits (bounded) until all R flags of this rank carry the epoch and merges
+// the R partials into the output.  Exchange t uses parity t & 1: a rank can
+// only start exchange t+2 after every rank has pushed t+1, which each rank
+// does only after its merge of t, so a parity is never overwritten while a
+// rank still reads it.
+// ------------------------------------------------------------------------
+constexpr int kMaxPeers = 8;
+struct PeerXchg {
+    float *gather[kMaxPeers];    // rank r's receive buffer (mapped here)
+    unsigned *flags[kMaxPeers];  // rank r's flags [2][kMaxPeers]
+    unsigned *counter;           // this rank's grid ticket (0 between calls)
+    size_t rank_stride;          // floats per rank slot: max_batch * 8 * 258
+    size_t parity_stride;        // R * rank_stride
+    unsigned epoch;              // > 0, same sequence on every rank
+    int me, R;
+};
+
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned *p, unsigned v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__global__ void __launch_bounds__(256) merge_partials_push(const float *__restrict__ partials, int nparts,
+                                                           size_t bstride, size_t hstride, size_t pstride,
+                                                           const PeerXchg px) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int b = blockIdx.x / kHeads, h = blockIdx.x % kHeads, d = threadIdx.x;
+    const float *base = partials + (size_t)b * bstride + (size_t)h * hstride;
+    float M = -INFINITY;
+    for (int i = 0; i < nparts; ++i) M = fmaxf(M, base[(size_t)i * pstride]);
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+        for (int i = 0; i < nparts; ++i) {
+            const float *pp = base + (size_t)i * pstride;
+            if (pp[0] == -INFINITY) continue;
+            const float f = ex2_approx(pp[0] - M);
+            L += pp[1] * f;
+            O += pp[2 + d] * f;
+        }
+    }
+    const size_t off = (size_t)(px.epoch & 1u) * px.parity_stride + (size_t)px.me * px.rank_stride +
+                       ((size_t)b * kHeads + h) * (kHeadDim + 2);
+    for (int r = 0; r < px.R; ++r) {
+        float *e = px.gather[r] + off;
+        if (d == 0) {
+            e[0] = M;
+            e[1] = L;
+        }
+        e[2 + d] = O;
+    }
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (atomicAdd(px.counter, 1u) == gridDim.x - 1) {
+            // every CTA's stores are fenced before its ticket: publish
+            *px.counter = 0u;
+            __threadfence_system();
+            for (int r = 0; r < px.R; ++r) st_release_sys(px.flags[r] + (px.epoch & 1u) * kMaxPeers + px.me, px.epoch);
+        }
+    }
+}
+
+__global__ void __launch_bounds__(256) merge_peer_partials(const PeerXchg px, float *__restrict__ out,
+                                                           unsigned *err) {
+    pdl_launch_dependents();
+    pdl_wait();
+    __shared__ int ok;
+    const unsigned par = px.epoch & 1u;
+    if (threadIdx.x == 0) {
+        const unsigned *f = px.flags[px.me] + par * kMaxPeers;
+        const uint64_t t0 = globaltimer_ns();
+        bool good = true;
+        for (int r = 0; good && r < px.R; ++r) {
+            for (uint32_t i = 1; ld_acquire_sys(f + r) != px.epoch; ++i) {
+                if ((i & 63u) == 0 && (*(volatile unsigned *)err || globaltimer_ns() - t0 > kWaitLimitNs)) {
+                    good = false;
+                    break;
+                }
+            }
+        }
+        if (!good) atomicOr(err, kErrWaitTimeout);
+        ok = good;
+    }
+    __syncthreads();
+    if (!ok) return;
+    const int b = blockIdx.x / kHeads, h = blockIdx.x % kHeads, d = threadIdx.x;
+    const float *base = px.gather[px.me] + (size_t)par * px.parity_stride + ((size_t)b * kHeads + h) * (kHeadDim + 2);
+    float M = -INFINITY;
+    for (int r = 0; r < px.R; ++r) M = fmaxf(M, __ldcg(base + (size_t)r * px.rank_stride));
+    float L = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+        for (int r = 0; r < px.R; ++r) {
+            const float *pp = base + (size_t)r * px.rank_stride;
+            const float m = __ldcg(pp);
+            if (m == -INFINITY) continue;
+            const float f = ex2_approx(m - M);
+            L += __ldcg(pp + 1) * f;
+            O += __ldcg(pp + 2 + d) * f;
+        }
+    }
+    out[(size_t)b * kHeads * kHeadDim + h * kHeadDim + d] = L > 0.f ? O / L : 0.f;
+}
+
+// ------------------------------------------------------------------------
 // Prefill flash attention on tcgen05 / TMEM (persistent CTAs).
 //
 // Work unit = (block of 64 query tokens, kv head g); the MMA M dimension

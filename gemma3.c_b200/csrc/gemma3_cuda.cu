@@ -89,6 +89,7 @@ static int nccl_load() {
     return 0;
 }
 static const int kNcclFloat32 = 7;  // ncclFloat32 in nccl.h
+static const int kNcclInt8 = 0;     // ncclInt8 in nccl.h
 
 // ------------------------------------------------------------------ TMA encode (driver entry point)
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -223,6 +224,14 @@ struct gemma3_cuda_ctx {
     long long launches = 0;
     int sm_count = 148;
     g3NcclComm comm = nullptr;
+    // peer-memory exchange of the context-parallel split (gemma3_cuda_peer_init)
+    float *pgather = nullptr;     // own receive buffer [2][kv_ranks][max_batch][8][258]
+    unsigned *pflags = nullptr;   // own flags [2][kMaxPeers]
+    unsigned *pcounter = nullptr; // grid ticket of merge_partials_push
+    float *peer_g[g3::kMaxPeers] = {};
+    unsigned *peer_f[g3::kMaxPeers] = {};
+    bool peer_ready = false, use_peer = false;
+    unsigned xepoch = 0;
     // profiling of the dominant kernels (decode_splitkv = 0, prefill_fa = 1)
     bool prof = false;
     std::vector<cudaEvent_t> ev_pool;
@@ -276,6 +285,14 @@ static void ctx_release(gemma3_cuda_ctx *c) {
     cudaSetDevice(c->cfg.device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     if (c->comm && g_nccl.ok) g_nccl.commDestroy(c->comm);
+    for (int r = 0; r < g3::kMaxPeers; ++r)
+        if (r != c->cfg.kv_rank) {
+            if (c->peer_g[r]) cudaIpcCloseMemHandle(c->peer_g[r]);
+            if (c->peer_f[r]) cudaIpcCloseMemHandle(c->peer_f[r]);
+        }
+    cudaFree(c->pgather);
+    cudaFree(c->pflags);
+    cudaFree(c->pcounter);
     for (auto &L : c->layers) {
         cudaFree(L.kv);
         cudaFree(L.qn);
@@ -691,7 +708,8 @@ static void plan_decode(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_i
 // partial per (seq, head) into `partial_out` [B][8][258] via merge_partials.
 template <typename KVT>
 static int decode_impl(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_ids, const int *pos, const float *Q,
-                       const float *K, const float *V, float *out, float *partial_out) {
+                       const float *K, const float *V, float *out, float *partial_out,
+                       const g3::PeerXchg *px = nullptr) {
     DecodePlan pl;
     plan_decode<KVT>(ctx, layer, B, seq_ids, pos, pl);
     g3::LayerDev L = layer_dev(ctx, layer);
@@ -739,7 +757,13 @@ static int decode_impl(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_id
         prof_end(ctx, 0, e0, rows * kKvHeads * 2.0 * kHeadDim * sizeof(KVT));
     }
     if (int r = check_launch(ctx, 1)) return r;
-    if (p.write_partial && !p.tickets) {
+    if (px) {
+        // merged partial straight into every rank's receive buffer (NVLink)
+        const size_t hs = (size_t)pl.nsplit * kPartialStride;
+        launch_pdl(g3::merge_partials_push, dim3(B * kHeads), dim3(256), 0, ctx->stream, (const float *)ctx->partial,
+                   pl.nsplit, (size_t)(kHeads * hs), hs, (size_t)kPartialStride, *px);
+        if (int r = check_launch(ctx, 1)) return r;
+    } else if (p.write_partial && !p.tickets) {
         const size_t hs = (size_t)pl.nsplit * kPartialStride;
         launch_pdl(g3::merge_partials, dim3(B * kHeads), dim3(256), 0, ctx->stream, (const float *)ctx->partial,
                    pl.nsplit, (size_t)(kHeads * hs), hs, (size_t)kPartialStride, out, partial_out);
@@ -749,10 +773,27 @@ static int decode_impl(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_id
 }
 
 static int decode_dispatch(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_ids, const int *pos,
-                           const float *Q, const float *K, const float *V, float *out, float *partial_out) {
+                           const float *Q, const float *K, const float *V, float *out, float *partial_out,
+                           const g3::PeerXchg *px = nullptr) {
     if (ctx->cfg.kv_dtype == GEMMA3_CUDA_KV_BF16)
-        return decode_impl<__nv_bfloat16>(ctx, layer, B, seq_ids, pos, Q, K, V, out, partial_out);
-    return decode_impl<float>(ctx, layer, B, seq_ids, pos, Q, K, V, out, partial_out);
+        return decode_impl<__nv_bfloat16>(ctx, layer, B, seq_ids, pos, Q, K, V, out, partial_out, px);
+    return decode_impl<float>(ctx, layer, B, seq_ids, pos, Q, K, V, out, partial_out, px);
+}
+
+// Kernel parameters of the next peer-memory exchange (advances the epoch).
+static void peer_params(gemma3_cuda_ctx *ctx, g3::PeerXchg *px) {
+    const int R = ctx->cfg.kv_ranks;
+    for (int r = 0; r < g3::kMaxPeers; ++r) {
+        px->gather[r] = r < R ? ctx->peer_g[r] : nullptr;
+        px->flags[r] = r < R ? ctx->peer_f[r] : nullptr;
+    }
+    px->counter = ctx->pcounter;
+    px->rank_stride = (size_t)ctx->cfg.max_batch * kHeads * kPartialStride;
+    px->parity_stride = (size_t)R * px->rank_stride;
+    if (++ctx->xepoch == 0) ctx->xepoch = 1;  // 0 is the flags' initial value
+    px->epoch = ctx->xepoch;
+    px->me = ctx->cfg.kv_rank;
+    px->R = R;
 }
 
 extern "C" int gemma3_cuda_merge_partials_dev(gemma3_cuda_ctx *ctx, int n_parts, int B, const float *partials,
@@ -783,6 +824,15 @@ extern "C" int gemma3_cuda_attn_decode_dev(gemma3_cuda_ctx *ctx, int layer, int 
     CU_TRY(cudaSetDevice(ctx->cfg.device));
     const bool split = ctx->layers[layer].is_global && ctx->cfg.kv_ranks > 1;
     if (!split) return decode_dispatch(ctx, layer, B, seq_ids, pos, Q, K, V, out, nullptr);
+    if (ctx->use_peer) {
+        // fused exchange: merge + NVLink push in one kernel, bounded flag
+        // wait + final merge in the next
+        g3::PeerXchg px;
+        peer_params(ctx, &px);
+        if (int r = decode_dispatch(ctx, layer, B, seq_ids, pos, Q, K, V, nullptr, ctx->emit, &px)) return r;
+        launch_pdl(g3::merge_peer_partials, dim3(B * kHeads), dim3(256), 0, ctx->stream, px, out, ctx->err);
+        return check_launch(ctx, 1);
+    }
     if (!ctx->comm)
         return fail(GEMMA3_CUDA_ERR_INVALID_ARG,
                     "global layer of a context-parallel context needs gemma3_cuda_comm_init (or the partial API)");
@@ -1426,6 +1476,77 @@ extern "C" int gemma3_cuda_comm_init(gemma3_cuda_ctx *ctx, const void *id_128_by
         return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "ncclCommInitRank failed: %s",
                     g_nccl.getErrorString ? g_nccl.getErrorString(nr) : "?");
     }
+    return 0;
+}
+
+// Peer-memory exchange: every rank exports its receive buffer and flags
+// (CUDA IPC), the handles travel over the communicator (an NCCL all-gather
+// of 128 bytes per rank), and every rank maps the others'.  Collective:
+// all kv_ranks contexts call it.
+extern "C" int gemma3_cuda_peer_init(gemma3_cuda_ctx *ctx) {
+    if (!ctx) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null context");
+    const int R = ctx->cfg.kv_ranks, me = ctx->cfg.kv_rank;
+    if (R < 2 || R > g3::kMaxPeers)
+        return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "peer exchange needs 2 <= kv_ranks <= %d", g3::kMaxPeers);
+    if (!ctx->comm) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "peer exchange needs gemma3_cuda_comm_init first");
+    if (ctx->peer_ready) return 0;
+    CU_TRY(cudaSetDevice(ctx->cfg.device));
+    const size_t gfloats = 2 * (size_t)R * ctx->cfg.max_batch * kHeads * kPartialStride;
+    CU_TRY(cudaMalloc(&ctx->pgather, gfloats * 4));
+    CU_TRY(cudaMalloc(&ctx->pflags, 2 * g3::kMaxPeers * sizeof(unsigned)));
+    CU_TRY(cudaMalloc(&ctx->pcounter, sizeof(unsigned)));
+    CU_TRY(cudaMemsetAsync(ctx->pgather, 0, gfloats * 4, ctx->stream));
+    CU_TRY(cudaMemsetAsync(ctx->pflags, 0, 2 * g3::kMaxPeers * sizeof(unsigned), ctx->stream));
+    CU_TRY(cudaMemsetAsync(ctx->pcounter, 0, sizeof(unsigned), ctx->stream));
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    unsigned char mine[128];
+    cudaIpcMemHandle_t hg, hf;
+    CU_TRY(cudaIpcGetMemHandle(&hg, ctx->pgather));
+    CU_TRY(cudaIpcGetMemHandle(&hf, ctx->pflags));
+    memcpy(mine, &hg, 64);
+    memcpy(mine + 64, &hf, 64);
+    unsigned char *dbuf = nullptr;
+    CU_TRY(cudaMalloc(&dbuf, 128 * (R + 1)));
+    std::vector<unsigned char> all(128 * (size_t)R);
+    int nr = 0;
+    cudaError_t ce = cudaMemcpyAsync(dbuf, mine, 128, cudaMemcpyHostToDevice, ctx->stream);
+    if (ce == cudaSuccess) nr = g_nccl.allGather(dbuf, dbuf + 128, 128, kNcclInt8, ctx->comm, ctx->stream);
+    if (ce == cudaSuccess && nr == 0)
+        ce = cudaMemcpyAsync(all.data(), dbuf + 128, 128 * (size_t)R, cudaMemcpyDeviceToHost, ctx->stream);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(ctx->stream);
+    cudaFree(dbuf);
+    if (nr != 0)
+        return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "ncclAllGather of IPC handles failed: %s",
+                    g_nccl.getErrorString ? g_nccl.getErrorString(nr) : "?");
+    CU_TRY(ce);
+    for (int r = 0; r < R; ++r) {
+        if (r == me) {
+            ctx->peer_g[r] = ctx->pgather;
+            ctx->peer_f[r] = ctx->pflags;
+            continue;
+        }
+        memcpy(&hg, &all[128 * (size_t)r], 64);
+        memcpy(&hf, &all[128 * (size_t)r + 64], 64);
+        void *pg = nullptr, *pf = nullptr;
+        CU_TRY(cudaIpcOpenMemHandle(&pg, hg, cudaIpcMemLazyEnablePeerAccess));
+        ctx->peer_g[r] = (float *)pg;
+        CU_TRY(cudaIpcOpenMemHandle(&pf, hf, cudaIpcMemLazyEnablePeerAccess));
+        ctx->peer_f[r] = (unsigned *)pf;
+    }
+    ctx->xepoch = 0;
+    ctx->peer_ready = ctx->use_peer = true;
+    return 0;
+}
+
+extern "C" int gemma3_cuda_set_exchange(gemma3_cuda_ctx *ctx, int mode) {
+    if (!ctx) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null context");
+    if (mode != GEMMA3_CUDA_XCHG_NCCL && mode != GEMMA3_CUDA_XCHG_PEER)
+        return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad exchange mode %d", mode);
+    if (mode == GEMMA3_CUDA_XCHG_PEER && !ctx->peer_ready)
+        return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "peer exchange not set up (gemma3_cuda_peer_init)");
+    if (mode == GEMMA3_CUDA_XCHG_NCCL && !ctx->comm)
+        return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "NCCL exchange needs gemma3_cuda_comm_init");
+    ctx->use_peer = mode == GEMMA3_CUDA_XCHG_PEER;
     return 0;
 }
 

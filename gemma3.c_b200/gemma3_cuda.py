@@ -28,6 +28,8 @@ ERR_CONTEXT_OVERFLOW = -8
 
 KV_F32 = 0
 KV_BF16 = 1
+XCHG_NCCL = 0
+XCHG_PEER = 1
 
 N_LAYERS = 34
 N_HEADS = 8
@@ -94,6 +96,8 @@ SIGNATURES = {
     "gemma3_cuda_attn_prefill": (_I, [_P, _I, _I, _FP, _FP, _FP, _I, _I, _FP]),
     "gemma3_cuda_attn_prefill_dev": (_I, [_P, _I, _I, _P, _P, _P, _I, _I, _P]),
     "gemma3_cuda_attn_decode": (_I, [_P, _I, _I, _IP, _IP, _FP, _FP, _FP, _FP]),
+    "gemma3_cuda_peer_init": (_I, [_P]),
+    "gemma3_cuda_set_exchange": (_I, [_P, _I]),
     "gemma3_cuda_attn_decode_dev": (_I, [_P, _I, _I, _IP, _IP, _P, _P, _P, _P]),
     "gemma3_cuda_attn_decode_partial_dev": (_I, [_P, _I, _I, _IP, _IP, _P, _P, _P, _P]),
     "gemma3_cuda_merge_partials_dev": (_I, [_P, _I, _I, _P, _P]),
@@ -430,6 +434,15 @@ class Context:
     def comm_init(self, uid: bytes):
         assert len(uid) == 128
         self._chk(self.lib.gemma3_cuda_comm_init(self.h, ctypes.create_string_buffer(uid, 128)))
+
+    def peer_init(self):
+        """Maps every rank's receive buffer for the peer-memory exchange
+        (collective over the kv_ranks contexts, after comm_init)."""
+        self._chk(self.lib.gemma3_cuda_peer_init(self.h))
+
+    def set_exchange(self, mode: int):
+        """XCHG_NCCL (all-gather) or XCHG_PEER (NVLink stores + flags)."""
+        self._chk(self.lib.gemma3_cuda_set_exchange(self.h, mode))
 
     # -- cache utilities ----------------------------------------------------
     def cache_rows(self, layer: int) -> int:

@@ -289,6 +289,28 @@ int gemma3_cuda_merge_partials_dev(gemma3_cuda_ctx *ctx, int n_parts, int B,
 int gemma3_cuda_comm_unique_id(void *id_128_bytes);
 int gemma3_cuda_comm_init(gemma3_cuda_ctx *ctx, const void *id_128_bytes);
 
+/* Exchange used by the context-parallel split on global layers.  No
+ * counterpart in the reference (its attention runs on one CPU); it replaces
+ * the all-gather of the (m, l, O) partials:
+ *   GEMMA3_CUDA_XCHG_NCCL  ncclAllGather of the partials, then a merge kernel;
+ *   GEMMA3_CUDA_XCHG_PEER  the kernel that merges this rank's splits stores
+ *                          its partial directly into every rank's receive
+ *                          buffer over NVLink (P2P stores to CUDA-IPC mapped
+ *                          memory) and raises a per-rank flag; the final
+ *                          merge waits on the flags (bounded, about 2 s, then
+ *                          GEMMA3_CUDA_ERR_GENERATION_FAILED) -- no library
+ *                          collective on the data path.
+ * gemma3_cuda_peer_init is collective over the kv_ranks contexts (after
+ * gemma3_cuda_comm_init, same node, GPUs with peer access); it maps every
+ * rank's buffers and selects GEMMA3_CUDA_XCHG_PEER.  Every rank must then
+ * issue the same sequence of global-layer decode calls; after a failed
+ * exchange the ranks' epochs may disagree, so free and re-create the
+ * contexts. */
+#define GEMMA3_CUDA_XCHG_NCCL 0
+#define GEMMA3_CUDA_XCHG_PEER 1
+int gemma3_cuda_peer_init(gemma3_cuda_ctx *ctx);
+int gemma3_cuda_set_exchange(gemma3_cuda_ctx *ctx, int mode);
+
 /* Marks every cache empty (counters only in the reference,
  * gemma3_transformer.c:226-233; here the device cache is also zeroed, as the
  * Metal backend does at gemma3_metal.m:989-997). */

@@ -9,7 +9,7 @@ partials are all-gathered and merged.
   * test_split_emulated_*    - one GPU: R contexts with kv_rank/kv_ranks set,
                                partial + merge through the C-ABI, against an
                                unsplit context;
-  * test_split_nccl_2gpu     - two GPUs: NCCL all-gather inside
+  * test_split_nccl_2gpu     - two GPUs: NCCL all-gather, then the peer-memory exchange, inside
                                gemma3_cuda_attn_decode_dev (skipped with fewer).
 """
 import os
@@ -180,12 +180,29 @@ out = torch.empty(B, 2048, device="cuda")
 c.attn_decode_dev(layer, [0, 1], pos, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr())
 c.synchronize()
 got = out.cpu().numpy()
+# the same call through the peer-memory exchange, three times in a row (both
+# buffer parities, and a parity reused), then once more through NCCL
+c.peer_init()
+peer = []
+for _ in range(3):
+    out.zero_()
+    c.attn_decode_dev(layer, [0, 1], pos, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr())
+    c.synchronize()
+    peer.append(out.cpu().numpy())
+c.set_exchange(gc.XCHG_NCCL)
+out.zero_()
+c.attn_decode_dev(layer, [0, 1], pos, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr())
+c.synchronize()
+again = out.cpu().numpy()
 if rank == 0:
     ref = gc.Context(max_context=ctxlen, max_batch=B, kv_dtype=gc.KV_BF16, device=0, max_prefill=64)
     setup(ref)
     want = ref.attn_decode(layer, [0, 1], pos, Q, K, V)
-    e = np.max(np.abs(got - want)) / np.sqrt(np.mean(want ** 2))
-    print(json.dumps({"err": float(e)}))
+    rms = np.sqrt(np.mean(want ** 2))
+    e = np.max(np.abs(got - want)) / rms
+    ep = max(float(np.max(np.abs(p_ - got)) / rms) for p_ in peer)
+    ea = float(np.max(np.abs(again - got)) / rms)
+    print(json.dumps({"err": float(e), "peer_vs_nccl": ep, "nccl_again": ea}))
 c.close()
 dist.destroy_process_group()
 '''
@@ -205,4 +222,9 @@ def test_split_nccl_2gpu(tmp_path):
     assert r.returncode == 0, r.stderr[-3000:]
     line = [l for l in r.stdout.splitlines() if l.startswith("{")][-1]
     import json
-    assert json.loads(line)["err"] <= 1e-3
+    res = json.loads(line)
+    assert res["err"] <= 1e-3
+    # the peer exchange merges the same partials in the same order as the
+    # all-gather path: identical up to float rounding of the merge
+    assert res["peer_vs_nccl"] <= 1e-6
+    assert res["nccl_again"] <= 1e-6
