@@ -924,7 +924,9 @@ __global__ void __launch_bounds__(256) merge_peer_partials(const PeerXchg px, fl
 // prologue_prefill), accumulation fp32.
 //
 // TMEM columns (512): Q 0-127 (fp16 pairs), S 128-191 (fp32), P 192-255
-// (2 x 32, fp16 pairs), O 256-511 (fp32).
+// (2 x 32, fp16 pairs), O 256-511 (fp32).  (A second S buffer, with P written
+// over its S, was measured: no faster, since S at N=64 and PV already keep the
+// tensor pipe busy for ~1,536 of the ~1,750 cycles of a tile.)
 //
 // Online softmax with a lazily updated reference max: P = 2^(s*c - m) is
 // computed against the row's current reference m, which is only raised
@@ -940,6 +942,7 @@ __global__ void __launch_bounds__(256) merge_peer_partials(const PeerXchg px, fl
 // All barrier phases run on per-CTA counters (tile counter gi, unit counter
 // uk) that continue across units.
 // ------------------------------------------------------------------------
+constexpr int kPfMaxCtas = 160;
 struct PrefillParams {
     float *out;       // [T][8][256]
     int T;
@@ -948,6 +951,24 @@ struct PrefillParams {
     int is_global;
     int nqb;          // query blocks of 64 tokens
     unsigned *err;
+    // Work schedule.  sched 0: cost-sorted units dealt to the CTAs in
+    // snake-order rounds.  sched 1 (local layers, whose units are all of
+    // near-equal cost, when the unit count is not a multiple of the grid):
+    // the nunits - nfull units left over after the full rounds are cut into
+    // `split` key-range pieces each and run FIRST, one piece per CTA (piece
+    // q = blockIdx.x: unit nfull + q / split, part q % split); then come the
+    // nfull units in full snake rounds.  Each piece writes its unnormalised
+    // (O, m, l) to scratch slot q; the last piece of a unit to finish
+    // (ticket q / split) merges the unit's pieces into out while its CTA
+    // already computes the next unit.  Keeping the rounds keeps the units
+    // that share K/V tiles close in time (L2 reuse), which a contiguous cut
+    // of the unit list per CTA loses.
+    int sched;
+    int nfull;           // units in full rounds (a multiple of gridDim.x)
+    int split;           // pieces per left-over unit (2..4)
+    float *pscratch;     // [kPfMaxCtas][128][256]
+    float2 *pml;         // [kPfMaxCtas][128] (m, l), m in the log2 domain
+    unsigned *ptickets;  // [kPfMaxCtas], zero between launches
 };
 
 constexpr int kPfSoftmaxThreads = 256;
@@ -965,7 +986,7 @@ constexpr int kExpEmuQuarters = G3_EXP_EMU_QUARTERS;
 // Development-only per-tile timestamps of CTA 0 (build with -DG3_PF_TRACE);
 // compiled out of the library.
 #ifdef G3_PF_TRACE
-__device__ long long g3_pf_trace[8][512];
+__device__ long long g3_pf_trace[16][512];
 #define G3_TRACE(slot, i)                                                     \
     do {                                                                      \
         if (blockIdx.x == 0 && (i) < 512) g3_pf_trace[slot][i] = clock64();   \
@@ -986,7 +1007,8 @@ constexpr uint32_t kPfOffV = kPfOffK + kPfKStages * kPfKVStage;
 constexpr uint32_t kPfOffBar = kPfOffV + kPfVStages * kPfKVStage;
 constexpr uint32_t kPfOffRed = kPfOffBar + 256;
 // row-max exchange: bf16 [2 parity][2 half][128] (1 KB); row sums fp32 [2 half][128] (1 KB)
-constexpr uint32_t kPfSmem = kPfOffRed + 2048;  // 231,680 B: needs a 1024-aligned base (checked)
+// + the rows' reference maxima for the piece partials, fp32 [128] (512 B)
+constexpr uint32_t kPfSmem = kPfOffRed + 2560;  // 232,192 B: needs a 1024-aligned base (checked)
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemQ = 0;
 constexpr uint32_t kTmemS = 128;
@@ -997,6 +1019,8 @@ constexpr uint32_t kTmemO = 256;
 // (causal rows grow with the block index; local-layer blocks are equal).
 struct PfUnit {
     int t0, qlo, qhi, j0, ntiles, g;
+    int slot, tix;    // piece of a cut unit: scratch slot and ticket; -1 for a whole unit
+    int first, nparts;  // the unit's pieces occupy slots first .. first + nparts - 1
 };
 // Unit k of this CTA: the cost-sorted list is dealt out in rounds of
 // gridDim.x, alternating direction each round (snake order), which evens out
@@ -1018,7 +1042,48 @@ __device__ __forceinline__ PfUnit pf_unit(const PrefillParams &p, int idx) {
     const int kmin = p.is_global ? 0 : max(0, u.qlo - (kWindow - 1));
     u.j0 = (kmin - p.kv_pos0) / 64;
     u.ntiles = (u.qhi - p.kv_pos0) / 64 + 1 - u.j0;
+    u.slot = u.tix = u.first = -1;
+    u.nparts = 1;
     return u;
+}
+
+// Items of this CTA (units or pieces of cut units), in processing order.
+__device__ __forceinline__ int pf_count(const PrefillParams &p, int nunits) {
+    if (!p.sched) return pf_unit_rounds(nunits);
+    return 1 + p.nfull / (int)gridDim.x;
+}
+// Item k; false when this CTA has no unit / piece in that round.
+__device__ __forceinline__ bool pf_get(const PrefillParams &p, int nunits, int k, PfUnit &u) {
+    if (!p.sched) {
+        const int idx = pf_unit_index(k, nunits);
+        if (idx < 0) return false;
+        u = pf_unit(p, idx);
+        return true;
+    }
+    if (k > 0) {
+        u = pf_unit(p, pf_unit_index(k - 1, p.nfull));
+        return true;
+    }
+    const int q = blockIdx.x;
+    const int idx = p.nfull + q / p.split, part = q % p.split;
+    if (idx >= nunits) return false;
+    u = pf_unit(p, idx);
+    const int n = u.ntiles, np = min(p.split, n);
+    if (part >= np) return false;  // a unit of fewer tiles than `split` has fewer pieces
+    const int lo = n * part / np, hi = n * (part + 1) / np;
+    u.j0 += lo;
+    u.ntiles = hi - lo;
+    u.slot = q;
+    u.first = q - part;
+    u.nparts = np;
+    u.tix = q / p.split;
+    return true;
+}
+__device__ __forceinline__ bool pf_next(const PrefillParams &p, int nunits, int k, PfUnit &u) {
+    const int n = pf_count(p, nunits);
+    for (++k; k < n; ++k)
+        if (pf_get(p, nunits, k, u)) return true;
+    return false;
 }
 
 __global__ void __launch_bounds__(kPfThreads, 1)
@@ -1038,6 +1103,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     unsigned char *sV = sm + kPfOffV;
     __nv_bfloat16 *redm = reinterpret_cast<__nv_bfloat16 *>(sm + kPfOffRed);  // [2 parity][2 half][128] maxima
     float *reds = reinterpret_cast<float *>(sm + kPfOffRed + 1024);             // [2 half][128] row sums
+    float *redmx = reinterpret_cast<float *>(sm + kPfOffRed + 2048);            // [128] row reference maxima
+    volatile int *s_last = reinterpret_cast<volatile int *>(sm + kPfOffBar + 28 * 8);  // epilogue: piece merges
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kPfOffBar);
     uint64_t *q_smem = bars + 0;    // Q tile landed in staging (TMA)
     uint64_t *k_full = bars + 1;    // [3]
@@ -1045,7 +1112,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     uint64_t *v_full = bars + 7;    // [2]
     uint64_t *v_empty = bars + 9;   // [2]
     uint64_t *s_full = bars + 11;
-    uint64_t *s_free = bars + 12;   // 256 arrivals
+    uint64_t *s_free = bars + 12;
     uint64_t *p_full = bars + 13;   // [2], 256 arrivals
     uint64_t *p_empty = bars + 15;  // [2]
     uint64_t *mma_done = bars + 17;
@@ -1065,12 +1132,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < 24; ++i) mbar_init(&bars[i], 1);
-        mbar_init(s_free, kPfSoftmaxThreads);
         for (int b = 0; b < 2; ++b) {
             mbar_init(&p_full[b], kPfSoftmaxThreads);
             mbar_init(&red_bar[b], kPfSoftmaxThreads);
         }
         mbar_init(fin_bar, kPfSoftmaxThreads);
+        mbar_init(s_free, kPfSoftmaxThreads);
         mbar_init(o_free, 128);
         mbar_init(epi_bar, 128);
         mbar_init(epi_done, 128);
@@ -1091,29 +1158,24 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             prefetch_tmap(&tmV);
             // Q of unit uk is loaded one unit ahead: right after the first
             // tile of unit uk-1 (once that unit's Q has left the staging).
-            auto load_q = [&](int idx) {
-                const PfUnit u = pf_unit(p, idx);
+            auto load_q = [&](const PfUnit &u) {
                 mbar_expect_tx(q_smem, kPfQBytes);
                 for (int c = 0; c < 4; ++c)
                     for (int hh = 0; hh < 2; ++hh)
                         tma_load_3d(sQ + c * 16384 + hh * 8192, &tmQ, 64 * c, u.t0, 2 * u.g + hh, q_smem);
             };
-            auto next_unit = [&](int k) {
-                for (++k; k < pf_unit_rounds(nunits); ++k)
-                    if (pf_unit_index(k, nunits) >= 0) return pf_unit_index(k, nunits);
-                return -1;
-            };
             int gi = 0, uk = 0;
+            const int nitems = pf_count(p, nunits);
             {
-                const int first = pf_unit_index(0, nunits);
-                if (first >= 0) load_q(first);
+                PfUnit f;
+                if (pf_next(p, nunits, -1, f)) load_q(f);
             }
-            for (int k = 0; k < pf_unit_rounds(nunits) && !*s_abort; ++k) {
-                const int idx = pf_unit_index(k, nunits);
-                if (idx < 0) continue;
-                const PfUnit u = pf_unit(p, idx);
+            for (int k = 0; k < nitems && !*s_abort; ++k) {
+                PfUnit u, un;
+                if (!pf_get(p, nunits, k, u)) continue;
                 const int ukc = uk++;
-                const int nxt = next_unit(k);
+                const bool has_nxt = pf_next(p, nunits, k, un);
+                bool q_pending = has_nxt;  // the next item's Q is still to be loaded
                 G3_TRACE(3, ukc);
                 for (int i = 0; i < u.ntiles; ++i, ++gi) {
                     const int sk = gi % kPfKStages, nk = gi / kPfKStages;
@@ -1130,11 +1192,19 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     tma_load_4d(sV + sv * kPfKVStage, &tmV, 0, krow, 0, u.g, &v_full[sv]);
                     // prefetch the next unit's Q into the staging once this
                     // unit's Q is in TMEM and the previous unit's epilogue
-                    // has stopped using the staging for its output
-                    if (i == min(2, u.ntiles - 1) && nxt >= 0) {
-                        if (!mbar_wait(q_tmem, ukc & 1, p.err)) { *s_abort = 1; break; }
-                        if (ukc >= 1 && !mbar_wait(epi_done, (ukc - 1) & 1, p.err)) { *s_abort = 1; break; }
-                        load_q(nxt);
+                    // has stopped using the staging for its output.  Polled
+                    // from the third tile on, so the K/V stream never waits
+                    // for the epilogue; only the unit's last tile blocks.
+                    if (q_pending && i >= min(2, u.ntiles - 1)) {
+                        if (i == u.ntiles - 1) {
+                            if (!mbar_wait(q_tmem, ukc & 1, p.err)) { *s_abort = 1; break; }
+                            if (ukc >= 1 && !mbar_wait(epi_done, (ukc - 1) & 1, p.err)) { *s_abort = 1; break; }
+                            q_pending = false;
+                        } else {
+                            q_pending = !(mbar_try_wait(q_tmem, ukc & 1) &&
+                                          (ukc < 1 || mbar_try_wait(epi_done, (ukc - 1) & 1)));
+                        }
+                        if (!q_pending) load_q(un);
                     }
                 }
             }
@@ -1150,10 +1220,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             const uint64_t dK0 = smem_desc_sw128(smem_u32(sK), 16, 1024);
             bool ok = true;
             int gi = 0, uk = 0;
-            for (int k = 0; ok && k < pf_unit_rounds(nunits); ++k) {
-                const int idx = pf_unit_index(k, nunits);
-                if (idx < 0) continue;
-                const PfUnit u = pf_unit(p, idx);
+            const int nitems = pf_count(p, nunits);
+            for (int k = 0; ok && k < nitems; ++k) {
+                PfUnit u;
+                if (!pf_get(p, nunits, k, u)) continue;
                 const int ukc = uk++;
                 if (*s_abort || !mbar_wait(q_smem, ukc & 1, p.err)) { ok = false; break; }
                 tc_fence_after();
@@ -1192,10 +1262,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             const uint64_t dV0 = smem_desc_sw128(smem_u32(sV), 8192, 1024);
             bool ok = true;
             int gi = 0, uk = 0;
-            for (int k = 0; ok && k < pf_unit_rounds(nunits); ++k) {
-                const int idx = pf_unit_index(k, nunits);
-                if (idx < 0) continue;
-                const PfUnit u = pf_unit(p, idx);
+            const int nitems = pf_count(p, nunits);
+            for (int k = 0; ok && k < nitems; ++k) {
+                PfUnit u;
+                if (!pf_get(p, nunits, k, u)) continue;
                 const int ukc = uk++;
                 for (int i = 0; i < u.ntiles; ++i, ++gi) {
                     if (*s_abort) { ok = false; break; }
@@ -1223,21 +1293,17 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     } else if (warp >= kPfWarpEpi) {
         // ------------------------------------------------ epilogue warps
         // O / (l_half0 + l_half1) -> out[t][2g+hh][:], one warp per TMEM lane
-        // quadrant, thread = row.  Staged through the Q staging buffer (free
-        // once the next unit's Q is in TMEM) in two 128-column halves, so the
-        // stores are coalesced and O is released to the next unit right after
-        // the second half has been read from TMEM.  Staging: [128 rows][32
-        // 16-byte chunks], chunk c of row r at slot c ^ (r & 7).
+        // quadrant, thread = row.  Columns 0-127 go through the Q staging
+        // buffer (free once the next unit's Q is in TMEM) for coalesced
+        // stores; columns 128-255 go from registers straight to the row's
+        // contiguous 512 bytes, and O is released to the next unit right after
+        // that last TMEM read, before the staged half is stored.  Staging:
+        // [128 rows][32 16-byte chunks], chunk c of row r at slot c ^ (r & 7).
         const int quad = warp & 3;
         const int row = quad * 32 + lane;
         const int et = threadIdx.x - kPfWarpEpi * 32;  // 0..127
         const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
         float4 *stage = reinterpret_cast<float4 *>(sQ);
-        auto next_unit = [&](int k) {
-            for (++k; k < pf_unit_rounds(nunits); ++k)
-                if (pf_unit_index(k, nunits) >= 0) return true;
-            return false;
-        };
         bool ok = true;
         int gi = 0, uk = 0, eph = 0;
         auto epi_sync = [&]() {
@@ -1246,14 +1312,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             ++eph;
             return __all_sync(0xffffffffu, w);
         };
-        for (int k = 0; ok && k < pf_unit_rounds(nunits); ++k) {
-            const int idx = pf_unit_index(k, nunits);
-            if (idx < 0) continue;
-            const PfUnit u = pf_unit(p, idx);
+        const int nitems = pf_count(p, nunits);
+        for (int k = 0; ok && k < nitems; ++k) {
+            PfUnit u, un;
+            if (!pf_get(p, nunits, k, u)) continue;
             const int ukc = uk++;
             gi += u.ntiles;
             const int gl = gi - 1;  // the unit's last tile
-            const bool more = next_unit(k);
+            const bool more = pf_next(p, nunits, k, un);
             // the staging still holds the next unit's Q until it is in TMEM
             if (!__all_sync(0xffffffffu, !*s_abort && mbar_wait(fin_bar, ukc & 1, p.err) &&
                                              mbar_wait(&p_empty[gl & 1], (gl >> 1) & 1, p.err) &&
@@ -1262,43 +1328,158 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 break;
             }
             tc_fence_after();
+            if (et == 0) G3_TRACE(12, ukc);
             fence_proxy_async_smem();  // the staging was last touched by TMA / tcgen05.cp
             const float lt = reds[row] + reds[128 + row];
-            const float inv = lt > 0.f ? 1.0f / lt : 0.f;
+            // a piece of a cut unit leaves O unnormalised, with (m, l) beside it
+            const bool piece = u.slot >= 0;
+            const float inv = piece ? 1.0f : lt > 0.f ? 1.0f / lt : 0.f;
+            if (piece) p.pml[(size_t)u.slot * 128 + row] = make_float2(redmx[row], lt);
             const int nvalid = min(64, p.T - u.t0);
-            for (int hc = 0; ok && hc < 2; ++hc) {
+            // columns 0-127: TMEM -> shared staging (stored coalesced below);
+            // TMEM loads go out two at a time (64 columns per wait)
 #pragma unroll 1
-                for (int cc = 0; cc < 4; ++cc) {
-                    float o[32];
-                    tmem_ld32(lane_base + kTmemO + hc * 128 + cc * 32, o);
-                    tc_wait_ld();
-                    if (hc == 1 && cc == 3) {
-                        // all of O read from TMEM: the next unit's PV may overwrite it
-                        tc_fence_before();
-                        mbar_arrive(o_free);
-                    }
+            for (int cc = 0; cc < 4; cc += 2) {
+                float o[2][32];
+                tmem_ld32(lane_base + kTmemO + cc * 32, o[0]);
+                tmem_ld32(lane_base + kTmemO + cc * 32 + 32, o[1]);
+                tc_wait_ld();
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
 #pragma unroll
                     for (int k4 = 0; k4 < 8; ++k4) {
-                        const int c = cc * 8 + k4;
-                        stage[row * 32 + (c ^ (row & 7))] =
-                            make_float4(o[4 * k4] * inv, o[4 * k4 + 1] * inv, o[4 * k4 + 2] * inv, o[4 * k4 + 3] * inv);
+                        const int c = (cc + h) * 8 + k4;
+                        stage[row * 32 + (c ^ (row & 7))] = make_float4(o[h][4 * k4] * inv, o[h][4 * k4 + 1] * inv,
+                                                                        o[h][4 * k4 + 2] * inv, o[h][4 * k4 + 3] * inv);
+                    }
+            }
+            // columns 128-255: TMEM -> registers -> this row's 512 contiguous
+            // bytes; O is released to the next unit's PV right after the last
+            // TMEM read, before any store of this unit has to drain
+            {
+                float *rdst = piece ? p.pscratch + ((size_t)u.slot * 128 + row) * kHeadDim
+                                    : p.out + ((size_t)(u.t0 + (row & 63)) * kHeads + 2 * u.g + (row >> 6)) * kHeadDim;
+                const bool rok = piece || (row & 63) < nvalid;
+#pragma unroll 1
+                for (int cc = 0; cc < 4; cc += 2) {
+                    float o[2][32];
+                    tmem_ld32(lane_base + kTmemO + 128 + cc * 32, o[0]);
+                    tmem_ld32(lane_base + kTmemO + 128 + cc * 32 + 32, o[1]);
+                    tc_wait_ld();
+                    if (cc == 2) {
+                        // all of O read from TMEM: the next unit's PV may overwrite it
+                        tc_fence_before();
+                        if (et == 0) G3_TRACE(13, ukc);
+                        mbar_arrive(o_free);
+                    }
+                    if (rok) {
+                        float4 *d4 = reinterpret_cast<float4 *>(rdst + 128 + cc * 32);
+#pragma unroll
+                        for (int k4 = 0; k4 < 16; ++k4) {
+                            const float *src = o[k4 >> 3] + 4 * (k4 & 7);
+                            d4[k4] = make_float4(src[0] * inv, src[1] * inv, src[2] * inv, src[3] * inv);
+                        }
                     }
                 }
-                if (!epi_sync()) { ok = false; break; }
-                // 128 threads store 128 rows x 512 B; a warp covers one row's 512 contiguous bytes
-                for (int f = et; f < 128 * 32; f += 128) {
-                    const int r = f >> 5, c = f & 31;
-                    if ((r & 63) < nvalid) {
-                        float *dst = p.out + ((size_t)(u.t0 + (r & 63)) * kHeads + 2 * u.g + (r >> 6)) * kHeadDim +
-                                     hc * 128 + c * 4;
-                        *reinterpret_cast<float4 *>(dst) = stage[r * 32 + (c ^ (r & 7))];
-                    }
+            }
+            if (!epi_sync()) { ok = false; break; }
+            // 128 threads store 128 rows x 512 B of the staging; a warp covers
+            // one row's 512 contiguous bytes
+            for (int f = et; f < 128 * 32; f += 128) {
+                const int r = f >> 5, c = f & 31;
+                if (piece) {
+                    float *dst = p.pscratch + ((size_t)u.slot * 128 + r) * kHeadDim + c * 4;
+                    *reinterpret_cast<float4 *>(dst) = stage[r * 32 + (c ^ (r & 7))];
+                } else if ((r & 63) < nvalid) {
+                    float *dst = p.out + ((size_t)(u.t0 + (r & 63)) * kHeads + 2 * u.g + (r >> 6)) * kHeadDim + c * 4;
+                    *reinterpret_cast<float4 *>(dst) = stage[r * 32 + (c ^ (r & 7))];
                 }
-                if (hc == 0 && !epi_sync()) { ok = false; break; }
             }
             if (!ok) break;
             fence_proxy_async_smem();  // our staging reads before the next Q's TMA write
+            if (et == 0) G3_TRACE(14, ukc);
             mbar_arrive(epi_done);     // the staging is free for the next Q
+            if (piece) {
+                // Both pieces of the cut unit publish; the second to arrive
+                // merges them (the CTA's MMA / softmax warps meanwhile run
+                // the next item).  No waiting on the other CTA.
+                __threadfence();
+                if (!epi_sync()) { ok = false; break; }
+                if (et == 0) {
+                    const unsigned old = atomicAdd(&p.ptickets[u.tix], 1u);
+                    *s_last = old == (unsigned)(u.nparts - 1) ? 1 : 0;
+                    if (*s_last) p.ptickets[u.tix] = 0u;  // ready for the next launch
+                }
+                if (!epi_sync()) { ok = false; break; }
+                if (*s_last) {
+                    __threadfence();
+                    const int np = u.nparts;
+                    const float *o0 = p.pscratch + (size_t)u.first * 128 * kHeadDim;
+                    const float2 *m0 = p.pml + (size_t)u.first * 128;
+                    // lane = row of this warp's 32: each piece's weight, normalised
+                    const int rr = quad * 32 + lane;
+                    float wm[4], M = -INFINITY;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        wm[j] = -INFINITY;
+                        if (j < np) {
+                            const float2 a = __ldcg(m0 + (size_t)j * 128 + rr);
+                            wm[j] = a.x;
+                            M = fmaxf(M, a.x);
+                        }
+                    }
+                    float Lr = 0.f;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        const float w = wm[j] == -INFINITY ? 0.f : ex2_approx(wm[j] - M);
+                        if (j < np) Lr += __ldcg(m0 + (size_t)j * 128 + rr).y * w;
+                        wm[j] = w;
+                    }
+                    const float il = Lr > 0.f ? 1.0f / Lr : 0.f;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) wm[j] *= il;
+                    // warp = 32 rows, lanes along the 64 float4 of a row, 2 rows per batch
+                    for (int r0 = 0; r0 < 32; r0 += 2) {
+                        float4 acc[2][2];
+#pragma unroll
+                        for (int jr = 0; jr < 2; ++jr)
+#pragma unroll
+                            for (int h2 = 0; h2 < 2; ++h2) acc[jr][h2] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            if (j >= np) break;
+                            float4 x[2][2];
+#pragma unroll
+                            for (int jr = 0; jr < 2; ++jr)
+#pragma unroll
+                                for (int h2 = 0; h2 < 2; ++h2)
+                                    x[jr][h2] = __ldcg(reinterpret_cast<const float4 *>(
+                                                           o0 + ((size_t)j * 128 + quad * 32 + r0 + jr) * kHeadDim) +
+                                                       lane + 32 * h2);
+#pragma unroll
+                            for (int jr = 0; jr < 2; ++jr) {
+                                const float w = __shfl_sync(0xffffffffu, wm[j], r0 + jr);
+#pragma unroll
+                                for (int h2 = 0; h2 < 2; ++h2) {
+                                    acc[jr][h2].x += x[jr][h2].x * w;
+                                    acc[jr][h2].y += x[jr][h2].y * w;
+                                    acc[jr][h2].z += x[jr][h2].z * w;
+                                    acc[jr][h2].w += x[jr][h2].w * w;
+                                }
+                            }
+                        }
+#pragma unroll
+                        for (int jr = 0; jr < 2; ++jr) {
+                            const int r = quad * 32 + r0 + jr;
+                            if ((r & 63) >= nvalid) continue;
+                            float4 *dst = reinterpret_cast<float4 *>(
+                                p.out + ((size_t)(u.t0 + (r & 63)) * kHeads + 2 * u.g + (r >> 6)) * kHeadDim);
+#pragma unroll
+                            for (int h2 = 0; h2 < 2; ++h2) dst[lane + 32 * h2] = acc[jr][h2];
+                        }
+                    }
+                }
+            }
         }
         if (!ok) *s_abort = 1;
     } else {
@@ -1309,10 +1490,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
         bool ok = true;
         int gi = 0, uk = 0;
-        for (int k = 0; ok && k < pf_unit_rounds(nunits); ++k) {
-            const int idx = pf_unit_index(k, nunits);
-            if (idx < 0) continue;
-            const PfUnit u = pf_unit(p, idx);
+        const int nitems = pf_count(p, nunits);
+        for (int k = 0; ok && k < nitems; ++k) {
+            PfUnit u;
+            if (!pf_get(p, nunits, k, u)) continue;
             const int ukc = uk++;
             const int qpos = p.start_pos + u.t0 + tr;
             const int lo_ok = p.is_global ? INT_MIN : qpos - (kWindow - 1);
@@ -1357,6 +1538,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     ok = false;
                     break;
                 }
+                if (threadIdx.x == 0) G3_TRACE(8, gi);
                 mx = fmaxf(__bfloat162float(mine), __bfloat162float(redm[(pb * 2 + (half ^ 1)) * 128 + row]));
                 const bool raise = mx > m + kRescaleLog2;  // false while the row has no valid key
                 const float m_new = raise ? mx : m;
@@ -1386,7 +1568,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     ok = false;
                     break;
                 }
-                const bool rescale = i >= 1 && __any_sync(0xffffffffu, raise);
+                // a row without a valid key so far has O = 0 and l = 0: its
+                // first real maximum needs no rescale (alpha = 0 leaves l exact);
+                // local units' first tile (window edge) leaves many such rows
+                if (threadIdx.x == 0) G3_TRACE(9, gi);
+                const bool rescale = i >= 1 && __any_sync(0xffffffffu, raise && m != -INFINITY);
                 if (rescale && !__all_sync(0xffffffffu, mbar_wait(&p_empty[pb ^ 1], ((gi - 1) >> 1) & 1, p.err))) {
                     ok = false;
                     break;
@@ -1405,6 +1591,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     }
                     tc_wait_st();
                 }
+                if (threadIdx.x == 0) G3_TRACE(10, gi);
+                if (threadIdx.x == 0 && rescale) G3_TRACE(11, gi);
                 l = l * alpha + rs;
                 m = m_new;
                 tmem_st16(lane_base + kTmemP + pb * 32 + half * 16, pk);
@@ -1423,6 +1611,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 break;
             }
             reds[half * 128 + row] = l;  // read by the epilogue before it releases O
+            if (half == 0) redmx[row] = m;
             mbar_arrive(fin_bar);
         }
         if (!ok) *s_abort = 1;

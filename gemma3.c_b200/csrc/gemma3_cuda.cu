@@ -223,6 +223,10 @@ struct gemma3_cuda_ctx {
     unsigned *err_host = nullptr;  // pinned copy of *err, read back on the stream
     long long launches = 0;
     int sm_count = 148;
+    // prefill piece partials of the balanced local-layer schedule (first use)
+    float *pf_scratch = nullptr;
+    float2 *pf_ml = nullptr;
+    unsigned *pf_tickets = nullptr;
     g3NcclComm comm = nullptr;
     // peer-memory exchange of the context-parallel split (gemma3_cuda_peer_init)
     float *pgather = nullptr;     // own receive buffer [2][kv_ranks][max_batch][8][258]
@@ -291,6 +295,9 @@ static void ctx_release(gemma3_cuda_ctx *c) {
             if (c->peer_f[r]) cudaIpcCloseMemHandle(c->peer_f[r]);
         }
     cudaFree(c->pgather);
+    cudaFree(c->pf_scratch);
+    cudaFree(c->pf_ml);
+    cudaFree(c->pf_tickets);
     cudaFree(c->pflags);
     cudaFree(c->pcounter);
     for (auto &L : c->layers) {
@@ -438,6 +445,8 @@ extern "C" int gemma3_cuda_synchronize(gemma3_cuda_ctx *ctx) {
     if (e) {
         // an aborted launch may leave split tickets counted: start clean
         cudaMemsetAsync(ctx->tickets, 0, (size_t)ctx->cfg.max_batch * kKvHeads * sizeof(unsigned), ctx->stream);
+        if (ctx->pf_tickets)
+            cudaMemsetAsync(ctx->pf_tickets, 0, g3::kPfMaxCtas * sizeof(unsigned), ctx->stream);
         cudaMemsetAsync(ctx->err, 0, sizeof(unsigned), ctx->stream);
         cudaStreamSynchronize(ctx->stream);
         return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "device status 0x%x (%s)", e,
@@ -561,7 +570,41 @@ static int prefill_impl(gemma3_cuda_ctx *ctx, int layer, int seq, const float *Q
     p.err = ctx->err;
     const int nqb = (T + 63) / 64;
     p.nqb = nqb;
-    const int grid = std::min(nqb * kKvHeads, ctx->sm_count);  // persistent: one CTA per SM
+    int grid = std::min(nqb * kKvHeads, ctx->sm_count);  // persistent: one CTA per SM
+    p.sched = 0;
+    p.nfull = 0;
+    p.split = 1;
+    p.pscratch = ctx->pf_scratch;
+    p.pml = ctx->pf_ml;
+    p.ptickets = ctx->pf_tickets;
+    if (!global) {
+        // Local-layer units are near-equal (up to 17 tiles), so whole units
+        // in snake rounds leave the last round short of work on most SMs
+        // (configs[2]: 512 units on 148 SMs, 3 full rounds and 68 units
+        // over: 4 SMs run four 17-tile units, 80 run three).  Schedule 1 of
+        // PrefillParams runs the left-over units first, cut into 2-4 pieces
+        // spread over the CTAs, and merges each unit's pieces behind the
+        // full rounds.
+        const int nunits = nqb * kKvHeads;
+        const int G = std::min(ctx->sm_count, g3::kPfMaxCtas);
+        const int rest = nunits % G;
+        const int split = rest > 0 ? std::min(4, G / rest) : 0;
+        if (nunits > G && split >= 2) {
+            if (!ctx->pf_scratch) {
+                CU_TRY(cudaMalloc(&ctx->pf_scratch, (size_t)g3::kPfMaxCtas * 128 * kHeadDim * sizeof(float)));
+                CU_TRY(cudaMalloc(&ctx->pf_ml, (size_t)g3::kPfMaxCtas * 128 * sizeof(float2)));
+                CU_TRY(cudaMalloc(&ctx->pf_tickets, g3::kPfMaxCtas * sizeof(unsigned)));
+                CU_TRY(cudaMemsetAsync(ctx->pf_tickets, 0, g3::kPfMaxCtas * sizeof(unsigned), ctx->stream));
+                p.pscratch = ctx->pf_scratch;
+                p.pml = ctx->pf_ml;
+                p.ptickets = ctx->pf_tickets;
+            }
+            p.sched = 1;
+            p.nfull = nunits - rest;
+            p.split = split;
+            grid = G;
+        }
+    }
     size_t e0;
     prof_begin(ctx, &e0);
     g3::prefill_fa_sm100<<<grid, g3::kPfThreads, g3::kPfSmem, ctx->stream>>>(tq, tk, tv, p);

@@ -341,3 +341,35 @@ def test_decode_streamk_runs(oracle, ropes, kv, layer, positions):
     for c in caches:
         oracle.free_cache(c)
     ctx.close()
+
+
+def test_prefill_local_balanced_chunked(ropes):
+    """Local layer, second prefill chunk (positions 2048..7167 over keys from
+    1025): 320 units of 17 tiles on 148 CTAs, two full rounds and 24 units
+    left over, which the kernel runs first as 4 key-range pieces each on
+    different CTAs and merges.  Checked against exact fp32 attention (torch,
+    GPU) of the reference's semantics on the bf16 cache contents."""
+    import torch
+    layer, T0, T1 = 2, 2048, 5120
+    T = T0 + T1
+    rope = ropes[0]
+    qn, kn = synth.qk_norm_gains(77)
+    Q, K, V = qkv(999, T)
+    ctx = make_ctx(ropes, gc.KV_BF16, max_context=8192, max_prefill=T1)
+    ctx.set_qk_norm(layer, qn, kn)
+    ctx.attn_prefill(layer, 0, Q[:T0], K[:T0], V[:T0], 0)
+    got = ctx.attn_prefill(layer, 0, Q[T0:], K[T0:], V[T0:], T0)
+    ctx.close()
+    Qn = torch.from_numpy(_norm_rope_np(Q[T0:], 8, qn, rope, T0)).cuda().view(T1, 8, 256)
+    Kn = torch.from_numpy(bf16_round(_norm_rope_np(K, 4, kn, rope, 0))).cuda().view(T, 4, 256)
+    Vb = torch.from_numpy(bf16_round(V)).cuda().view(T, 4, 256)
+    qp = torch.arange(T0, T, device="cuda")[:, None]
+    kp = torch.arange(T, device="cuda")[None, :]
+    ok = (kp <= qp) & (kp > qp - 1024)
+    want = torch.empty(T1, 8, 256, device="cuda")
+    for h in range(8):
+        s = (Qn[:, h] @ Kn[:, h // 2].T) / 16.0
+        want[:, h] = torch.softmax(s.masked_fill(~ok, float("-inf")), dim=1) @ Vb[:, h // 2]
+    want = want.view(T1, 2048).cpu().numpy()
+    assert np.isfinite(got).all()
+    assert rel_err(got, want) <= TOL, rel_err(got, want)
