@@ -685,26 +685,45 @@ def secondary_context_parallel(args, dist, torch, gc, pk):
         return t
 
     ms = ms_nccl = timed()
+    peer_note = None
     if dist.world > 1:
         # fused exchange: merged partials stored into the peers' buffers over
-        # NVLink by the merge kernel, flags instead of a library collective
-        c.peer_init()
-        ms = timed()
+        # NVLink by the merge kernel, flags instead of a library collective.
+        # Every rank must have mapped its peers before any uses the path, so
+        # the ranks agree on the set-up outcome first.
+        try:
+            c.peer_init()
+            ok = 1.0
+        except Exception as e:  # reported in the line, the NCCL figure stays
+            peer_note = f"peer exchange unavailable: {type(e).__name__}: {e}"
+            ok = 0.0
+        if dist.sum(ok) == dist.world:
+            try:
+                ms = timed()
+            except Exception as e:  # a device-side failure is seen by every rank alike
+                peer_note = f"peer exchange failed: {type(e).__name__}: {e}"
+                ms = ms_nccl
+        else:
+            peer_note = peer_note or "peer exchange unavailable on another rank"
+            if ok:
+                c.set_exchange(gc.XCHG_NCCL)
     dist.barrier()
     c.close()
     del q, k, v, out
     torch.cuda.empty_cache()
     byts = (len(GLOBAL_LAYERS) * ctxlen + (N_LAYERS - len(GLOBAL_LAYERS)) * 1024) * B * ROW_BYTES_BF16
     gbs = byts * steps / (ms / 1e3) / 1e9
-    xchg = ("merge kernel stores partials into peers' buffers over NVLink + flag wait + LSE merge"
-            if dist.world > 1 else "no exchange")
+    xchg = ("no exchange" if dist.world == 1 else "NCCL all-gather + LSE merge" if peer_note else
+            "merge kernel stores partials into peers' buffers over NVLink + flag wait + LSE merge")
     res = {"workload": "configs[4] long-context decode, B=4 @ 131072 keys, global-layer KV split over "
                        f"{dist.world} GPU(s), {xchg}; local layers on every rank",
            "value": round(gbs, 1), "unit": "GB/s", "ms_per_step": round(ms / steps, 3),
            "algorithmic_bytes_per_step": byts, "frac_of_n_x_hbm": round(gbs / (pk["hbm_gbs"] * dist.world), 4)}
-    if dist.world > 1:
+    if dist.world > 1 and not peer_note:
         res["nccl_allgather"] = {"value": round(byts * steps / (ms_nccl / 1e3) / 1e9, 1),
                                  "ms_per_step": round(ms_nccl / steps, 3)}
+    if peer_note:
+        res["note"] = peer_note
     return res
 
 
