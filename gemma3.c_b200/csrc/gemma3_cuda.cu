@@ -580,7 +580,7 @@ static int prefill_impl(gemma3_cuda_ctx *ctx, int layer, int seq, const float *Q
     if (!global) {
         // Local-layer units are near-equal (up to 17 tiles), so whole units
         // in snake rounds leave the last round short of work on most SMs
-        // (configs[2]: 512 units on 148 SMs, 3 full rounds and 68 units
+        // (T = 8192: 512 units on 148 SMs, 3 full rounds and 68 units
         // over: 4 SMs run four 17-tile units, 80 run three).  Schedule 1 of
         // PrefillParams runs the left-over units first, cut into 2-4 pieces
         // spread over the CTAs, and merges each unit's pieces behind the
