@@ -10,10 +10,15 @@
 //                     coalesced bulk-copied rows, warp-shuffle reductions,
 //                     online softmax in the log2 domain;
 //   merge_partials    log-sum-exp merge of the (m, l, O) partials;
+//   merge_partials_push / merge_peer_partials
+//                     the same merge across the GPUs of a context-parallel
+//                     split: partials stored into every rank's buffer over
+//                     NVLink, flags, bounded wait, final merge;
 //   prefill_fa_sm100  causal / sliding-window flash attention for prefill on
-//                     the 5th-generation tensor core: TMA-staged K/V tiles,
-//                     tcgen05.mma (fp16 x fp16 -> fp32) into TMEM, online
-//                     softmax by four warps, P staged through shared memory.
+//                     the 5th-generation tensor core: persistent CTAs, TMA-
+//                     staged K/V tiles, tcgen05.mma (fp16 x fp16 -> fp32)
+//                     into TMEM, online softmax by eight warps with P written
+//                     back to TMEM as the A operand of the PV MMA.
 //
 // Device KV-cache layout (per layer): [seq][K|V][kv_head][row][256] in the
 // cache dtype (fp32 or bf16), rows = max_context (global layer, or this
