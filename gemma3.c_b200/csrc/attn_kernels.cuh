@@ -361,20 +361,6 @@ __device__ __forceinline__ void load_row8<float>(const float *row, int lane, flo
 // (DecodeParams::qraw) and the in-kernel merge (DecodeParams::tickets); the
 // plain form is compiled without that code, which measurably slows the long
 // streaming loop even when it is not executed.
-// Development-only per-CTA phase timestamps of the decode kernel (build with
-// -DG3_DEC_TRACE); compiled out of the library.
-#ifdef G3_DEC_TRACE
-__device__ unsigned long long g3_dec_trace[1024][6];
-#define G3_DTRACE(k)                                                                                  \
-    do {                                                                                              \
-        const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);          \
-        if (threadIdx.x == 0 && cta < 1024) g3_dec_trace[cta][k] = globaltimer_ns();                  \
-    } while (0)
-#else
-#define G3_DTRACE(k) \
-    do {             \
-    } while (0)
-#endif
 
 
 // Running online-softmax state of one warp for the two query heads of a GQA
@@ -572,7 +558,6 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
 
     // Dependent launch: the next kernel may start its set-up now; this one
     // touches global memory only after the previous kernel has completed.
-    G3_DTRACE(0);
     pdl_launch_dependents();
     if (threadIdx.x == 0) {
         s_abort = 0;
@@ -584,7 +569,6 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
     }
     __syncthreads();
     pdl_wait();
-    G3_DTRACE(1);
 
     // q and fresh-row buffers of the fused prologue live after the ring.
     float(*qsm)[kHeadDim] = reinterpret_cast<float(*)[kHeadDim]>(smem + 2 * NS * kPlaneTile);
@@ -668,7 +652,6 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
             store4<KVT>(&newkv[sel][128 + 4 * lane], r.b);
         }
         __syncthreads();
-        G3_DTRACE(2);
         if (threadIdx.x == 0)
             for (int i = early; i < NS && i < ntiles; ++i) issue(i);
     }
@@ -693,7 +676,6 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
             s_abort = 1;
             break;
         }
-        if (i == 0) G3_DTRACE(3);
         if (s_abort) break;
         const int nr = min(TK, r1 - (r0 + i * TK));
         decode_tile<KVT>(kbuf + (size_t)s * TK * kHeadDim, vbuf + (size_t)s * TK * kHeadDim, nr, warp, lane, q0, q1,
@@ -735,7 +717,6 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
             // Split-K style completion: the last split of this (seq, kv head)
             // to finish merges all partials; no CTA ever waits for another.
             __syncthreads();
-            G3_DTRACE(4);
             if (threadIdx.x == 0)
                 s_last = atom_add_acqrel_gpu(&p.tickets[b * kKvHeads + g], 1u) == (unsigned)(p.nsplit - 1);
             __syncthreads();
@@ -743,7 +724,6 @@ __global__ void __launch_bounds__(256, 2) decode_splitkv(const DecodeParams p, c
             merge_group(p.partial + ((size_t)b * kHeads + 2 * g) * p.nsplit * (kHeadDim + 2),
                         (size_t)p.nsplit * (kHeadDim + 2), p.nsplit, p.out + (size_t)b * kHeads * kHeadDim + 2 * g * kHeadDim);
             if (threadIdx.x == 0) p.tickets[b * kKvHeads + g] = 0u;
-            G3_DTRACE(5);
         }
     } else {
         const float inv = Ls > 0.f ? 1.0f / Ls : 0.f;
@@ -983,24 +963,7 @@ constexpr int kPfWarpMma = 9;  // Q copies + S MMAs; also owns the TMEM allocati
 constexpr int kPfWarpPv = 10;  // PV MMAs
 constexpr int kPfWarpEpi = 11; // 11-14: epilogue, one per TMEM lane quadrant
 constexpr float kRescaleLog2 = 8.0f;
-#ifndef G3_EXP_EMU_QUARTERS
-#define G3_EXP_EMU_QUARTERS 0
-#endif
-constexpr int kExpEmuQuarters = G3_EXP_EMU_QUARTERS;
 
-// Development-only per-tile timestamps of CTA 0 (build with -DG3_PF_TRACE);
-// compiled out of the library.
-#ifdef G3_PF_TRACE
-__device__ long long g3_pf_trace[16][512];
-#define G3_TRACE(slot, i)                                                     \
-    do {                                                                      \
-        if (blockIdx.x == 0 && (i) < 512) g3_pf_trace[slot][i] = clock64();   \
-    } while (0)
-#else
-#define G3_TRACE(slot, i) \
-    do {                  \
-    } while (0)
-#endif
 
 constexpr uint32_t kPfQBytes = 128 * 256 * 2;
 constexpr uint32_t kPfKVStage = 64 * 256 * 2;
@@ -1131,7 +1094,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     uint64_t *epi_bar = bars + 26;   // 128 arrivals: epilogue-internal steps (3 per unit)
     uint64_t *epi_done = bars + 27;  // 128 arrivals: epilogue done with the Q staging
 
-    if (threadIdx.x == 0) G3_TRACE(7, 0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nunits = p.nqb * kKvHeads;
 
@@ -1181,7 +1143,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 const int ukc = uk++;
                 const bool has_nxt = pf_next(p, nunits, k, un);
                 bool q_pending = has_nxt;  // the next item's Q is still to be loaded
-                G3_TRACE(3, ukc);
                 for (int i = 0; i < u.ntiles; ++i, ++gi) {
                     const int sk = gi % kPfKStages, nk = gi / kPfKStages;
                     const int sv = gi % kPfVStages, nv = gi / kPfVStages;
@@ -1252,7 +1213,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                                       dK + (uint64_t)(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4), idS, kk > 0 ? 1u : 0u);
                     tc_commit(&k_empty[s]);
                     tc_commit(s_full);
-                    G3_TRACE(0, gi);
                 }
             }
             if (!ok) *s_abort = 1;
@@ -1277,7 +1237,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     const int su = gi % kPfVStages, pb = gi & 1;
                     if (!mbar_wait(&p_full[pb], (gi >> 1) & 1, p.err)) { ok = false; break; }
                     if (!mbar_wait(&v_full[su], (gi / kPfVStages) & 1, p.err)) { ok = false; break; }
-                    G3_TRACE(1, gi);
                     // the first PV of a unit overwrites O: the previous unit's
                     // epilogue must have read it
                     if (i == 0 && ukc >= 1 && !mbar_wait(o_free, (ukc - 1) & 1, p.err)) { ok = false; break; }
@@ -1333,7 +1292,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 break;
             }
             tc_fence_after();
-            if (et == 0) G3_TRACE(12, ukc);
             fence_proxy_async_smem();  // the staging was last touched by TMA / tcgen05.cp
             const float lt = reds[row] + reds[128 + row];
             // a piece of a cut unit leaves O unnormalised, with (m, l) beside it
@@ -1374,7 +1332,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     if (cc == 2) {
                         // all of O read from TMEM: the next unit's PV may overwrite it
                         tc_fence_before();
-                        if (et == 0) G3_TRACE(13, ukc);
                         mbar_arrive(o_free);
                     }
                     if (rok) {
@@ -1402,7 +1359,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             }
             if (!ok) break;
             fence_proxy_async_smem();  // our staging reads before the next Q's TMA write
-            if (et == 0) G3_TRACE(14, ukc);
             mbar_arrive(epi_done);     // the staging is free for the next Q
             if (piece) {
                 // Both pieces of the cut unit publish; the second to arrive
@@ -1513,7 +1469,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                if (threadIdx.x == 0) G3_TRACE(2, gi);
                 float x[32];
                 tmem_ld32(lane_base + kTmemS + half * 32, x);
                 tc_wait_ld();
@@ -1543,7 +1498,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     ok = false;
                     break;
                 }
-                if (threadIdx.x == 0) G3_TRACE(8, gi);
                 mx = fmaxf(__bfloat162float(mine), __bfloat162float(redm[(pb * 2 + (half ^ 1)) * 128 + row]));
                 const bool raise = mx > m + kRescaleLog2;  // false while the row has no valid key
                 const float m_new = raise ? mx : m;
@@ -1557,12 +1511,9 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     const float nm = -m_new;
 #pragma unroll
                     for (int k = 0; k < 16; ++k) {
-                        // kExpEmuQuarters of every four element pairs use the
-                        // FMA-pipe exp2, the rest the transcendental unit.
-                        const bool emu = (k & 3) < kExpEmuQuarters;
                         const float a0 = fmaf(x[2 * k], kScaleLog2, nm), a1 = fmaf(x[2 * k + 1], kScaleLog2, nm);
-                        const float e0 = emu ? ex2_poly(a0) : ex2_approx(a0);
-                        const float e1 = emu ? ex2_poly(a1) : ex2_approx(a1);
+                        const float e0 = ex2_approx(a0);
+                        const float e1 = ex2_approx(a1);
                         rs += e0 + e1;
                         pk[k] = pack_f16x2(e0, e1);
                     }
@@ -1576,7 +1527,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 // a row without a valid key so far has O = 0 and l = 0: its
                 // first real maximum needs no rescale (alpha = 0 leaves l exact);
                 // local units' first tile (window edge) leaves many such rows
-                if (threadIdx.x == 0) G3_TRACE(9, gi);
                 const bool rescale = i >= 1 && __any_sync(0xffffffffu, raise && m != -INFINITY);
                 if (rescale && !__all_sync(0xffffffffu, mbar_wait(&p_empty[pb ^ 1], ((gi - 1) >> 1) & 1, p.err))) {
                     ok = false;
@@ -1596,21 +1546,17 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     }
                     tc_wait_st();
                 }
-                if (threadIdx.x == 0) G3_TRACE(10, gi);
-                if (threadIdx.x == 0 && rescale) G3_TRACE(11, gi);
                 l = l * alpha + rs;
                 m = m_new;
                 tmem_st16(lane_base + kTmemP + pb * 32 + half * 16, pk);
                 tc_wait_st();
                 tc_fence_before();
-                if (threadIdx.x == 0) G3_TRACE(4, gi);
                 mbar_arrive(&p_full[pb]);
             }
             if (!ok) break;
             // ---- hand the unit to the epilogue warps: this half's row sum.
             // Stay at most one unit ahead of the epilogue: its barriers count
             // phases by parity, and it reads the sums before releasing O.
-            if (threadIdx.x == 0) G3_TRACE(5, ukc);
             if (ukc >= 1 && !__all_sync(0xffffffffu, mbar_wait(o_free, (ukc - 1) & 1, p.err))) {
                 ok = false;
                 break;
@@ -1621,7 +1567,6 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         }
         if (!ok) *s_abort = 1;
     }
-    if (threadIdx.x == 0) G3_TRACE(6, 0);
     tc_fence_before();
     __syncthreads();
     if (warp == kPfWarpTma && lane == 0 && *s_abort) {

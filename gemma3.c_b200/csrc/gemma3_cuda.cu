@@ -737,10 +737,6 @@ static void plan_decode(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_i
         }
         if (c == 2 * TK) break;  // smaller splits only repeat this one
     }
-#ifdef G3_PLAN_ENV  // development-only planner override, compiled out of the library
-    if (const char *e = getenv(L.is_global ? "G3_CHUNK_GLOBAL" : "G3_CHUNK_LOCAL"))
-        if (atoi(e) > 0) chunk = std::max<long long>(atoi(e), (maxrows + kMaxSplit - 1) / kMaxSplit);
-#endif
     pl.chunk = (int)chunk;
     pl.nsplit = std::max(1, (int)((maxrows + chunk - 1) / chunk));
 }
@@ -823,7 +819,15 @@ static int decode_dispatch(gemma3_cuda_ctx *ctx, int layer, int B, const int *se
     return decode_impl<float>(ctx, layer, B, seq_ids, pos, Q, K, V, out, partial_out, px);
 }
 
-// Kernel parameters of the next peer-memory exchange (advances the epoch).
+// Epoch of the exchange after `e`.  Its parity selects the receive slot and
+// must alternate from one exchange to the next; 0 is the flags' initial value,
+// so the wrap goes from 0xFFFFFFFF (odd) to 2 (even).
+static unsigned next_epoch(unsigned e) { return e == 0xFFFFFFFFu ? 2u : e + 1u; }
+
+// Kernel parameters of the next peer-memory exchange.  The caller advances
+// the context's epoch only once the push (which raises the flags) has been
+// enqueued, so a launch refused before it leaves the epochs of all ranks in
+// step; gemma3_cuda_reset on every rank clears epochs and flags together.
 static void peer_params(gemma3_cuda_ctx *ctx, g3::PeerXchg *px) {
     const int R = ctx->cfg.kv_ranks;
     for (int r = 0; r < g3::kMaxPeers; ++r) {
@@ -833,8 +837,7 @@ static void peer_params(gemma3_cuda_ctx *ctx, g3::PeerXchg *px) {
     px->counter = ctx->pcounter;
     px->rank_stride = (size_t)ctx->cfg.max_batch * kHeads * kPartialStride;
     px->parity_stride = (size_t)R * px->rank_stride;
-    if (++ctx->xepoch == 0) ctx->xepoch = 1;  // 0 is the flags' initial value
-    px->epoch = ctx->xepoch;
+    px->epoch = next_epoch(ctx->xepoch);
     px->me = ctx->cfg.kv_rank;
     px->R = R;
 }
@@ -873,6 +876,7 @@ extern "C" int gemma3_cuda_attn_decode_dev(gemma3_cuda_ctx *ctx, int layer, int 
         g3::PeerXchg px;
         peer_params(ctx, &px);
         if (int r = decode_dispatch(ctx, layer, B, seq_ids, pos, Q, K, V, nullptr, ctx->emit, &px)) return r;
+        ctx->xepoch = px.epoch;  // the push is enqueued: it raises this epoch's flags
         launch_pdl(g3::merge_peer_partials, dim3(B * kHeads), dim3(256), 0, ctx->stream, px, out, ctx->err);
         return check_launch(ctx, 1);
     }
@@ -1600,6 +1604,13 @@ extern "C" int gemma3_cuda_reset(gemma3_cuda_ctx *ctx) {
     for (auto &L : ctx->layers)
         CU_TRY(cudaMemsetAsync(L.kv, 0, (size_t)ctx->cfg.max_batch * 2 * kKvHeads * L.rows * kHeadDim * ctx->esz,
                                ctx->stream));
+    if (ctx->peer_ready) {
+        // peer exchange back to its initial state; every rank resets, with no
+        // exchange in flight, so epochs and flags agree again
+        CU_TRY(cudaMemsetAsync(ctx->pflags, 0, 2 * g3::kMaxPeers * sizeof(unsigned), ctx->stream));
+        CU_TRY(cudaMemsetAsync(ctx->pcounter, 0, sizeof(unsigned), ctx->stream));
+        ctx->xepoch = 0;
+    }
     return gemma3_cuda_synchronize(ctx);
 }
 
@@ -1749,6 +1760,15 @@ float *g_noalloc_addr[kNoAllocMaxDevices] = {};
 
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocQ + kNoAllocPart + kNoAllocStatus];
 
+// Runs after the merge: a failed device wait in the split kernel (its status
+// word is non-zero) turns the whole output into NaN, so a caller that has no
+// status channel still cannot read a partial result as a valid one.
+__global__ void noalloc_poison_on_error(const unsigned *status, float *out, int n) {
+    if (*(volatile const unsigned *)status == 0u) return;
+    const float nan = __int_as_float(0x7fc00000);
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) out[i] = nan;
+}
+
 __global__ void noalloc_scale_q(const float *__restrict__ q, float *__restrict__ dst, int n) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) dst[i] = q[i] * g3::kScaleLog2;
@@ -1757,6 +1777,9 @@ __global__ void noalloc_scale_q(const float *__restrict__ q, float *__restrict__
 extern "C" int gemma3_cuda_gqa_decode_noalloc(const float *q, const void *kv, int kv_dtype, int rows, int B,
                                               const int *nrows, float *out, void *stream) {
     if (!q || !kv || !nrows || !out) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null argument");
+    // the split kernel streams the cache with 16-byte bulk copies
+    if (reinterpret_cast<uintptr_t>(kv) & 15u)
+        return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "kv must be 16-byte aligned (bulk copies)");
     if (kv_dtype != GEMMA3_CUDA_KV_F32 && kv_dtype != GEMMA3_CUDA_KV_BF16)
         return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad kv_dtype %d", kv_dtype);
     if (B < 1 || B > kNoAllocMaxBatch)
@@ -1847,19 +1870,9 @@ extern "C" int gemma3_cuda_gqa_decode_noalloc(const float *q, const void *kv, in
     }
     const size_t hs = (size_t)nsplit * kPartialStride;
     g3::merge_partials<<<B * kHeads, 256, 0, st>>>(part, nsplit, kHeads * hs, hs, kPartialStride, out, nullptr);
+    noalloc_poison_on_error<<<(nq + 1023) / 1024, 256, 0, st>>>(status, out, nq);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess)
         return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "kernel launch failed: %s", cudaGetErrorString(e));
     return 0;
 }
-
-#ifdef G3_DEC_TRACE
-extern "C" int g3_debug_read_dec_trace(unsigned long long *host) {
-    return (int)cudaMemcpyFromSymbol(host, g3::g3_dec_trace, sizeof(g3::g3_dec_trace));
-}
-#endif
-#ifdef G3_PF_TRACE
-extern "C" int g3_debug_read_trace(long long *host) {
-    return (int)cudaMemcpyFromSymbol(host, g3::g3_pf_trace, sizeof(g3::g3_pf_trace));
-}
-#endif

@@ -283,24 +283,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
     return y;
 }
 
-// 2^x on the FMA/ALU pipes, to take load off the transcendental unit.
-// x = n + f with n = round(x) (obtained by the 1.5*2^23 rounding trick) and
-// f in [-0.5, 0.5]; 2^f = e^(f ln2) by its Taylor series to degree 5
-// (truncation error < 3e-6 relative), and 2^n is added to the exponent
-// field as an integer.  Inputs below -127 (including -inf) give +0.
-__device__ __forceinline__ float ex2_poly(float x) {
-    x = fmaxf(x, -127.f);
-    const float t = x + 12582912.f;
-    const float n = t - 12582912.f;
-    const float f = x - n;
-    float p = fmaf(f, 1.3333558e-3f, 9.6181291e-3f);
-    p = fmaf(p, f, 5.5504109e-2f);
-    p = fmaf(p, f, 2.4022651e-1f);
-    p = fmaf(p, f, 6.9314718e-1f);
-    p = fmaf(p, f, 1.0f);
-    return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
-}
-
 __device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
     uint32_t r;
     asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));

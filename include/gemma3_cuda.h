@@ -313,7 +313,10 @@ int gemma3_cuda_set_exchange(gemma3_cuda_ctx *ctx, int mode);
 
 /* Marks every cache empty (counters only in the reference,
  * gemma3_transformer.c:226-233; here the device cache is also zeroed, as the
- * Metal backend does at gemma3_metal.m:989-997). */
+ * Metal backend does at gemma3_metal.m:989-997).  On a context with the peer
+ * exchange set up it also clears the exchange epoch and flags: after a failed
+ * exchange, every rank of the group calls it (with no exchange in flight) to
+ * bring the group back in step. */
 int gemma3_cuda_reset(gemma3_cuda_ctx *ctx);
 
 /* Debug/test: copies one sequence's cache of one layer to the host in the
@@ -359,9 +362,11 @@ int gemma3_cuda_profile_read(gemma3_cuda_ctx *ctx, int kernel, long long *launch
  * split-KV kernels as gemma3_cuda_attn_decode_dev on a cache the caller owns,
  * keeping its scratch (scaled queries and split partials) in a static device
  * array of 4.6 MB that every GPU loading this library holds until exit.
- *   q      device fp32 [B][8][256], already QK-normed and rotated (the q that
- *          gemma3_gqa receives, gemma3_kernels.h:188);
- *   kv     device cache, layout [B][K,V][4][rows][256] in kv_dtype;
+ *   q      device fp32 [B][8][256]: the query heads after their RMSNorm and
+ *          rotary embedding, unscaled (the 1/16 score scale is applied here);
+ *   kv     device cache, layout [B][K,V][4][rows][256] in kv_dtype, 16-byte
+ *          aligned (it is streamed with bulk copies; a misaligned pointer is
+ *          rejected with GEMMA3_CUDA_ERR_INVALID_ARG before anything runs);
  *   nrows  host int[B], rows 0..nrows[b]-1 of sequence b are attended
  *          (1 <= nrows[b] <= rows);
  *   out    device fp32 [B][8*256];
@@ -370,7 +375,11 @@ int gemma3_cuda_profile_read(gemma3_cuda_ctx *ctx, int kernel, long long *launch
  * The first call on a device resolves the array's address on that device
  * (the current one), so make it before any stream capture.  All calls share
  * the one array: calls that overlap on the GPU (other streams, other host
- * threads) race and must be serialised by the caller.  Enqueues only. */
+ * threads) race and must be serialised by the caller.  Enqueues only: the
+ * return code covers the arguments and the launches.  A failure on the device
+ * (a bounded wait in the split kernel that gave up) cannot be returned by an
+ * enqueue-only call, so it fills all of out with NaN instead; check out once
+ * the stream has reached it. */
 int gemma3_cuda_gqa_decode_noalloc(const float *q, const void *kv, int kv_dtype,
                                    int rows, int B, const int *nrows, float *out,
                                    void *stream);

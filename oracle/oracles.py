@@ -43,9 +43,20 @@ def _u16(a):
     return np.ascontiguousarray(a, dtype=np.uint16).ctypes.data_as(_U16)
 
 
+def ref_dir():
+    """The reference checkout the oracle is compiled from: $GEMMA3_REF_DIR, else
+    the checkout this build was made against when it is present, else None
+    (the GPU box has no reference sources; it uses the prebuilt oracle/_ref)."""
+    d = os.environ.get("GEMMA3_REF_DIR") or "/root/reference"
+    return d if os.path.isfile(os.path.join(d, "gemma3_kernels.c")) else None
+
+
 def build_oracles():
     """Builds whatever oracle/Makefile can build here (no-op when up to date)."""
-    subprocess.run(["make", "-s", "-C", ORACLE], check=False, capture_output=True)
+    cmd = ["make", "-s", "-C", ORACLE]
+    if ref_dir():
+        cmd.append("REF_DIR=" + ref_dir())
+    subprocess.run(cmd, check=False, capture_output=True)
 
 
 class _Cache:

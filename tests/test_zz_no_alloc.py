@@ -7,14 +7,16 @@ processes, embedders owning all buffers); its scratch is a static device array. 
 existing entry point with QK-norm off and identity RoPE tables, so the raw Q
 is exactly the query both paths attend with, exports the cache the existing
 path built, and checks two consecutive no-allocation calls against it within
-the parity tolerance.  The file is named to be collected last.
+the parity tolerance; both are also checked against the reference's own
+gemma3_gqa (oracle/_ref) on the same cache rows.  The file is named to be
+collected last.
 """
 import numpy as np
 import pytest
 
 import gemma3_cuda as gc
 import synth
-from oracles import rel_err
+from oracles import best_oracle, rel_err
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-2
@@ -34,6 +36,7 @@ def _kv_device(torch, ctx, seqs, dtype):
 @pytest.mark.parametrize("kv_dtype", [gc.KV_F32, gc.KV_BF16])
 def test_noalloc_matches_context_path(kv_dtype):
     import torch
+    oracle = best_oracle()
     ident = np.zeros((MAXCTX, 128, 2), dtype=np.float32)
     ident[..., 0] = 1.0
     ctx = gc.Context(max_context=MAXCTX, max_batch=2, kv_dtype=kv_dtype, max_prefill=64)
@@ -48,6 +51,12 @@ def test_noalloc_matches_context_path(kv_dtype):
         K = synth.normal(310 + call, (2, gc.KV_SIZE))
         V = synth.normal(320 + call, (2, gc.KV_SIZE))
         want = ctx.attn_decode(LAYER, [0, 1], positions, Q, K, V)
+        # the reference's gemma3_gqa on the same cache rows (what both paths
+        # attend: QK-norm is off and the RoPE table is the identity)
+        for b, s in enumerate((0, 1)):
+            k, v = ctx.export_cache(LAYER, s)
+            ref = oracle.gqa(Q[b], k, v, positions[b] + 1)
+            assert rel_err(want[b], ref) <= TOL
         kv = _kv_device(torch, ctx, [0, 1], kv_dtype)
         q = torch.from_numpy(Q).cuda()
         out = torch.full((2, gc.Q_SIZE), float("nan"), device="cuda")
@@ -57,6 +66,9 @@ def test_noalloc_matches_context_path(kv_dtype):
         got = out.cpu().numpy()
         assert np.isfinite(got).all()
         assert rel_err(got, want) <= TOL, (call, rel_err(got, want))
+        for b in range(2):
+            k, v = ctx.export_cache(LAYER, b)
+            assert rel_err(got[b], oracle.gqa(Q[b], k, v, positions[b] + 1)) <= TOL
         positions = [p + 1 for p in positions]
     ctx.close()
 
@@ -69,3 +81,16 @@ def test_noalloc_rejects_oversize_batch():
     with pytest.raises(gc.Gemma3CudaError) as e:
         gc.gqa_decode_noalloc(q.data_ptr(), kv.data_ptr(), gc.KV_F32, 16, [1] * 65, out.data_ptr())
     assert e.value.code == gc.ERR_INVALID_ARG
+
+
+def test_noalloc_rejects_misaligned_cache():
+    """The cache is streamed with 16-byte bulk copies: a pointer off that
+    boundary is refused before any launch (nothing runs on the GPU)."""
+    import torch
+    q = torch.zeros(1, gc.Q_SIZE, device="cuda")
+    kv = torch.zeros(2 * 4 * 16 * 256 + 4, device="cuda")
+    out = torch.zeros(1, gc.Q_SIZE, device="cuda")
+    with pytest.raises(gc.Gemma3CudaError) as e:
+        gc.gqa_decode_noalloc(q.data_ptr(), kv.data_ptr() + 4, gc.KV_F32, 16, [16], out.data_ptr())
+    assert e.value.code == gc.ERR_INVALID_ARG
+    assert "aligned" in str(e.value)
