@@ -180,7 +180,14 @@ class Dist:
 # sequences on parallel threads (ctypes releases the GIL).
 # ---------------------------------------------------------------------------
 class CpuReference:
-    def __init__(self, threads):
+    """Per thread, one sequence's full set of caches as gemma3_kv_cache_alloc
+    lays them out (gemma3_transformer.c:180-214): 29 local 1024-row rings and
+    the global caches of 32,769 rows (5, or 1 shared by the 5 global layers
+    when host memory is short; a 268 MB global cache is far larger than L3
+    either way).  A thread runs its sequences one after another on its own
+    caches, so no sequence-step finds another layer's cache in L3."""
+
+    def __init__(self, threads, separate_globals=True):
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
         from oracles import RefOracle  # the reference's own code
         import synth
@@ -193,38 +200,61 @@ class CpuReference:
         self.qn, self.kn = synth.qk_norm_gains(11)
         base_g = synth.normal(5, (CTX, 4, 256))
         base_l = synth.normal(6, (1024, 4, 256))
+        g_bytes = 2 * max_seq * 4 * 256 * 4
+        avail = os.sysconf("SC_AVPHYS_PAGES") * os.sysconf("SC_PAGE_SIZE")
+        self.n_global = (len(GLOBAL_LAYERS) if separate_globals and threads * len(GLOBAL_LAYERS) * g_bytes < 0.6 * avail
+                         else 1)
         self.caches = []
         for _ in range(threads):
-            g = self.ref.new_cache(True, max_seq)
-            l = self.ref.new_cache(False, max_seq)
-            for c, base in ((g, base_g), (l, base_l)):
+            per = {}
+            for i, layer in enumerate(range(N_LAYERS)):
+                glob = layer in GLOBAL_LAYERS
+                if glob and GLOBAL_LAYERS.index(layer) >= self.n_global:
+                    per[layer] = per[GLOBAL_LAYERS[0]]
+                    continue
+                c = self.ref.new_cache(glob, max_seq)
+                base = base_g if glob else base_l
                 k, v = self.ref.cache_arrays(c)
                 k[:base.shape[0]] = base
                 v[:base.shape[0]] = base
-            self.caches.append((g, l))
+                per[layer] = c
+            self.caches.append(per)
         self.q = synth.normal(7, (1, 2048))
         self.k = synth.normal(8, (1, 1024))
         self.v = synth.normal(9, (1, 1024))
 
+    def caches_note(self):
+        return (f"per thread 29 local caches + {self.n_global} global cache(s) of 32769 rows"
+                + ("" if self.n_global == len(GLOBAL_LAYERS) else " shared by the 5 global layers"))
+
     def unit(self, tid):
-        g, l = self.caches[tid]
+        per = self.caches[tid]
         for layer in range(N_LAYERS):
             glob = layer in GLOBAL_LAYERS
-            self.ref.attn_core_tokens(g if glob else l, self.q, self.k, self.v, self.qn, self.kn,
+            self.ref.attn_core_tokens(per[layer], self.q, self.k, self.v, self.qn, self.kn,
                                       self.rope_g if glob else self.rope_l, POS)
 
     def run(self, units):
-        """Runs `units` sequence-steps on the thread pool; returns seconds."""
+        """Runs `units` sequence-steps, thread t taking sequences t, t+th, ...
+        on its own caches; returns seconds."""
         from concurrent.futures import ThreadPoolExecutor
+
+        def worker(t):
+            for _ in range(t, units, self.threads):
+                self.unit(t)
+
         t0 = time.perf_counter()
         with ThreadPoolExecutor(self.threads) as ex:
-            list(ex.map(lambda i: self.unit(i % self.threads), range(units)))
+            list(ex.map(worker, range(min(self.threads, units))))
         return time.perf_counter() - t0
 
     def close(self):
-        for g, l in self.caches:
-            self.ref.free_cache(g)
-            self.ref.free_cache(l)
+        seen = set()
+        for per in self.caches:
+            for c in per.values():
+                if id(c) not in seen:
+                    seen.add(id(c))
+                    self.ref.free_cache(c)
 
 
 def cpu_threads():
@@ -238,36 +268,37 @@ def cpu_baseline_sample(target_s=12.0):
     """Times the reference on a bounded sample of the headline workload."""
     os.environ.setdefault("OPENBLAS_NUM_THREADS", "1")
     th = cpu_threads()
-    cpu = CpuReference(th)
+    cpu = CpuReference(th, separate_globals=False)  # bounded set-up time inside the GPU bench
     cpu.run(th)  # warm
     units, secs = 0, 0.0
     while secs < target_s:
         secs += cpu.run(th)
         units += th
+    note = cpu.caches_note()
     cpu.close()
     gbs = units * BYTES_PER_SEQ_STEP / secs / 1e9
     return {"value": round(gbs, 3), "unit": "GB/s", "cores": th, "kind": "reference",
             "sample": f"{units} sequence-steps (each: 34 layers, 5 x 32769-row global + 29 x 1024-row local "
-                      f"gemma3_gqa, fp32 cache) on {th} threads, {secs:.1f} s; credited "
+                      f"gemma3_gqa, fp32 cache; {note}) on {th} threads, {secs:.1f} s; credited "
                       f"{BYTES_PER_SEQ_STEP / 1e6:.1f} MB (BF16 algorithmic bytes) per sequence-step"}
 
 
 def run_reference_arm(args, dist):
-    """--impl reference: the reference's CPU path on the same workload."""
+    """--impl reference: the reference's CPU path on the same workload.  Every
+    step runs all 64 sequence-steps (34 layers each) on the host's threads."""
     if dist.rank != 0:
         return None
     os.environ.setdefault("OPENBLAS_NUM_THREADS", "1")
     th = cpu_threads()
     cpu = CpuReference(th)
     for _ in range(args.warmup):
-        cpu.run(th)
-    # a step is a bounded sample of the 64-sequence step: `th` sequences
-    # (one per core), scaled to the 64 sequences of the workload.
-    secs = [cpu.run(th) for _ in range(args.steps)]
+        cpu.run(B_TOTAL)
+    secs = [cpu.run(B_TOTAL) for _ in range(args.steps)]
+    note = cpu.caches_note()
     cpu.close()
     t = sum(secs)
-    gbs = args.steps * th * BYTES_PER_SEQ_STEP / t / 1e9
-    step_ms = t / args.steps * (B_TOTAL / th) * 1e3
+    gbs = args.steps * B_TOTAL * BYTES_PER_SEQ_STEP / t / 1e9
+    step_ms = t / args.steps * 1e3
     return {
         "metric": "decode attention KV throughput, 34-layer Gemma-3-4B, B=64 @ 32768 ctx",
         "value": round(gbs, 3), "unit": "GB/s", "impl": "reference", "n_gpus": args.gpus, "steps": args.steps,
@@ -276,7 +307,8 @@ def run_reference_arm(args, dist):
         "config": {"workload": "configs[3] batched decode B=64, ctx 32768, 34 layers (5 global + 29 local)",
                    "batch": B_TOTAL, "context": CTX, "layers": N_LAYERS, "kv_cache": "fp32 (reference dtype)"},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": th, "kind": "reference",
-                         "sample": f"each step: {th} of the 64 sequences (one per thread), scaled to 64"},
+                         "sample": f"every step: all {B_TOTAL} sequence-steps on {th} threads ({note}); "
+                                   f"timed region {t:.1f} s"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -445,6 +477,230 @@ def secondary_prefill(args, torch, gc, pk, dev):
             "roofline": {"bound": "tensor", "kernel": "prefill_fa_sm100 (fp16 tcgen05, fp32 acc)",
                          "achieved": round(tf_kernel, 1), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                          "frac": round(tf_kernel / pk["bf16_tflops"], 4), "launches": n,
+                         "avg_launch_us": round(kms / max(n, 1) * 1e3, 2)}}
+
+
+def secondary_config0(args, torch, gc, pk, dev, with_cpu):
+    """one local layer's attention core in prefill, B=1, T=512,
+    positions 0..511, seed 0.  Q/K/V come from the projections of seeded
+    N(0,1) activations through N(0,0.02) BF16 weights, computed on the host
+    by the reference's own matvec (layer_attention through oracle/_ref), as
+    the config prescribes; the timed region is the attention core (QK-norm,
+    RoPE, cache append, GQA) on the GPU and, beside it, the reference's own
+    CPU loop (gemma3_transformer.c:641-692 body, single-threaded as the
+    reference runs it)."""
+    import synth
+    T, layer = 512, 0
+    flops = 8.0 * 4 * 256 * (T * (T + 1) // 2)          # 1.076 GFLOP
+    qn, kn = synth.qk_norm_gains(0)
+    rope_l = gc.rope_table(1024, 10000.0)
+    res = {"workload": "configs[0] one local layer prefill, T=512, positions 0..511, seed 0",
+           "algorithmic_gflop": round(flops / 1e9, 4)}
+    Q = K = V = None
+    ref = None
+    if with_cpu:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        try:
+            from oracles import RefOracle
+            ref = RefOracle()
+        except Exception as e:  # reported, the GPU figure stays
+            res["cpu_baseline"] = {"value": None, "error": f"{type(e).__name__}: {e}"}
+    if ref is not None:
+        x = synth.normal(0, (T, gc.HIDDEN))
+        w = [synth.bf16_trunc(synth.normal(s_, shape, 0.02)) for s_, shape in
+             ((1, (gc.Q_SIZE, gc.HIDDEN)), (2, (gc.KV_SIZE, gc.HIDDEN)), (3, (gc.KV_SIZE, gc.HIDDEN)),
+              (4, (gc.HIDDEN, gc.Q_SIZE)))]
+        c = ref.new_cache(False, 1024)
+        rope_ref = ref.rope_table(1024, 10000.0)
+        # the raw (pre-norm) projections layer_attention computes
+        _, Q, K, V, _ = ref.layer_attention_tokens(c, x, *w, qn, kn, rope_ref, layer, 0)
+        ref.free_cache(c)
+    if Q is None:
+        Q, K, V = synth.normal(10, (T, gc.Q_SIZE)), synth.normal(11, (T, gc.KV_SIZE)), synth.normal(12, (T, gc.KV_SIZE))
+        res["inputs"] = "seeded N(0,1) q/k/v (reference projections unavailable)"
+    else:
+        res["inputs"] = "q/k/v = reference matvec projections of x~N(0,1) through W~N(0,0.02) (host)"
+    # GPU: attention core through the C-ABI, device buffers (value) and host buffers (e2e)
+    ctx = gc.Context(max_context=1024, max_batch=1, kv_dtype=gc.KV_F32, device=dev, max_prefill=T, num_layers=1)
+    if ref is not None:
+        rope_l = rope_ref  # the host's own table, as the integration uploads it
+    ctx.upload_rope(rope_l, rope_l)
+    ctx.set_qk_norm(layer, qn, kn)
+    d = f"cuda:{dev}"
+    q, k, v = (torch.from_numpy(np.ascontiguousarray(a)).to(d) for a in (Q, K, V))
+    o = torch.empty(T, gc.Q_SIZE, device=d)
+    stream = torch.cuda.ExternalStream(ctx.stream, device=d)
+    flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=d)
+    call = lambda: ctx.attn_prefill_dev(layer, 0, q.data_ptr(), k.data_ptr(), v.data_ptr(), T, 0, o.data_ptr())
+    for _ in range(5):
+        call()
+    ctx.synchronize()
+    iters, tot = 50, 0.0
+    ctx.profile(True)
+    for _ in range(iters):
+        with torch.cuda.stream(stream):
+            flush.zero_()
+        tot += ev_time(torch, stream, call)
+    n, kms, _ = ctx.profile_read(1)
+    ctx.profile(False)
+    us = tot / iters * 1e3
+    Qh, Kh, Vh = (np.ascontiguousarray(a, dtype=np.float32) for a in (Q, K, V))
+    oh = np.empty((T, gc.Q_SIZE), dtype=np.float32)
+    for _ in range(3):
+        ctx.attn_prefill(layer, 0, Qh, Kh, Vh, 0, out=oh)
+    t0 = time.perf_counter()
+    reps = 50
+    for _ in range(reps):
+        ctx.attn_prefill(layer, 0, Qh, Kh, Vh, 0, out=oh)
+    e2e_s = (time.perf_counter() - t0) / reps
+    ctx.close()
+    del flush
+    res["gpu"] = {"us_per_call": round(us, 2), "tok_per_s": round(T / (us / 1e6), 1),
+                  "kernel_us": round(kms / max(n, 1) * 1e3, 2) if n else None,
+                  "e2e_us_per_call": round(e2e_s * 1e6, 2), "e2e_tok_per_s": round(T / e2e_s, 1),
+                  "roofline": {"bound": "tensor", "achieved": round(flops / (us / 1e6) / 1e12, 2),
+                               "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                               "frac": round(flops / (us / 1e6) / 1e12 / pk["bf16_tflops"], 4),
+                               "note": "1.08 GFLOP: too small to fill 148 SMs; latency-bound"},
+                  "api": "gemma3_cuda_attn_prefill_dev (value) / gemma3_cuda_attn_prefill host buffers (e2e)"}
+    if ref is not None:
+        c = ref.new_cache(False, 1024)
+        ref.attn_core_tokens(c, Q, K, V, qn, kn, rope_ref, 0)  # warm
+        runs, secs = 0, 0.0
+        while secs < 2.0:
+            ref.free_cache(c)
+            c = ref.new_cache(False, 1024)
+            t0 = time.perf_counter()
+            ref.attn_core_tokens(c, Q, K, V, qn, kn, rope_ref, 0)
+            secs += time.perf_counter() - t0
+            runs += 1
+        ref.free_cache(c)
+        res["cpu_baseline"] = {"value": round(T * runs / secs, 1), "unit": "tok/s", "cores": 1, "kind": "reference",
+                               "ms_per_call": round(secs / runs * 1e3, 2),
+                               "sample": f"the whole T=512 layer, {runs} runs; gemma3_gqa and the token loop are "
+                                         "single-threaded in the reference"}
+    return res
+
+
+def cpu_prefill_stack_sample(target_s=8.0):
+    """Reference CPU baseline for configs[2] (34-layer prefill, T=8192),
+    sampled: the whole stack is ~10 minutes of CPU.  Query tokens at evenly
+    spaced positions of a local and of a global layer run through the
+    reference's own per-token attention core (norm, RoPE, cache_kv,
+    gemma3_gqa) over caches already holding the earlier positions; each
+    host thread takes its own positions on its own cache.  The measured
+    FLOP rate of each layer type, applied to that type's algorithmic FLOPs
+    (29 x 7,864,832 and 5 x 33,558,528 (query, key) pairs x 8192 FLOP),
+    gives the projected stack time."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    from oracles import RefOracle
+    from concurrent.futures import ThreadPoolExecutor
+    import synth
+    os.environ.setdefault("OPENBLAS_NUM_THREADS", "1")
+    ref = RefOracle()
+    T = 8192
+    th = cpu_threads()
+    rope = {True: ref.rope_table(T, 1e6), False: ref.rope_table(T, 1e4)}
+    qn, kn = synth.qk_norm_gains(3)
+    base = synth.normal(17, (T, 4, 256))
+    q1, k1, v1 = synth.normal(18, (1, 2048)), synth.normal(19, (1, 1024)), synth.normal(20, (1, 1024))
+    rates = {}
+    for glob in (False, True):
+        caches = []
+        for _ in range(th):
+            c = ref.new_cache(glob, T)
+            k, v = ref.cache_arrays(c)
+            k[:] = base[:k.shape[0]]
+            v[:] = base[:v.shape[0]]
+            caches.append(c)
+        # positions spread evenly over [0, T): position j*stride + offset
+        per_thread = 4
+        npos = th * per_thread
+        positions = [int((i + 0.5) * T / npos) for i in range(npos)]
+
+        def worker(t):
+            pairs = 0
+            for p in positions[t::th]:
+                ref.attn_core_tokens(caches[t], q1, k1, v1, qn, kn, rope[glob], p)
+                pairs += p + 1 if glob else min(p + 1, 1024)
+            return pairs
+
+        with ThreadPoolExecutor(th) as ex:
+            list(ex.map(worker, range(th)))  # warm
+        pairs, secs = 0, 0.0
+        while secs < target_s / 2:
+            t0 = time.perf_counter()
+            with ThreadPoolExecutor(th) as ex:
+                pairs += sum(ex.map(worker, range(th)))
+            secs += time.perf_counter() - t0
+        rates[glob] = pairs * 8192.0 / secs
+        for c in caches:
+            ref.free_cache(c)
+    fl_local, fl_global = 29 * 7864832 * 8192.0, 5 * 33558528 * 8192.0
+    stack_s = fl_local / rates[False] + fl_global / rates[True]
+    return {"value": round(T / stack_s, 2), "unit": "tok/s", "cores": th, "kind": "reference",
+            "tflops": round((fl_local + fl_global) / stack_s / 1e12, 5),
+            "projected_stack_s": round(stack_s, 1),
+            "sample": f"{th * 4} query positions spread over 0..8191 per layer type (local / global), "
+                      f"each through the reference's per-token attention core on a pre-filled cache, "
+                      f"{th} threads, ~{target_s:.0f} s; stack time projected from the measured "
+                      f"GFLOP/s per layer type ({rates[False] / 1e9:.2f} local, {rates[True] / 1e9:.2f} global)"}
+
+
+def secondary_decode_f32(args, torch, gc, pk, dev):
+    """configs[3] with the reference's own cache dtype (fp32): 101.5 GB of KV
+    per step on one GPU."""
+    import synth
+    Bl = B_TOTAL
+    ctx = gc.Context(max_context=POS + 1, max_batch=Bl, kv_dtype=gc.KV_F32, device=dev, max_prefill=64)
+    ctx.upload_rope(gc.rope_table(POS + 1, 10000.0), gc.rope_table(POS + 1, 1000000.0))
+    for l in range(N_LAYERS):
+        qn, kn = synth.qk_norm_gains(100 + l)
+        ctx.set_qk_norm(l, qn, kn)
+        rows = CTX if l in GLOBAL_LAYERS else 1024
+        for s_ in range(Bl):
+            ctx.fill_cache_random(l, s_, rows, 1000 * s_ + l)
+    ctx.synchronize()
+    d = f"cuda:{dev}"
+    g = torch.Generator(device=d).manual_seed(1234)
+    q = torch.randn(N_LAYERS, Bl, 2048, device=d, generator=g)
+    k = torch.randn(N_LAYERS, Bl, 1024, device=d, generator=g)
+    v = torch.randn(N_LAYERS, Bl, 1024, device=d, generator=g)
+    out = torch.empty(N_LAYERS, Bl, 2048, device=d)
+    seq_a = np.arange(Bl, dtype=np.int32)
+    pos_a = np.full(Bl, POS, dtype=np.int32)
+    sp = seq_a.ctypes.data_as(ctypes.POINTER(ctypes.c_int))
+    pp = pos_a.ctypes.data_as(ctypes.POINTER(ctypes.c_int))
+    ptrs = [(q[l].data_ptr(), k[l].data_ptr(), v[l].data_ptr(), out[l].data_ptr()) for l in range(N_LAYERS)]
+    fn, h = ctx.lib.gemma3_cuda_attn_decode_dev, ctx.h
+    stream = torch.cuda.ExternalStream(ctx.stream, device=d)
+
+    def step():
+        for l in range(N_LAYERS):
+            if fn(h, l, Bl, sp, pp, *ptrs[l]) != 0:
+                raise RuntimeError(ctx.last_error())
+
+    for _ in range(3):
+        step()
+    ctx.synchronize()
+    steps = max(3, args.steps // 2)
+    ms = ev_time(torch, stream, lambda: [step() for _ in range(steps)])
+    ctx.profile(True)
+    step()
+    ctx.synchronize()
+    n, kms, byts = ctx.profile_read(0)
+    ctx.profile(False)
+    ctx.close()
+    del q, k, v, out
+    torch.cuda.empty_cache()
+    step_bytes = Bl * BYTES_PER_SEQ_STEP * 2
+    gbs = step_bytes * steps / (ms / 1e3) / 1e9
+    kg = byts / (kms / 1e3) / 1e9
+    return {"workload": "configs[3] batched decode B=64, ctx 32768, 34 layers, fp32 KV cache (reference dtype)",
+            "value": round(gbs, 1), "unit": "GB/s", "ms_per_step": round(ms / steps, 3),
+            "algorithmic_bytes_per_step": step_bytes,
+            "roofline": {"bound": "hbm", "kernel": "decode_splitkv<f32>", "achieved": round(kg, 1),
+                         "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": round(kg / pk["hbm_gbs"], 4),
                          "avg_launch_us": round(kms / max(n, 1) * 1e3, 2)}}
 
 
@@ -854,7 +1110,10 @@ def main():
         cp = secondary_context_parallel(args, dist, torch, gc, pk)
     if dist.rank == 0 and dist.world == 1:
         if not args.no_secondary:
-            line["secondary"] = {"prefill": secondary_prefill(args, torch, gc, pk, dist.local),
+            line["secondary"] = {"config0": secondary_config0(args, torch, gc, pk, dist.local,
+                                                              not args.no_cpu_baseline),
+                                 "decode_f32": secondary_decode_f32(args, torch, gc, pk, dist.local),
+                                 "prefill": secondary_prefill(args, torch, gc, pk, dist.local),
                                  "decode_b1": secondary_decode1(args, torch, gc, pk, dist.local),
                                  "projections": secondary_projections(args, torch, gc, pk, dist.local),
                                  "model": secondary_model(args, torch, gc, pk, dist.local)}
@@ -865,6 +1124,10 @@ def main():
                 line["cpu_baseline"] = cpu_baseline_sample()
             except Exception as e:  # reported, never silently replaced
                 line["cpu_baseline"] = {"value": None, "error": f"{type(e).__name__}: {e}"}
+            try:
+                line["secondary"]["prefill"]["cpu_baseline"] = cpu_prefill_stack_sample()
+            except Exception as e:
+                line["secondary"]["prefill"]["cpu_baseline"] = {"value": None, "error": f"{type(e).__name__}: {e}"}
     if dist.rank == 0:
         print(json.dumps(line), flush=True)
     dist.close()

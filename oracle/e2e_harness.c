@@ -2,8 +2,9 @@
  * e2e_harness.c - end-to-end greedy decoding on a random-init Gemma-3-4B,
  * with and without the B200 attention path.  TEST INFRASTRUCTURE ONLY.
  *
- * Arm "reference": the reference's own gemma3_transformer_forward
- * (gemma3_transformer.c:400-512), token by token, host KV cache.
+ * Arm "reference": the reference's own gemma3_transformer_prefill for the
+ * prompt (gemma3_transformer.c:791-825) and gemma3_transformer_forward
+ * (:400-512) for every generated token, host KV cache.
  * Arm "cuda": the same model and the same reference kernels for everything
  * except the attention core, which goes through include/gemma3_cuda.h the way
  * the USE_CUDA hook does it: the prompt with one gemma3_cuda_attn_prefill per
@@ -188,9 +189,11 @@ int e2e_greedy(int n_prompt, int n_steps, uint64_t seed, int use_cuda, int kv_dt
     if (!use_cuda) {
         gemma3_kv_cache *cache = gemma3_kv_cache_alloc(cfg, max_ctx);
         int pos = 0, tok = 0;
-        for (int i = 0; i < n_prompt; i++, pos++)
-            gemma3_transformer_forward(logits, prompt[i], pos, w, cache, buf, cfg, i == n_prompt - 1, rope_l,
-                                       rope_g, pool);
+        /* the prompt goes through the reference's own prefill, as gemma3_generate
+         * does (gemma3.c:328 -> gemma3_transformer_prefill, batched sgemm in a
+         * USE_BLAS build, gemma3_transformer.c:791-825) */
+        gemma3_transformer_prefill(logits, prompt, n_prompt, 0, w, cache, buf, cfg, rope_l, rope_g, pool);
+        pos = n_prompt;
         for (int s = 0; s < n_steps; s++, pos++) {
             top2(logits, cfg->vocab_size, &tok, &margins_out[s]);
             tokens_out[s] = tok;

@@ -86,6 +86,10 @@ class RefOracle:
         lib.ref_layer_attention_tokens.argtypes = [_F, _F, _U16, _U16, _U16, _U16, _U16, _U16, _P, _F, _I, _I, _I, _I,
                                                    _F, _F, _F, _F]
         lib.gemma3_rope_precompute.argtypes = [_F, _I, _I, ctypes.c_float]
+        lib.ref_st_num_slots.restype = _I
+        lib.ref_st_load_slots.restype = _P
+        lib.ref_st_load_slots.argtypes = [ctypes.c_char_p, ctypes.POINTER(_P)]
+        lib.ref_st_free.argtypes = [_P]
         self.lib = lib
 
     def rope_table(self, max_pos, theta):
@@ -118,6 +122,29 @@ class RefOracle:
                                       int(c.is_global), T, start_pos, c.max_seq, _fp(out))
         self.last_qk = (Q, K)  # the reference normalises/rotates Q and K in place
         return out
+
+    def load_weights(self, model_dir, shapes):
+        """The reference's st_load + gemma3_load_weights on `model_dir`.
+        shapes: {slot: shape} of the slots to copy out (slot numbering of
+        ref_st_load_slots: 0 embed, 1 + 13 l + j layer l's j-th weight,
+        1 + 13 * 34 final norm).  Returns ({slot: uint16 array}, [slots the
+        loader left NULL])."""
+        n = self.lib.ref_st_num_slots()
+        slots = (_P * n)()
+        h = self.lib.ref_st_load_slots(model_dir.encode(), slots)
+        if not h:
+            raise RuntimeError("reference loader failed")
+        try:
+            got = {}
+            for i, shape in shapes.items():
+                if slots[i]:
+                    cnt = int(np.prod(shape))
+                    buf = (ctypes.c_uint16 * cnt).from_address(slots[i])
+                    got[i] = np.frombuffer(buf, dtype=np.uint16).reshape(shape).copy()
+            missing = [i for i in range(n) if not slots[i]]
+        finally:
+            self.lib.ref_st_free(h)
+        return got, missing
 
     def gqa(self, q, kc, vc, seq_len):
         out = np.zeros(NH * HD, dtype=np.float32)

@@ -164,3 +164,61 @@ void ref_layer_attention_tokens(float *out, const float *x, const uint16_t *wq,
     }
     free(qb); free(kb); free(vb); free(ab); free(mask); free(scores); free(tmp);
 }
+
+/* ---------------------------------------------------------------------- */
+/* The reference's SafeTensors loader: st_load (gemma3_safetensors.c:393-486) */
+/* and gemma3_load_weights (:651-713), declared the way gemma3.c:49-55     */
+/* declares them.  ref_st_load_slots fills, in gemma3_weights_t order,      */
+/* slots[0] = embed_tokens, slots[1 + 13 l + j] = layer l's j-th weight     */
+/* (input_layernorm, q/k/v/o_proj, q/k_norm, post_attention_layernorm,      */
+/* gate/up/down_proj, pre/post_feedforward_layernorm), slots[1 + 13 * 34] = */
+/* the final norm: the pointers the reference model would read (NULL where  */
+/* the loader found no tensor).  Returns a handle for ref_st_free, or NULL  */
+/* when the loader fails.                                                   */
+/* ---------------------------------------------------------------------- */
+typedef struct st_context st_context;
+st_context *st_load(const char *model_dir);
+void st_free(st_context *ctx);
+gemma3_weights_t *gemma3_load_weights(st_context *st);
+void gemma3_free_weights(gemma3_weights_t *w);
+
+typedef struct { st_context *st; gemma3_weights_t *w; } ref_st_handle;
+
+int ref_st_num_slots(void) { return 2 + 13 * GEMMA3_NUM_LAYERS; }
+
+void *ref_st_load_slots(const char *dir, const uint16_t **slots) {
+    st_context *st = st_load(dir);
+    if (!st) return NULL;
+    gemma3_weights_t *w = gemma3_load_weights(st);
+    if (!w) { st_free(st); return NULL; }
+    slots[0] = w->embed_tokens;
+    for (int l = 0; l < GEMMA3_NUM_LAYERS; l++) {
+        const uint16_t **s = slots + 1 + 13 * l;
+        s[0] = w->layers[l].input_layernorm;
+        s[1] = w->layers[l].q_proj;
+        s[2] = w->layers[l].k_proj;
+        s[3] = w->layers[l].v_proj;
+        s[4] = w->layers[l].o_proj;
+        s[5] = w->layers[l].q_norm;
+        s[6] = w->layers[l].k_norm;
+        s[7] = w->layers[l].post_attention_layernorm;
+        s[8] = w->layers[l].gate_proj;
+        s[9] = w->layers[l].up_proj;
+        s[10] = w->layers[l].down_proj;
+        s[11] = w->layers[l].pre_feedforward_layernorm;
+        s[12] = w->layers[l].post_feedforward_layernorm;
+    }
+    slots[1 + 13 * GEMMA3_NUM_LAYERS] = w->norm;
+    ref_st_handle *h = (ref_st_handle *)malloc(sizeof(ref_st_handle));
+    h->st = st;
+    h->w = w;
+    return h;
+}
+
+void ref_st_free(void *p) {
+    ref_st_handle *h = (ref_st_handle *)p;
+    if (!h) return;
+    gemma3_free_weights(h->w);
+    st_free(h->st);
+    free(h);
+}

@@ -24,7 +24,7 @@ from oracles import bf16_round, best_oracle, rel_err
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-2
-CTX = 32769          # rows 0..32767 cached, the new token at position 32768
+CTX = 32770          # rows 0..32767 cached; new tokens at positions 32768 and 32769
 LAYER = 5            # the only global layer of a 6-layer context
 LAUNCHES_LONG = 3    # prologue_decode + decode_splitkv<plain> + merge_partials
 

@@ -113,6 +113,98 @@ def test_check_rejects_bad_checkpoints(tmp_path, case, needle):
     assert needle in str(e.value)
 
 
+SLOT_NAMES = [n for n, _ in LAYER_TENSORS]  # gemma3_weights_t order of a layer's 13 weights
+REF_LAYERS = 34                              # gemma3_load_weights always walks GEMMA3_NUM_LAYERS
+
+
+def _ref_oracle():
+    from oracles import RefOracle
+    try:
+        return RefOracle()
+    except (FileNotFoundError, OSError):
+        pytest.skip("reference build (oracle/_ref) not available")
+
+
+def _random_checkpoint(d, L, V, seed):
+    """L layers, vocab V, BF16 ~N(0, 0.02) matrices and ~N(0, 0.1) norms, two shards."""
+    import synth
+    rng = np.random.default_rng(seed)
+
+    def w(shape, std=0.02):
+        return synth.bf16_trunc((rng.standard_normal(shape, dtype=np.float32) * std).astype(np.float32))
+
+    pre = "language_model.model."
+    data = {pre + "embed_tokens.weight": w((V, H)), pre + "norm.weight": w((H,), 0.1)}
+    for l in range(L):
+        for n, shp in LAYER_TENSORS:
+            data[f"{pre}layers.{l}.{n}"] = w(shp, 0.1 if len(shp) == 1 else 0.02)
+    write_model(d, L, V, data)
+    return data
+
+
+def _slot_shapes(L, V):
+    shapes = {0: (V, H), 1 + 13 * REF_LAYERS: (H,)}
+    for l in range(L):
+        for j, (_, shp) in enumerate(LAYER_TENSORS):
+            shapes[1 + 13 * l + j] = shp
+    return shapes
+
+
+def test_reference_loader_reads_the_fixture(tmp_path):
+    """The reference's own loader (st_load + gemma3_load_weights, compiled
+    from its sources into oracle/_ref) resolves every weight of the two-shard
+    fixture to the bytes written, and leaves the absent layers NULL: the
+    fixture is a checkpoint in the reference's sense."""
+    ref = _ref_oracle()
+    L, V = 2, 96
+    data = _random_checkpoint(str(tmp_path), L, V, 7100)
+    got, missing = ref.load_weights(str(tmp_path), _slot_shapes(L, V))
+    pre = "language_model.model."
+    assert np.array_equal(got[0], data[pre + "embed_tokens.weight"])
+    assert np.array_equal(got[1 + 13 * REF_LAYERS], data[pre + "norm.weight"])
+    for l in range(L):
+        for j, n in enumerate(SLOT_NAMES):
+            assert np.array_equal(got[1 + 13 * l + j], data[f"{pre}layers.{l}.{n}"]), (l, n)
+    assert missing == list(range(1 + 13 * L, 1 + 13 * REF_LAYERS))
+
+
+@pytest.mark.gpu
+def test_load_matches_reference_loader(tmp_path):
+    """gemma3_cuda_load_safetensors against the reference's loader: the
+    weights the reference's gemma3_load_weights resolves (read through its
+    own pointers) are uploaded directly into one context, the checkpoint is
+    loaded by this library into another, and a prompt plus one greedy step
+    give identical tokens and top-1 logits."""
+    ref = _ref_oracle()
+    L, V = 2, 512
+    _random_checkpoint(str(tmp_path), L, V, 7200)
+    got, _ = ref.load_weights(str(tmp_path), _slot_shapes(L, V))
+
+    def run(ctx):
+        ctx.upload_rope(gc.rope_table(256, 1e4), gc.rope_table(256, 1e6))
+        nxt, top = ctx.prefill_greedy(0, [3, 1, 4, 1, 5, 9, 2, 6], 0)
+        n2, t2 = ctx.greedy_step([0], [8], [nxt])
+        return nxt, top, int(n2[0]), float(t2[0])
+
+    a = gc.Context(max_context=256, max_batch=1, max_prefill=8, num_layers=L)
+    try:
+        a.load_safetensors(str(tmp_path))
+        mine = run(a)
+    finally:
+        a.close()
+    b = gc.Context(max_context=256, max_batch=1, max_prefill=8, num_layers=L)
+    try:
+        for l in range(L):
+            lw = {n.replace(".weight", "").replace("self_attn.", "").replace("mlp.", ""): got[1 + 13 * l + j]
+                  for j, n in enumerate(SLOT_NAMES)}
+            b.set_layer_weights(l, **lw)
+        b.set_embeddings(got[0], got[1 + 13 * REF_LAYERS])
+        theirs = run(b)
+    finally:
+        b.close()
+    assert mine == theirs
+
+
 @pytest.mark.gpu
 def test_load_matches_direct_upload(tmp_path):
     """2 layers, vocab 512: a prompt and one greedy step give the same tokens
