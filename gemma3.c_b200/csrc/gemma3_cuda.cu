@@ -892,17 +892,62 @@ extern "C" int gemma3_cuda_attn_decode_dev(gemma3_cuda_ctx *ctx, int layer, int 
     return gemma3_cuda_merge_partials_dev(ctx, ctx->cfg.kv_ranks, B, ctx->gather, out);
 }
 
+// Device address of a page-locked (cudaHostAlloc / cudaHostRegister) host
+// buffer, or null for ordinary pageable memory.
+static const void *mapped_host(const void *p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();  // pageable memory on older runtimes reports an error: clear it
+        return nullptr;
+    }
+    return a.type == cudaMemoryTypeHost ? a.devicePointer : nullptr;
+}
+
+// Whether the decode of this call runs the fused kernel with more than one
+// split per (sequence, kv head): each such CTA reads its q and k/v rows
+// itself, so inputs in host memory would cross PCIe once per split.
+static bool decode_rereads_inputs(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_ids, const int *pos) {
+    DecodePlan pl;
+    if (ctx->cfg.kv_dtype == GEMMA3_CUDA_KV_BF16)
+        plan_decode<__nv_bfloat16>(ctx, layer, B, seq_ids, pos, pl);
+    else
+        plan_decode<float>(ctx, layer, B, seq_ids, pos, pl);
+    return pl.chunk < 2048 && pl.nsplit > 1;
+}
+
 extern "C" int gemma3_cuda_attn_decode(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_ids, const int *pos,
                                        const float *Q, const float *K, const float *V, float *out) {
     if (int r = decode_check(ctx, layer, B, seq_ids, pos)) return r;
     if (!Q || !K || !V || !out) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null buffer");
     CU_TRY(cudaSetDevice(ctx->cfg.device));
     float *dq = ctx->io, *dk = dq + (size_t)B * 2048, *dv = dk + (size_t)B * 1024, *dout = dv + (size_t)B * 1024;
-    CU_TRY(cudaMemcpyAsync(dq, Q, (size_t)B * 2048 * 4, cudaMemcpyHostToDevice, ctx->stream));
-    CU_TRY(cudaMemcpyAsync(dk, K, (size_t)B * 1024 * 4, cudaMemcpyHostToDevice, ctx->stream));
-    CU_TRY(cudaMemcpyAsync(dv, V, (size_t)B * 1024 * 4, cudaMemcpyHostToDevice, ctx->stream));
-    if (int r = gemma3_cuda_attn_decode_dev(ctx, layer, B, seq_ids, pos, dq, dk, dv, dout)) return r;
-    CU_TRY(cudaMemcpyAsync(out, dout, (size_t)B * 2048 * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    // Page-locked host buffers are used in place: the kernels read q/k/v and
+    // write the output across PCIe themselves (inside the launches, so the
+    // transfer overlaps the cache streaming), instead of separate copies
+    // around them.  Pageable buffers, context-parallel global layers and
+    // calls whose fused kernel would read its inputs once per split go
+    // through the staging copies.
+    const bool split = ctx->layers[layer].is_global && ctx->cfg.kv_ranks > 1;
+    const float *hq = nullptr, *hk = nullptr, *hv = nullptr;
+    float *hout = nullptr;
+    if (!split) {
+        hout = (float *)mapped_host(out);
+        if (hout && !decode_rereads_inputs(ctx, layer, B, seq_ids, pos)) {
+            hq = (const float *)mapped_host(Q);
+            hk = (const float *)mapped_host(K);
+            hv = (const float *)mapped_host(V);
+        }
+    }
+    const bool in_place = hq && hk && hv;
+    if (!in_place) {
+        CU_TRY(cudaMemcpyAsync(dq, Q, (size_t)B * 2048 * 4, cudaMemcpyHostToDevice, ctx->stream));
+        CU_TRY(cudaMemcpyAsync(dk, K, (size_t)B * 1024 * 4, cudaMemcpyHostToDevice, ctx->stream));
+        CU_TRY(cudaMemcpyAsync(dv, V, (size_t)B * 1024 * 4, cudaMemcpyHostToDevice, ctx->stream));
+    }
+    if (int r = gemma3_cuda_attn_decode_dev(ctx, layer, B, seq_ids, pos, in_place ? hq : dq, in_place ? hk : dk,
+                                            in_place ? hv : dv, hout ? hout : dout))
+        return r;
+    if (!hout) CU_TRY(cudaMemcpyAsync(out, dout, (size_t)B * 2048 * 4, cudaMemcpyDeviceToHost, ctx->stream));
     return gemma3_cuda_synchronize(ctx);
 }
 

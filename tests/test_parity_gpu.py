@@ -373,3 +373,34 @@ def test_prefill_local_balanced_chunked(ropes):
     want = want.view(T1, 2048).cpu().numpy()
     assert np.isfinite(got).all()
     assert rel_err(got, want) <= TOL, rel_err(got, want)
+
+
+@pytest.mark.parametrize("layer,B,pos,ctxlen", [
+    (0, 64, 1100, 2048),     # local layer, fused kernel, one split per (seq, kv head): in place
+    (5, 64, 16384, 16385),   # global layer, long-range form (prologue + split + merge): in place
+    (0, 4, 1100, 2048),      # fused kernel with several splits: inputs staged, output in place
+])
+def test_decode_pinned_host_buffers(ropes, layer, B, pos, ctxlen):
+    """gemma3_cuda_attn_decode with page-locked host buffers (used in place
+    by the kernels) gives bit-identical results to pageable buffers (staged
+    through device copies).  Decoding the same token twice at the same
+    position rewrites the same cache row, so both calls see the same cache."""
+    import torch
+    rope_l = gc.rope_table(ctxlen, 1e4)
+    rope_g = gc.rope_table(ctxlen, 1e6)
+    ctx = gc.Context(max_context=ctxlen, max_batch=B, kv_dtype=gc.KV_BF16, max_prefill=64, num_layers=6)
+    ctx.upload_rope(rope_l, rope_g)
+    qn, kn = synth.qk_norm_gains(61)
+    ctx.set_qk_norm(layer, qn, kn)
+    for s in range(B):
+        ctx.fill_cache_random(layer, s, pos if gc.is_global_layer(layer) else 1024, 4000 + s)
+    Q, K, V = (synth.normal(62, (B, gc.Q_SIZE)), synth.normal(63, (B, gc.KV_SIZE)),
+               synth.normal(64, (B, gc.KV_SIZE)))
+    seqs, poss = list(range(B)), [pos] * B
+    want = ctx.attn_decode(layer, seqs, poss, Q, K, V)
+    pin = [torch.from_numpy(a).pin_memory() for a in (Q, K, V)]
+    out = torch.full((B, gc.Q_SIZE), float("nan")).pin_memory()
+    for _ in range(2):
+        got = ctx.attn_decode(layer, seqs, poss, pin[0].numpy(), pin[1].numpy(), pin[2].numpy(), out=out.numpy())
+        assert np.array_equal(got, want)
+    ctx.close()
