@@ -21,10 +21,12 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <type_traits>
 #include <vector>
 
 #include "../../include/gemma3_cuda.h"
 #include "attn_kernels.cuh"
+#include "decode_tc.cuh"
 #include "proj_kernels.cuh"
 #include "layer_kernels.cuh"
 #include "safetensors.hpp"
@@ -136,6 +138,21 @@ static int make_map4(CUtensorMap *m, const void *base, int rows, size_t plane_st
     return 0;
 }
 
+// A layer's BF16 cache [planes][rows][256] viewed as 4-D {64 dims, rows,
+// 4 dim-blocks, planes}: one box {64, 128, 1, 1} is a 16 KB chunk [128
+// rows][128 B] (128-byte swizzle) of one plane, the unit decode_tc streams.
+static int make_map_kv(CUtensorMap *m, const void *base, int rows, int planes) {
+    cuuint64_t dims[4] = {64, (cuuint64_t)rows, (cuuint64_t)(kHeadDim / 64), (cuuint64_t)planes};
+    cuuint64_t strides[3] = {(cuuint64_t)kHeadDim * 2, 128, (cuuint64_t)rows * kHeadDim * 2};
+    cuuint32_t box[4] = {64, (cuuint32_t)g3::kTcTK, 1, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return 0;
+}
+
 // Launch with programmatic stream serialization: the kernel may begin while
 // the previous kernel of the stream drains; the decode-path kernels call
 // griddepcontrol.wait before touching memory another kernel writes.
@@ -158,6 +175,7 @@ static cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
 // ------------------------------------------------------------------ context
 struct LayerState {
     void *kv = nullptr;
+    CUtensorMap tm_kv;  // BF16 cache: the chunk map decode_tc streams
     int rows = 0;
     int is_global = 0;
     uint16_t *qn = nullptr, *kn = nullptr;
@@ -223,6 +241,7 @@ struct gemma3_cuda_ctx {
     unsigned *err_host = nullptr;  // pinned copy of *err, read back on the stream
     long long launches = 0;
     int sm_count = 148;
+    int dec_ctas_per_sm = 2;  // resident split-KV decode CTAs per SM (occupancy query)
     // prefill piece partials of the balanced local-layer schedule (first use)
     float *pf_scratch = nullptr;
     float2 *pf_ml = nullptr;
@@ -395,6 +414,16 @@ static int ctx_alloc(gemma3_cuda_ctx *c) {
     CU_TRY(cudaFuncSetAttribute(g3::decode_splitkv<__nv_bfloat16, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, dsm_bf));
     CU_TRY(cudaFuncSetAttribute(g3::decode_splitkv<float, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, dsm_f));
     if (int r = load_encode()) return r;
+    if (k.kv_dtype == GEMMA3_CUDA_KV_BF16) {
+        for (auto &L : c->layers)
+            if (int r = make_map_kv(&L.tm_kv, L.kv, L.rows, k.max_batch * 2 * kKvHeads)) return r;
+        CU_TRY(cudaFuncSetAttribute(g3::decode_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, g3::kTcSmem));
+        CU_TRY(cudaFuncSetAttribute(g3::decode_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, g3::kTcSmem));
+        CU_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&c->dec_ctas_per_sm, g3::decode_tc<false>,
+                                                             g3::kTcThreads, g3::kTcSmem));
+        if (c->dec_ctas_per_sm < 1)
+            return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "decode_tc cannot be resident on this device");
+    }
     CU_TRY(cudaStreamSynchronize(c->stream));
     return 0;
 }
@@ -687,7 +716,11 @@ static int decode_check(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_i
 template <typename KVT>
 static void plan_decode(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_ids, const int *pos, DecodePlan &pl) {
     const LayerState &L = ctx->layers[layer];
-    constexpr int TK = g3::DecodeCfg<KVT>::TK;
+    // tile rows: decode_tc streams 128-row tiles (BF16), decode_splitkv
+    // 16-row tiles (fp32); a split holds whole tiles except for its last
+    constexpr bool kTc = std::is_same<KVT, __nv_bfloat16>::value;
+    constexpr int TK = kTc ? g3::kTcTK : g3::DecodeCfg<KVT>::TK;
+    constexpr int kMinTiles = kTc ? 1 : 2;
     pl.rows.B = B;
     int maxrows = 0;
     for (int b = 0; b < B; ++b) {
@@ -715,7 +748,7 @@ static void plan_decode(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_i
     // B=64 x 32K global rows: splits of ~4K rows (7 full waves).  Splits hold
     // at least 2 tiles, and a unit at most kMaxSplit.
     const int units = B * kKvHeads;
-    const int slots = 2 * ctx->sm_count;
+    const int slots = (kTc ? ctx->dec_ctas_per_sm : 2) * ctx->sm_count;
     const double row_bytes = 2.0 * kHeadDim * sizeof(KVT);
     constexpr double kRate = 22.6e3;  // bytes per us per CTA
     constexpr double kFixed = 4.0, kMergeCost = 2.0;
@@ -723,7 +756,7 @@ static void plan_decode(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_i
     double best = 1e300;
     for (int s = 1; s <= kMaxSplit; ++s) {
         long long c = (maxrows + s - 1) / s;
-        c = std::max<long long>(c, 2 * TK);
+        c = std::max<long long>(c, kMinTiles * TK);
         c = (c + TK - 1) / TK * TK;
         const long long ns = (maxrows + c - 1) / c;
         if (ns > kMaxSplit) continue;
@@ -735,7 +768,7 @@ static void plan_decode(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_i
             best = t;
             chunk = c;
         }
-        if (c == 2 * TK) break;  // smaller splits only repeat this one
+        if (c == kMinTiles * TK) break;  // smaller splits only repeat this one
     }
     pl.chunk = (int)chunk;
     pl.nsplit = std::max(1, (int)((maxrows + chunk - 1) / chunk));
@@ -783,12 +816,19 @@ static int decode_impl(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_id
                      (fused ? g3::kFusedExtra<KVT> : 0);
     size_t e0;
     prof_begin(ctx, &e0);
-    if (fused)
-        launch_pdl(g3::decode_splitkv<KVT, true>, dim3(pl.nsplit, kKvHeads, B), dim3(256), smem, ctx->stream, p,
-                   pl.rows);
-    else
-        launch_pdl(g3::decode_splitkv<KVT, false>, dim3(pl.nsplit, kKvHeads, B), dim3(256), smem, ctx->stream, p,
-                   pl.rows);
+    const dim3 grid(pl.nsplit, kKvHeads, B);
+    if constexpr (std::is_same<KVT, __nv_bfloat16>::value) {
+        // BF16 cache: both contractions on the tensor core
+        const CUtensorMap &tm = ctx->layers[layer].tm_kv;
+        if (fused)
+            launch_pdl(g3::decode_tc<true>, grid, dim3(g3::kTcThreads), g3::kTcSmem, ctx->stream, tm, p, pl.rows);
+        else
+            launch_pdl(g3::decode_tc<false>, grid, dim3(g3::kTcThreads), g3::kTcSmem, ctx->stream, tm, p, pl.rows);
+    } else if (fused) {
+        launch_pdl(g3::decode_splitkv<KVT, true>, grid, dim3(256), smem, ctx->stream, p, pl.rows);
+    } else {
+        launch_pdl(g3::decode_splitkv<KVT, false>, grid, dim3(256), smem, ctx->stream, p, pl.rows);
+    }
     if (ctx->prof) {
         // algorithmic bytes: every attended K and V row once
         double rows = 0;
