@@ -42,13 +42,22 @@
 namespace g3 {
 
 constexpr int kTcTK = 128;                    // cache rows per tile
-constexpr int kTcSlots = 6;                   // ring of 16 KB chunks
 constexpr uint32_t kTcChunk = 128 * 128;      // [128 rows][64 dims] bf16
-constexpr uint32_t kTcOffQ = kTcSlots * kTcChunk;  // Qs [4 dim-chunks][16 rows][128 B]
-constexpr uint32_t kTcOffP = kTcOffQ + 8192;        // P^T [2 key-chunks][16 rows][128 B]
-constexpr uint32_t kTcOffQf = kTcOffP + 4096;       // fused prologue: q heads fp32 [2][256]
-constexpr uint32_t kTcOffBar = kTcOffQf + 2048;     // mbarriers, reductions, flags
-constexpr uint32_t kTcSmem = kTcOffBar + 512;       // 113,152 B: two CTAs per SM
+constexpr int kTcSlots = 6;                   // ring of 16 KB chunks
+// Shared memory: the ring, then
+//   Qs  [4 dim-chunks][16 rows][128 B]   8 KB
+//   P^T [2 key-chunks][16 rows][128 B]   4 KB
+//   q heads fp32 [2][256] (fused prologue) 2 KB
+//   mbarriers, reductions, flags           512 B
+// = 113,152 B: two CTAs per SM, so one CTA's softmax and copies overlap the
+// other's MMAs.  (A one-CTA-per-SM build with a 12-chunk ring and double-
+// buffered S^T / O^T / P^T, overlapping a CTA's own tiles, measured no
+// faster at any batch: a lone CTA streamed ~45 GB/s either way.)
+constexpr uint32_t kTcOffQ = kTcSlots * kTcChunk;
+constexpr uint32_t kTcOffP = kTcOffQ + 8192;
+constexpr uint32_t kTcOffQf = kTcOffP + 4096;
+constexpr uint32_t kTcOffBar = kTcOffQf + 2048;
+constexpr uint32_t kTcSmem = kTcOffBar + 512;
 constexpr int kTcThreads = 192;
 constexpr uint32_t kTcTmemCols = 128;
 constexpr uint32_t kTcTmemS = 0;
@@ -88,29 +97,52 @@ __device__ __forceinline__ uint16_t bf16_bits(float x) {
 }
 
 // Log-sum-exp merge of n partials [m, l, O[256]] of the two heads of group
-// g by 128 threads: thread t writes dims t and t + 128 of both heads.
+// g by 128 threads: thread t writes dims t and t + 128 of both heads.  One
+// online pass over the partials (read through L2: other CTAs wrote them),
+// 16 partials (48 loads) in flight per thread and head.
 __device__ __forceinline__ void tc_merge_group(const float *base, size_t hstride, int n, float *out_g) {
+    constexpr int C = 16;
     const int t = threadIdx.x;
-#pragma unroll
+#pragma unroll 1
     for (int hh = 0; hh < 2; ++hh) {
         const float *bh = base + hh * hstride;
-        float M = -INFINITY;
-        for (int i = 0; i < n; ++i) M = fmaxf(M, __ldcg(bh + (size_t)i * (kHeadDim + 2)));
-        float L = 0.f, A = 0.f, Bv = 0.f;
-        if (M != -INFINITY) {
-            for (int i = 0; i < n; ++i) {
-                const float *pp = bh + (size_t)i * (kHeadDim + 2);
-                const float m = __ldcg(pp);
-                if (m == -INFINITY) continue;
-                const float f = ex2_approx(m - M);
-                L += __ldcg(pp + 1) * f;
-                A += __ldcg(pp + 2 + t) * f;
-                Bv += __ldcg(pp + 2 + 128 + t) * f;
+        float Mx = -INFINITY, Lt = 0.f, At = 0.f, Bt = 0.f;
+#pragma unroll 1
+        for (int i0 = 0; i0 < n; i0 += C) {
+            float2 ml[C];
+            float oa[C], ob[C];
+#pragma unroll
+            for (int j = 0; j < C; ++j) {
+                if (i0 + j < n) {
+                    const float *pp = bh + (size_t)(i0 + j) * (kHeadDim + 2);
+                    ml[j] = __ldcg(reinterpret_cast<const float2 *>(pp));
+                    oa[j] = __ldcg(pp + 2 + t);
+                    ob[j] = __ldcg(pp + 2 + 128 + t);
+                } else {
+                    ml[j] = make_float2(-INFINITY, 0.f);
+                    oa[j] = ob[j] = 0.f;
+                }
             }
+            float cm = Mx;
+#pragma unroll
+            for (int j = 0; j < C; ++j) cm = fmaxf(cm, ml[j].x);
+            if (cm == -INFINITY) continue;  // no rows so far
+            const float sc = Mx == -INFINITY ? 0.f : ex2_approx(Mx - cm);
+            Lt *= sc;
+            At *= sc;
+            Bt *= sc;
+#pragma unroll
+            for (int j = 0; j < C; ++j) {
+                const float f = ml[j].x == -INFINITY ? 0.f : ex2_approx(ml[j].x - cm);
+                Lt += ml[j].y * f;
+                At += oa[j] * f;
+                Bt += ob[j] * f;
+            }
+            Mx = cm;
         }
-        const float inv = L > 0.f ? 1.0f / L : 0.f;
-        out_g[hh * kHeadDim + t] = A * inv;
-        out_g[hh * kHeadDim + 128 + t] = Bv * inv;
+        const float inv = Lt > 0.f ? 1.0f / Lt : 0.f;
+        out_g[hh * kHeadDim + t] = At * inv;
+        out_g[hh * kHeadDim + 128 + t] = Bt * inv;
     }
 }
 
@@ -131,7 +163,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     unsigned char *sP = sm + kTcOffP;
     float(*qf)[kHeadDim] = reinterpret_cast<float(*)[kHeadDim]>(sm + kTcOffQf);
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kTcOffBar);
-    uint64_t *full = bars, *empty = bars + kTcSlots;
+    uint64_t *full = bars, *empty = bars + kTcSlots;  // [kTcSlots] each
     uint64_t &q_ready = bars[12], &s_full = bars[13], &p_full = bars[14], &o_full = bars[15], &o_free = bars[16],
              &row_ready = bars[17], &mma_done = bars[18];
     uint32_t &tmem_slot = *reinterpret_cast<uint32_t *>(bars + 19);
@@ -139,6 +171,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     volatile int &s_flag = *reinterpret_cast<volatile int *>(bars + 21);  // compute warps: any failed / last split
     float(*red)[4][2] = reinterpret_cast<float(*)[4][2]>(bars + 22);     // [2][4][2] floats = 64 B
     float(*lred)[2] = reinterpret_cast<float(*)[2]>(bars + 30);          // [4][2] = 32 B
+    static_assert((kTcSlots % 2) == 0, "V chunk pairs must not wrap the ring");
 
     const int split = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -213,11 +246,11 @@ __global__ void __launch_bounds__(kTcThreads, 2)
             const uint64_t dQ = smem_desc_sw128(smem_u32(sQ), 16, 1024);
             const uint64_t dP = smem_desc_sw128(smem_u32(sP), 16, 1024);
             bool ok = mbar_wait(&q_ready, 0, p.err);
-            for (int i = 0; ok && i < ntiles; ++i) {
-                // S^T = K . Qs^T, the K tile's four dim-chunks as they land
-                for (int c = 0; c < 4 && ok; ++c) {
+            // S^T(i) = K(i) . Qs^T, the K tile's four dim-chunks as they land
+            auto issue_s = [&](int i) {
+                for (int c = 0; c < 4; ++c) {
                     const int q = 8 * i + c, s = q % kTcSlots;
-                    if (s_abort || !mbar_wait(&full[s], (q / kTcSlots) & 1, p.err)) { ok = false; break; }
+                    if (s_abort || !mbar_wait(&full[s], (q / kTcSlots) & 1, p.err)) return false;
                     tc_fence_after();
 #pragma unroll
                     for (int kk = 0; kk < 4; ++kk)
@@ -225,10 +258,13 @@ __global__ void __launch_bounds__(kTcThreads, 2)
                                    dQ + (uint64_t)((c * 2048 + kk * 32) >> 4), idS, (c | kk) ? 1u : 0u);
                     tc_commit(&empty[s]);
                 }
-                if (!ok) break;
                 tc_commit(&s_full);
-                // O^T = V^T . P^T once the softmax has written P (and, from the
-                // second tile on, the compute warps have read the last O^T)
+                return true;
+            };
+            if (ok && ntiles > 0) ok = issue_s(0);
+            for (int i = 0; ok && i < ntiles; ++i) {
+                // O^T(i) = V(i)^T . P^T(i) once the softmax has written P(i) and
+                // the compute warps have read the previous O^T
                 if (!mbar_wait(&p_full, i & 1, p.err) || (i >= 1 && !mbar_wait(&o_free, (i - 1) & 1, p.err))) {
                     ok = false;
                     break;
@@ -250,6 +286,9 @@ __global__ void __launch_bounds__(kTcThreads, 2)
                 }
                 if (!ok) break;
                 tc_commit(&o_full);
+                // the next tile's S overwrites the S^T the softmax has read
+                // (P(i) is written only after that read)
+                if (i + 1 < ntiles && !(ok = issue_s(i + 1))) break;
             }
             if (!ok) s_abort = 1;
             // drain: every MMA this thread issued has completed
@@ -259,7 +298,6 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     } else {
         // ------------------------------------------------ compute warps 0-3
         const int t = threadIdx.x;  // 0..127
-        const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
         // Fused prologue (gemma3_transformer.c:294-316): warps 0-1 normalise
         // + rotate the group's two query heads; in the CTA holding the new
         // token's cache row, warps 2-3 build that k / v row and append it.
@@ -319,6 +357,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
             mbar_arrive(&q_ready);
         }
 
+        const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
         float m0 = -INFINITY, m1 = -INFINITY;  // running maxima (log2 domain)
         float l0 = 0.f, l1 = 0.f;              // this thread's share of the sums
         float a00 = 0.f, a01 = 0.f, a10 = 0.f, a11 = 0.f;  // O[head][dim t / t+128]
@@ -326,6 +365,8 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         // whatever happens: after a failed wait a warp keeps iterating with
         // its waits and TMEM reads skipped (ok = false), so no barrier is
         // ever left one warp short.
+        // Tile i: S^T(i) -> P(i) -> (tensor core: O^T(i)) -> O^T(i) folded in,
+        // which releases the O^T accumulator for the next tile's P.V.
         bool ok = true;
         for (int i = 0; i < ntiles; ++i) {
             ok = __all_sync(0xffffffffu, ok && !s_abort && mbar_wait(&s_full, i & 1, p.err));
@@ -360,13 +401,14 @@ __global__ void __launch_bounds__(kTcThreads, 2)
             m0 = n0;
             m1 = n1;
             {
+                unsigned char *pb = sP;
                 const uint16_t h0 = bf16_bits(p0), h1 = bf16_bits(p1);
                 const uint16_t e0 = bf16_bits(p0 - __uint_as_float((uint32_t)h0 << 16));
                 const uint16_t e1 = bf16_bits(p1 - __uint_as_float((uint32_t)h1 << 16));
-                *reinterpret_cast<uint16_t *>(sP + sw128_off(0, t, 16)) = h0;
-                *reinterpret_cast<uint16_t *>(sP + sw128_off(1, t, 16)) = e0;
-                *reinterpret_cast<uint16_t *>(sP + sw128_off(2, t, 16)) = h1;
-                *reinterpret_cast<uint16_t *>(sP + sw128_off(3, t, 16)) = e1;
+                *reinterpret_cast<uint16_t *>(pb + sw128_off(0, t, 16)) = h0;
+                *reinterpret_cast<uint16_t *>(pb + sw128_off(1, t, 16)) = e0;
+                *reinterpret_cast<uint16_t *>(pb + sw128_off(2, t, 16)) = h1;
+                *reinterpret_cast<uint16_t *>(pb + sw128_off(3, t, 16)) = e1;
             }
             fence_proxy_async_smem();
             tc_fence_before();  // S read before the next S MMA overwrites it

@@ -241,7 +241,7 @@ struct gemma3_cuda_ctx {
     unsigned *err_host = nullptr;  // pinned copy of *err, read back on the stream
     long long launches = 0;
     int sm_count = 148;
-    int dec_ctas_per_sm = 2;  // resident split-KV decode CTAs per SM (occupancy query)
+    int dec_ctas_per_sm = 2;  // resident decode_tc CTAs per SM (occupancy query)
     // prefill piece partials of the balanced local-layer schedule (first use)
     float *pf_scratch = nullptr;
     float2 *pf_ml = nullptr;
