@@ -171,11 +171,11 @@ __device__ __forceinline__ void check_half_range(const HeadRow &r, unsigned *err
     bool bad = false;
 #pragma unroll
     for (int j = 0; j < 4; ++j) bad |= !(fabsf(r.a[j]) <= 65504.f) || !(fabsf(r.b[j]) <= 65504.f);
-    if (bad) atomicOr(err, kErrRange);
+    if (bad) raise_status(err, kErrRange);
 }
 
 __device__ __forceinline__ __half to_half_checked(float x, unsigned *err) {
-    if (!(fabsf(x) <= 65504.f)) atomicOr(err, kErrRange);
+    if (!(fabsf(x) <= 65504.f)) raise_status(err, kErrRange);
     return __float2half_rn(x);
 }
 
@@ -863,7 +863,7 @@ __global__ void __launch_bounds__(256) merge_peer_partials(const PeerXchg px, fl
                 }
             }
         }
-        if (!good) atomicOr(err, kErrWaitTimeout);
+        if (!good) raise_status(err, kErrWaitTimeout);
         ok = good;
     }
     __syncthreads();
@@ -1062,7 +1062,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     // layout uses all of the 227 KB, so there is no room to realign: refuse
     // to run (status bit, no memory touched) if the base is not aligned.
     if (smem_u32(smem_raw) & 1023u) {
-        if (threadIdx.x == 0) atomicOr(p.err, kErrBadIndex);
+        if (threadIdx.x == 0) raise_status(p.err, kErrBadIndex);
         return;
     }
     unsigned char *sm = smem_raw;

@@ -155,7 +155,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     // realign.
     extern __shared__ __align__(1024) unsigned char sm[];
     if (smem_u32(sm) & 1023u) {
-        if (threadIdx.x == 0) atomicOr(p.err, kErrBadIndex);
+        if (threadIdx.x == 0) raise_status(p.err, kErrBadIndex);
         return;
     }
     unsigned char *ring = sm;

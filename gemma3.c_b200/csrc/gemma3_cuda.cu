@@ -238,7 +238,7 @@ struct gemma3_cuda_ctx {
     float *io = nullptr;
     size_t io_rows = 0;
     unsigned *err = nullptr;
-    unsigned *err_host = nullptr;  // pinned copy of *err, read back on the stream
+    unsigned *err_host = nullptr;  // page-locked word the kernels set non-zero when they raise a bit of *err
     long long launches = 0;
     int sm_count = 148;
     int dec_ctas_per_sm = 2;  // resident decode_tc CTAs per SM (occupancy query)
@@ -399,10 +399,16 @@ static int ctx_alloc(gemma3_cuda_ctx *c) {
     CU_TRY(cudaMalloc(&c->gather, (size_t)k.kv_ranks * k.max_batch * kHeads * kPartialStride * 4));
     c->io_rows = std::max(k.max_prefill, k.max_batch);
     CU_TRY(cudaMalloc(&c->io, c->io_rows * (2048 + 1024 + 1024 + 2048) * sizeof(float)));
-    CU_TRY(cudaMalloc(&c->err, sizeof(unsigned)));
-    CU_TRY(cudaMemsetAsync(c->err, 0, sizeof(unsigned), c->stream));
-    CU_TRY(cudaHostAlloc((void **)&c->err_host, sizeof(unsigned), cudaHostAllocDefault));
+    // status block [bits][pad][address of err_host] (see g3::raise_status)
+    CU_TRY(cudaHostAlloc((void **)&c->err_host, sizeof(unsigned), cudaHostAllocMapped));
     *c->err_host = 0;
+    {
+        void *mirror = nullptr;
+        CU_TRY(cudaHostGetDevicePointer(&mirror, c->err_host, 0));
+        unsigned long long blk[2] = {0ull, (unsigned long long)(uintptr_t)mirror};
+        CU_TRY(cudaMalloc(&c->err, sizeof blk));
+        CU_TRY(cudaMemcpy(c->err, blk, sizeof blk, cudaMemcpyHostToDevice));
+    }
     CU_TRY(cudaFuncSetAttribute(g3::prefill_fa_sm100, cudaFuncAttributeMaxDynamicSharedMemorySize, g3::kPfSmem));
     CU_TRY(cudaFuncSetAttribute(g3::proj_gemm_sm100, cudaFuncAttributeMaxDynamicSharedMemorySize, g3::kProjSmem));
     const int dsm_bf = g3::DecodeCfg<__nv_bfloat16>::NS * 2 * g3::DecodeCfg<__nv_bfloat16>::TK * kHeadDim * 2;
@@ -466,24 +472,22 @@ extern "C" long long gemma3_cuda_launch_count(gemma3_cuda_ctx *ctx) { return ctx
 extern "C" int gemma3_cuda_synchronize(gemma3_cuda_ctx *ctx) {
     if (!ctx) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null context");
     CU_TRY(cudaSetDevice(ctx->cfg.device));
-    // The status word comes back on the stream behind the call's own work,
-    // so one stream synchronisation covers both (no second blocking copy).
-    CU_TRY(cudaMemcpyAsync(ctx->err_host, ctx->err, sizeof(unsigned), cudaMemcpyDeviceToHost, ctx->stream));
     CU_TRY(cudaStreamSynchronize(ctx->stream));
-    const unsigned e = *ctx->err_host;
-    if (e) {
-        // an aborted launch may leave split tickets counted: start clean
-        cudaMemsetAsync(ctx->tickets, 0, (size_t)ctx->cfg.max_batch * kKvHeads * sizeof(unsigned), ctx->stream);
-        if (ctx->pf_tickets)
-            cudaMemsetAsync(ctx->pf_tickets, 0, g3::kPfMaxCtas * sizeof(unsigned), ctx->stream);
-        cudaMemsetAsync(ctx->err, 0, sizeof(unsigned), ctx->stream);
-        cudaStreamSynchronize(ctx->stream);
-        return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "device status 0x%x (%s)", e,
-                    (e & g3::kErrWaitTimeout) ? "bounded wait timed out"
-                    : (e & g3::kErrRange)     ? "prefill operand outside the fp16 range"
-                                              : "bad index");
-    }
-    return 0;
+    // Kernels that raise a status bit also set the page-locked err_host, so
+    // the status itself is copied back only after a failure.
+    if (*reinterpret_cast<volatile unsigned *>(ctx->err_host) == 0u) return 0;
+    unsigned e = 0;
+    CU_TRY(cudaMemcpy(&e, ctx->err, sizeof(unsigned), cudaMemcpyDeviceToHost));
+    // an aborted launch may leave split tickets counted: start clean
+    cudaMemsetAsync(ctx->tickets, 0, (size_t)ctx->cfg.max_batch * kKvHeads * sizeof(unsigned), ctx->stream);
+    if (ctx->pf_tickets) cudaMemsetAsync(ctx->pf_tickets, 0, g3::kPfMaxCtas * sizeof(unsigned), ctx->stream);
+    cudaMemsetAsync(ctx->err, 0, sizeof(unsigned), ctx->stream);
+    cudaStreamSynchronize(ctx->stream);
+    *reinterpret_cast<volatile unsigned *>(ctx->err_host) = 0u;
+    return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "device status 0x%x (%s)", e,
+                (e & g3::kErrWaitTimeout) ? "bounded wait timed out"
+                : (e & g3::kErrRange)     ? "prefill operand outside the fp16 range"
+                                          : "bad index");
 }
 
 // Host RoPE table, the formula of gemma3_rope_precompute
@@ -701,11 +705,12 @@ static int decode_check(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_i
     if (B <= 0 || B > ctx->cfg.max_batch || !seq_ids || !pos)
         return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad batch B=%d (max_batch %d)", B, ctx->cfg.max_batch);
     if (!ctx->rope_local) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "RoPE tables not uploaded");
-    std::vector<char> seen(ctx->cfg.max_batch, 0);
+    uint64_t seen[g3::kMaxDecodeBatch / 64] = {};  // max_batch <= kMaxDecodeBatch (checked at init)
     for (int b = 0; b < B; ++b) {
-        if (seq_ids[b] < 0 || seq_ids[b] >= ctx->cfg.max_batch || seen[seq_ids[b]])
-            return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad or repeated sequence slot %d", seq_ids[b]);
-        seen[seq_ids[b]] = 1;
+        const int s = seq_ids[b];
+        if (s < 0 || s >= ctx->cfg.max_batch || ((seen[s >> 6] >> (s & 63)) & 1u))
+            return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad or repeated sequence slot %d", s);
+        seen[s >> 6] |= 1ull << (s & 63);
         if (pos[b] < 0) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "negative position");
         if (pos[b] >= ctx->cfg.max_context)
             return fail(GEMMA3_CUDA_ERR_CONTEXT_OVERFLOW, "position %d >= max_context %d", pos[b], ctx->cfg.max_context);
@@ -1906,7 +1911,8 @@ extern "C" int gemma3_cuda_gqa_decode_noalloc(const float *q, const void *kv, in
     float *qs = scratch;
     float *part = scratch + kNoAllocQ;
     unsigned *status = reinterpret_cast<unsigned *>(scratch + kNoAllocQ + kNoAllocPart);
-    CU_TRY(cudaMemsetAsync(status, 0, sizeof(unsigned), st));
+    // status block: bits, pad, no host mirror (g3::raise_status)
+    CU_TRY(cudaMemsetAsync(status, 0, 16, st));
 
     // Split plan as for the context path, capped by the scratch slots.
     const bool bf = kv_dtype == GEMMA3_CUDA_KV_BF16;

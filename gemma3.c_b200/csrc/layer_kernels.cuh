@@ -47,7 +47,7 @@ __device__ __forceinline__ void rms_apply(float (&v)[kNormPer], const uint16_t *
 }
 
 __device__ __forceinline__ __half to_half_rc(float v, unsigned *err) {
-    if (!(fabsf(v) <= 65504.f)) atomicOr(err, kErrRange);
+    if (!(fabsf(v) <= 65504.f)) raise_status(err, kErrRange);
     return __float2half_rn(v);
 }
 
@@ -125,7 +125,7 @@ __global__ void __launch_bounds__(kNormThreads) embed_rows(const int *__restrict
     pdl_wait();
     const int tok = tokens[blockIdx.x];
     const bool ok = tok >= 0 && tok < vocab;
-    if (!ok && threadIdx.x == 0) atomicOr(err, kErrBadIndex);
+    if (!ok && threadIdx.x == 0) raise_status(err, kErrBadIndex);
     const uint16_t *row = embed + (size_t)(ok ? tok : 0) * kHiddenDim;
 #pragma unroll
     for (int i = 0; i < kNormPer; ++i) {

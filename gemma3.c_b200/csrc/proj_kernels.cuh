@@ -73,7 +73,7 @@ __global__ void __launch_bounds__(kProjThreads, 1)
                     const ProjParams p) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
     if (smem_u32(smem_raw) & 1023u) {
-        if (threadIdx.x == 0) atomicOr(p.err, kErrBadIndex);
+        if (threadIdx.x == 0) raise_status(p.err, kErrBadIndex);
         return;
     }
     unsigned char *sm = smem_raw;
@@ -271,7 +271,7 @@ __global__ void __launch_bounds__(256) to_f16_rows(const float *__restrict__ x, 
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
         const float4 v = reinterpret_cast<const float4 *>(x)[i];
         const float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-        if (!(m <= 65504.f)) atomicOr(err, kErrRange);
+        if (!(m <= 65504.f)) raise_status(err, kErrRange);
         uint2 o;
         o.x = pack_f16x2(v.x, v.y);
         o.y = pack_f16x2(v.z, v.w);
@@ -286,7 +286,7 @@ __global__ void __launch_bounds__(256) bf16_to_f16(const uint16_t *__restrict__ 
                                                    unsigned *err) {
     for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         const float f = __uint_as_float((uint32_t)src[i] << 16);
-        if (!(fabsf(f) <= 65504.f)) atomicOr(err, kErrRange);
+        if (!(fabsf(f) <= 65504.f)) raise_status(err, kErrRange);
         dst[i] = __float2half_rn(f);
     }
 }

@@ -18,6 +18,18 @@ enum : unsigned {
     kErrRange = 4u,  // a prefill operand exceeded the fp16 range
 };
 
+// Raises status bit `bit`.  The status word is the first of a 16-byte block
+// whose bytes 8-15 hold the address of a page-locked host word (or null);
+// that host word is set non-zero together with the bit, so the host learns
+// of a failure after a stream synchronisation without copying the status
+// back after every call.  A plain store suffices: the host word only ever
+// goes from 0 to non-zero on the device side.
+__device__ __forceinline__ void raise_status(unsigned *err, unsigned bit) {
+    atomicOr(err, bit);
+    unsigned *mirror = *reinterpret_cast<unsigned *const *>(err + 2);
+    if (mirror) *reinterpret_cast<volatile unsigned *>(mirror) = 1u;
+}
+
 // A bounded wait gives up after this much wall-clock time (globaltimer ns).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
@@ -92,7 +104,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsign
             if (globaltimer_ns() - t0 > kWaitLimitNs) break;
         }
     }
-    if (err) atomicOr(err, kErrWaitTimeout);
+    if (err) raise_status(err, kErrWaitTimeout);
     return false;
 }
 
