@@ -182,7 +182,7 @@ __device__ __forceinline__ __half to_half_checked(float x, unsigned *err) {
 template <typename KVT>
 __global__ void __launch_bounds__(512) prologue_prefill(const float *__restrict__ Q, const float *__restrict__ K,
                                                         const float *__restrict__ V, LayerDev L, float eps, int seq,
-                                                        int T, int start_pos, int kv_pos0,
+                                                        int T, int start_pos, int kv_pos0, int kv_end,
                                                         __half *__restrict__ qst, __half *__restrict__ kst,
                                                         __half *__restrict__ vst, int st_rows, unsigned *err) {
     const int t = blockIdx.x, y = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -209,6 +209,7 @@ __global__ void __launch_bounds__(512) prologue_prefill(const float *__restrict_
         store4<KVT>(dst + 4 * lane, r.a);
         store4<KVT>(dst + 128 + 4 * lane, r.b);
     }
+    if (pos < kv_pos0 || pos >= kv_end) return;  // a key the attention does not see here
     through_dtype<KVT>(r.a);
     through_dtype<KVT>(r.b);
     check_half_range(r, err);
@@ -771,6 +772,38 @@ __global__ void __launch_bounds__(256) merge_partials(const float *__restrict__ 
 }
 
 // ------------------------------------------------------------------------
+// Log-sum-exp merge of prefill outputs over disjoint key ranges (context-
+// parallel ranks): part r holds, per token and head, the output O_r
+// normalised over its keys and (m_r, l_r) from PrefillParams::ml_out.
+// out = sum_r w_r O_r / sum_r w_r with w_r = l_r 2^(m_r - M), M the largest
+// m_r among the parts with l_r > 0.  grid (T * 8), block 256 (one dim each);
+// part r's outputs at outs + r * pstride, its (m, l) at mls + r * mstride
+// (float2 units).
+__global__ void __launch_bounds__(256) merge_prefill_partials(const float *__restrict__ outs, size_t pstride,
+                                                             const float2 *__restrict__ mls, size_t mstride,
+                                                             int nparts, float *__restrict__ out) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int th = blockIdx.x, d = threadIdx.x;  // th = token * 8 + head
+    float M = -INFINITY;
+    for (int r = 0; r < nparts; ++r) {
+        const float2 ml = mls[r * mstride + th];
+        if (ml.y > 0.f) M = fmaxf(M, ml.x);
+    }
+    float W = 0.f, O = 0.f;
+    if (M != -INFINITY) {
+        for (int r = 0; r < nparts; ++r) {
+            const float2 ml = mls[r * mstride + th];
+            if (!(ml.y > 0.f)) continue;
+            const float w = ml.y * ex2_approx(ml.x - M);
+            W += w;
+            O += w * outs[r * pstride + (size_t)th * kHeadDim + d];
+        }
+    }
+    out[(size_t)th * kHeadDim + d] = W > 0.f ? O / W : 0.f;
+}
+
+// ------------------------------------------------------------------------
 // Context-parallel exchange over peer memory (global layers split across
 // GPUs).  Every rank owns a receive buffer [2 parity][R ranks][B][8][258]
 // and flags [2 parity][8]; each rank maps all ranks' buffers (CUDA IPC).
@@ -933,6 +966,10 @@ struct PrefillParams {
     int T;
     int start_pos;
     int kv_pos0;      // position of K/V row 0
+    int kv_end;       // one past the last key position staged (keys >= kv_end are not attended)
+    float2 *ml_out;   // null, or [T][8] (m, l) of every output row: its reference max (log2
+                      // domain) and softmax sum, so that outputs over disjoint key ranges of
+                      // the same queries (context-parallel ranks) can be merged
     int is_global;
     int nqb;          // query blocks of 64 tokens
     unsigned *err;
@@ -1007,9 +1044,10 @@ __device__ __forceinline__ PfUnit pf_unit(const PrefillParams &p, int idx) {
     u.t0 = qb * 64;
     u.qlo = p.start_pos + u.t0;
     u.qhi = p.start_pos + min(u.t0 + 64, p.T) - 1;
-    const int kmin = p.is_global ? 0 : max(0, u.qlo - (kWindow - 1));
+    const int kmin = max(p.kv_pos0, p.is_global ? 0 : u.qlo - (kWindow - 1));
+    const int kmax = min(u.qhi, p.kv_end - 1);  // >= kmin: the host launches only queries >= kv_pos0
     u.j0 = (kmin - p.kv_pos0) / 64;
-    u.ntiles = (u.qhi - p.kv_pos0) / 64 + 1 - u.j0;
+    u.ntiles = (kmax - p.kv_pos0) / 64 + 1 - u.j0;
     u.slot = u.tix = u.first = -1;
     u.nparts = 1;
     return u;
@@ -1299,6 +1337,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             const float inv = piece ? 1.0f : lt > 0.f ? 1.0f / lt : 0.f;
             if (piece) p.pml[(size_t)u.slot * 128 + row] = make_float2(redmx[row], lt);
             const int nvalid = min(64, p.T - u.t0);
+            if (p.ml_out && !piece && (row & 63) < nvalid)
+                p.ml_out[(size_t)(u.t0 + (row & 63)) * kHeads + 2 * u.g + (row >> 6)] = make_float2(redmx[row], lt);
             // columns 0-127: TMEM -> shared staging (stored coalesced below);
             // TMEM loads go out two at a time (64 columns per wait)
 #pragma unroll 1
@@ -1475,14 +1515,15 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 tc_fence_before();
                 mbar_arrive(s_free);
                 const int tb = p.kv_pos0 + (u.j0 + i) * 64;  // position of the tile's first key
-                const bool edge = (tb + 63 > u.qlo) || (!p.is_global && tb < u.qhi - (kWindow - 1));
+                const bool edge = (tb + 63 > u.qlo) || (!p.is_global && tb < u.qhi - (kWindow - 1)) ||
+                                  (tb + 63 >= p.kv_end);
                 float mx = -INFINITY;
                 if (edge) {
                     const int kb = tb + half * 32;
 #pragma unroll
                     for (int k = 0; k < 32; ++k) {
                         const int kp = kb + k;
-                        if (!(kp <= qpos && kp >= lo_ok)) x[k] = -INFINITY;
+                        if (!(kp <= qpos && kp >= lo_ok && kp < p.kv_end)) x[k] = -INFINITY;
                         mx = fmaxf(mx, x[k]);
                     }
                 } else {

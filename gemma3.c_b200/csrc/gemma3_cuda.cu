@@ -238,6 +238,10 @@ struct gemma3_cuda_ctx {
     float *io = nullptr;
     size_t io_rows = 0;
     unsigned *err = nullptr;
+    // context-parallel prefill: this rank's partial [T][8][256] + [T][8](m, l),
+    // and the gathered partials of all ranks
+    float *pf_part = nullptr, *pf_gather = nullptr;
+    size_t pf_part_cap = 0;
     unsigned *err_host = nullptr;  // page-locked word the kernels set non-zero when they raise a bit of *err
     long long launches = 0;
     int sm_count = 148;
@@ -358,6 +362,8 @@ static void ctx_release(gemma3_cuda_ctx *c) {
     cudaFree(c->emit);
     cudaFree(c->gather);
     cudaFree(c->io);
+    cudaFree(c->pf_part);
+    cudaFree(c->pf_gather);
     cudaFree(c->err);
     for (auto e : c->ev_pool) cudaEventDestroy(e);
     if (c->stream) cudaStreamDestroy(c->stream);
@@ -561,13 +567,30 @@ static int check_launch(gemma3_cuda_ctx *ctx, int n) {
 }
 
 // ------------------------------------------------------------------ prefill
+// One prefill call of T tokens at start_pos.  out [T][2048]; ml null, or
+// [T][8] (m, l) per output row (context-parallel partials).  On a global
+// layer of a context-parallel context this rank holds positions
+// [shard_lo, shard_hi): it appends the call's rows in that range and attends
+// every query to its own keys only (rows of queries with none stay 0 with
+// l = 0), so the ranks' outputs merge by log-sum-exp.
 template <typename KVT>
 static int prefill_impl(gemma3_cuda_ctx *ctx, int layer, int seq, const float *Q, const float *K, const float *V,
-                        int T, int start_pos, float *out) {
+                        int T, int start_pos, float *out, float2 *ml) {
     g3::LayerDev L = layer_dev(ctx, layer);
     const bool global = ctx->layers[layer].is_global;
-    const int kv_pos0 = global ? 0 : std::max(0, start_pos - (kWindow - 1));
-    const int lrows = start_pos + T - kv_pos0;  // key rows the attention sees
+    const bool split = global && ctx->cfg.kv_ranks > 1;
+    const int kv_pos0 = split ? ctx->shard_lo : global ? 0 : std::max(0, start_pos - (kWindow - 1));
+    const int kv_end = split ? std::min(ctx->shard_hi, start_pos + T) : start_pos + T;
+    // queries from qa on can see a key of this context (all of them unless split)
+    const int qa = split ? std::max(start_pos, kv_pos0) : start_pos;
+    const int Tq = kv_end > kv_pos0 ? start_pos + T - qa : 0;
+    if (Tq < T) {
+        // queries before this rank's first key: no output, l = 0
+        const int n0 = T - Tq;
+        CU_TRY(cudaMemsetAsync(out, 0, (size_t)n0 * kHeads * kHeadDim * sizeof(float), ctx->stream));
+        if (ml) CU_TRY(cudaMemsetAsync(ml, 0, (size_t)n0 * kHeads * sizeof(float2), ctx->stream));
+    }
+    const int lrows = std::max(0, kv_end - kv_pos0);  // key rows the attention sees
     if (ctx->st_rows < lrows) {
         cudaFree(ctx->kst);
         cudaFree(ctx->vst);
@@ -578,29 +601,35 @@ static int prefill_impl(gemma3_cuda_ctx *ctx, int layer, int seq, const float *Q
         CU_TRY(cudaMalloc(&ctx->vst, (size_t)kKvHeads * want * kHeadDim * 2));
         ctx->st_rows = want;
     }
-    const int nprefix = start_pos - kv_pos0;
+    const int nprefix = std::min(start_pos, kv_end) - kv_pos0;
     if (nprefix > 0) {
         g3::stage_prefix<KVT><<<dim3(nprefix, 8), 32, 0, ctx->stream>>>(L, seq, kv_pos0, ctx->kst, ctx->vst,
                                                                           ctx->st_rows, ctx->err);
         if (int r = check_launch(ctx, 1)) return r;
     }
     g3::prologue_prefill<KVT><<<T, 512, 0, ctx->stream>>>(Q, K, V, L, ctx->cfg.rmsnorm_eps, seq, T,
-                                                                     start_pos, kv_pos0, ctx->qst, ctx->kst,
+                                                                     start_pos, kv_pos0, kv_end, ctx->qst, ctx->kst,
                                                                      ctx->vst, ctx->st_rows, ctx->err);
     if (int r = check_launch(ctx, 1)) return r;
+    if (Tq == 0) return 0;
 
     CUtensorMap tq, tk, tv;
     const size_t plane = (size_t)ctx->st_rows * kHeadDim;
-    if (int r = make_map(&tq, ctx->qst, T, (size_t)T * kHeadDim, kHeads)) return r;
+    const int q0 = qa - start_pos;  // first query token attended here
+    if (int r = make_map(&tq, ctx->qst + (size_t)q0 * kHeadDim, Tq, (size_t)T * kHeadDim, kHeads)) return r;
     if (int r = make_map4(&tk, ctx->kst, lrows, plane, kKvHeads, 64)) return r;
     if (int r = make_map4(&tv, ctx->vst, lrows, plane, kKvHeads, 64)) return r;
     g3::PrefillParams p;
-    p.out = out;
-    p.T = T;
-    p.start_pos = start_pos;
+    p.out = out + (size_t)q0 * kHeads * kHeadDim;
+    p.ml_out = ml ? ml + (size_t)q0 * kHeads : nullptr;
+    p.T = Tq;
+    p.start_pos = qa;
     p.kv_pos0 = kv_pos0;
+    p.kv_end = kv_end;
     p.is_global = global;
     p.err = ctx->err;
+    T = Tq;
+    start_pos = qa;
     const int nqb = (T + 63) / 64;
     p.nqb = nqb;
     int grid = std::min(nqb * kKvHeads, ctx->sm_count);  // persistent: one CTA per SM
@@ -646,7 +675,7 @@ static int prefill_impl(gemma3_cuda_ctx *ctx, int layer, int seq, const float *Q
         double keys = 0;
         for (int t = 0; t < T; ++t) {
             const int pos = start_pos + t;
-            keys += global ? pos + 1 : std::min(pos + 1, kWindow);
+            keys += split ? std::min(pos + 1, kv_end) - kv_pos0 : global ? pos + 1 : std::min(pos + 1, kWindow);
         }
         prof_end(ctx, 1, e0, keys * 4.0 * kHeadDim * kHeads);
     }
@@ -664,9 +693,34 @@ static int prefill_check(gemma3_cuda_ctx *ctx, int layer, int seq, int T, int st
         return fail(GEMMA3_CUDA_ERR_CONTEXT_OVERFLOW, "positions up to %d exceed max_context %d", start_pos + T - 1,
                     ctx->cfg.max_context);
     if (!ctx->rope_local) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "RoPE tables not uploaded");
-    if (ctx->layers[layer].is_global && ctx->cfg.kv_ranks > 1)
-        return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "prefill into a context-parallel global layer is not supported");
     return 0;
+}
+
+static int prefill_dispatch(gemma3_cuda_ctx *ctx, int layer, int seq, const float *Q, const float *K,
+                            const float *V, int T, int start_pos, float *out, float2 *ml) {
+    if (ctx->cfg.kv_dtype == GEMMA3_CUDA_KV_BF16)
+        return prefill_impl<__nv_bfloat16>(ctx, layer, seq, Q, K, V, T, start_pos, out, ml);
+    return prefill_impl<float>(ctx, layer, seq, Q, K, V, T, start_pos, out, ml);
+}
+
+extern "C" int gemma3_cuda_merge_prefill_partials_dev(gemma3_cuda_ctx *ctx, int n_parts, int T, const float *outs,
+                                                      const float *mls, float *out) {
+    if (!ctx || n_parts <= 0 || T <= 0 || !outs || !mls || !out)
+        return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "bad argument");
+    CU_TRY(cudaSetDevice(ctx->cfg.device));
+    launch_pdl(g3::merge_prefill_partials, dim3(T * kHeads), dim3(256), 0, ctx->stream, outs,
+               (size_t)T * kHeads * kHeadDim, reinterpret_cast<const float2 *>(mls), (size_t)T * kHeads, n_parts,
+               out);
+    return check_launch(ctx, 1);
+}
+
+extern "C" int gemma3_cuda_attn_prefill_partial_dev(gemma3_cuda_ctx *ctx, int layer, int seq, const float *Q,
+                                                    const float *K, const float *V, int T, int start_pos,
+                                                    float *out, float *ml) {
+    if (int r = prefill_check(ctx, layer, seq, T, start_pos)) return r;
+    if (!Q || !K || !V || !out || !ml) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null buffer");
+    CU_TRY(cudaSetDevice(ctx->cfg.device));
+    return prefill_dispatch(ctx, layer, seq, Q, K, V, T, start_pos, out, reinterpret_cast<float2 *>(ml));
 }
 
 extern "C" int gemma3_cuda_attn_prefill_dev(gemma3_cuda_ctx *ctx, int layer, int seq, const float *Q,
@@ -674,9 +728,36 @@ extern "C" int gemma3_cuda_attn_prefill_dev(gemma3_cuda_ctx *ctx, int layer, int
     if (int r = prefill_check(ctx, layer, seq, T, start_pos)) return r;
     if (!Q || !K || !V || !out) return fail(GEMMA3_CUDA_ERR_INVALID_ARG, "null buffer");
     CU_TRY(cudaSetDevice(ctx->cfg.device));
-    if (ctx->cfg.kv_dtype == GEMMA3_CUDA_KV_BF16)
-        return prefill_impl<__nv_bfloat16>(ctx, layer, seq, Q, K, V, T, start_pos, out);
-    return prefill_impl<float>(ctx, layer, seq, Q, K, V, T, start_pos, out);
+    if (!(ctx->layers[layer].is_global && ctx->cfg.kv_ranks > 1))
+        return prefill_dispatch(ctx, layer, seq, Q, K, V, T, start_pos, out, nullptr);
+    // Context-parallel global layer: this rank's partial over its keys, the
+    // ranks' partials all-gathered with NCCL, then the log-sum-exp merge.
+    if (!ctx->comm)
+        return fail(GEMMA3_CUDA_ERR_INVALID_ARG,
+                    "global layer of a context-parallel context needs gemma3_cuda_comm_init (or the partial API)");
+    const int R = ctx->cfg.kv_ranks;
+    const size_t part = (size_t)T * kHeads * (kHeadDim + 2);  // floats: outputs, then (m, l) pairs
+    if (ctx->pf_part_cap < part) {
+        cudaFree(ctx->pf_part);
+        cudaFree(ctx->pf_gather);
+        ctx->pf_part = ctx->pf_gather = nullptr;
+        ctx->pf_part_cap = 0;
+        const size_t cap = (size_t)ctx->cfg.max_prefill * kHeads * (kHeadDim + 2);
+        CU_TRY(cudaMalloc(&ctx->pf_part, cap * sizeof(float)));
+        CU_TRY(cudaMalloc(&ctx->pf_gather, cap * R * sizeof(float)));
+        ctx->pf_part_cap = cap;
+    }
+    float *mine = ctx->pf_part;
+    float2 *ml = reinterpret_cast<float2 *>(mine + (size_t)T * kHeads * kHeadDim);
+    if (int r = prefill_dispatch(ctx, layer, seq, Q, K, V, T, start_pos, mine, ml)) return r;
+    int nr = g_nccl.allGather(mine, ctx->pf_gather, part, kNcclFloat32, ctx->comm, ctx->stream);
+    if (nr != 0)
+        return fail(GEMMA3_CUDA_ERR_GENERATION_FAILED, "ncclAllGather failed: %s",
+                    g_nccl.getErrorString ? g_nccl.getErrorString(nr) : "?");
+    launch_pdl(g3::merge_prefill_partials, dim3(T * kHeads), dim3(256), 0, ctx->stream, (const float *)ctx->pf_gather,
+               part, reinterpret_cast<const float2 *>(ctx->pf_gather + (size_t)T * kHeads * kHeadDim),
+               part / 2, R, out);
+    return check_launch(ctx, 1);
 }
 
 extern "C" int gemma3_cuda_attn_prefill(gemma3_cuda_ctx *ctx, int layer, int seq, const float *Q, const float *K,

@@ -101,6 +101,8 @@ SIGNATURES = {
     "gemma3_cuda_attn_decode_dev": (_I, [_P, _I, _I, _IP, _IP, _P, _P, _P, _P]),
     "gemma3_cuda_attn_decode_partial_dev": (_I, [_P, _I, _I, _IP, _IP, _P, _P, _P, _P]),
     "gemma3_cuda_merge_partials_dev": (_I, [_P, _I, _I, _P, _P]),
+    "gemma3_cuda_attn_prefill_partial_dev": (_I, [_P, _I, _I, _P, _P, _P, _I, _I, _P, _P]),
+    "gemma3_cuda_merge_prefill_partials_dev": (_I, [_P, _I, _I, _P, _P, _P]),
     "gemma3_cuda_comm_unique_id": (_I, [ctypes.c_char_p]),
     "gemma3_cuda_comm_init": (_I, [_P, ctypes.c_char_p]),
     "gemma3_cuda_reset": (_I, [_P]),
@@ -417,6 +419,15 @@ class Context:
         p, pp = _iarr(pos)
         self._chk(self.lib.gemma3_cuda_attn_decode_partial_dev(self.h, layer, len(s), sp, pp, q_ptr, k_ptr, v_ptr,
                                                                partial_ptr))
+
+    def attn_prefill_partial_dev(self, layer, seq, q_ptr, k_ptr, v_ptr, T, start_pos, out_ptr, ml_ptr):
+        """This rank's share of a context-parallel global-layer prefill:
+        out [T][2048] over its keys, ml [T][8][2] (m, l) per row."""
+        self._chk(self.lib.gemma3_cuda_attn_prefill_partial_dev(self.h, layer, seq, q_ptr, k_ptr, v_ptr, T, start_pos,
+                                                                out_ptr, ml_ptr))
+
+    def merge_prefill_partials_dev(self, n_parts, T, outs_ptr, mls_ptr, out_ptr):
+        self._chk(self.lib.gemma3_cuda_merge_prefill_partials_dev(self.h, n_parts, T, outs_ptr, mls_ptr, out_ptr))
 
     def merge_partials_dev(self, n_parts, B, partials_ptr, out_ptr):
         self._chk(self.lib.gemma3_cuda_merge_partials_dev(self.h, n_parts, B, partials_ptr, out_ptr))

@@ -281,6 +281,25 @@ int gemma3_cuda_attn_decode_partial_dev(gemma3_cuda_ctx *ctx, int layer, int B,
 int gemma3_cuda_merge_partials_dev(gemma3_cuda_ctx *ctx, int n_parts, int B,
                                    const float *partials, float *out);
 
+/* Context-parallel prefill of a global layer (the reference fills its global
+ * caches through the same prefill loop, gemma3_transformer.c:641-692).  Each
+ * rank appends the call's cache rows whose positions it holds and attends
+ * every query token to its own keys only.  Step 1 writes, per token and q
+ * head, that output normalised over this rank's keys into out [T][2048] and
+ * its (m, l) -- reference max in the log2 domain and softmax sum -- into
+ * ml [T][8][2] (queries with no key on this rank: zeros, l = 0).  Step 2
+ * merges n_parts such results, outs [n_parts][T][2048] and
+ * mls [n_parts][T][8][2], into out [T][2048].  Device pointers; enqueue only.
+ * gemma3_cuda_attn_prefill[_dev] on such a layer does partial -> NCCL
+ * all-gather -> merge itself when a communicator is attached. */
+int gemma3_cuda_attn_prefill_partial_dev(gemma3_cuda_ctx *ctx, int layer, int seq,
+                                         const float *Q, const float *K,
+                                         const float *V, int T, int start_pos,
+                                         float *out, float *ml);
+int gemma3_cuda_merge_prefill_partials_dev(gemma3_cuda_ctx *ctx, int n_parts, int T,
+                                           const float *outs, const float *mls,
+                                           float *out);
+
 /* NCCL communicator for the context-parallel split (optional).  Rank 0 calls
  * gemma3_cuda_comm_unique_id and ships the 128 opaque bytes to every rank
  * (any host channel); each rank then calls gemma3_cuda_comm_init with its

@@ -228,3 +228,192 @@ def test_split_nccl_2gpu(tmp_path):
     # all-gather path: identical up to float rounding of the merge
     assert res["peer_vs_nccl"] <= 1e-6
     assert res["nccl_again"] <= 1e-6
+
+
+# ---------------------------------------------------------------- prefill
+def _prefill_partial(q, k, v, lo, hi):
+    """numpy: queries q [T][8][256] at positions 0..T-1, keys [lo, hi) of k/v
+    [T][4][256], causal.  Returns (O normalised over those keys [T][8][256],
+    m [T][8] log2-domain reference max, l [T][8]); rows with no key: 0, 0, 0."""
+    T = q.shape[0]
+    O = np.zeros((T, 8, 256))
+    m = np.zeros((T, 8))
+    l = np.zeros((T, 8))
+    for t in range(T):
+        kh = min(hi, t + 1)
+        if kh <= lo:
+            continue
+        for h in range(8):
+            s = (k[lo:kh, h // 2] @ q[t, h]) / 16.0 * LOG2E
+            mm = s.max()
+            p = np.exp2(s - mm)
+            m[t, h], l[t, h] = mm, p.sum()
+            O[t, h] = p @ v[lo:kh, h // 2] / p.sum()
+    return O, m, l
+
+
+def _prefill_merge(Os, ms, ls):
+    """The log-sum-exp merge of merge_prefill_partials: w_r = l_r 2^(m_r - M)."""
+    M = np.where(ls > 0, ms, -np.inf).max(axis=0)
+    w = np.where(ls > 0, ls * np.exp2(ms - np.where(np.isfinite(M), M, 0.0)), 0.0)
+    W = w.sum(0)
+    return (Os * w[..., None]).sum(0) / np.where(W > 0, W, 1.0)[..., None]
+
+
+def _gloo_prefill_worker(rank, world, port, T, result):
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    q = synth.normal(41, (T, 8, 256)).astype(np.float64)
+    k = synth.normal(42, (T, 4, 256)).astype(np.float64)
+    v = synth.normal(43, (T, 4, 256)).astype(np.float64)
+    S = -(-T // world)
+    lo, hi = min(T, rank * S), min(T, rank * S + S)
+    O, m, l = _prefill_partial(q, k, v, lo, hi)
+    mine = torch.from_numpy(np.concatenate([O.reshape(T, -1), m, l], axis=1))
+    gathered = [torch.zeros_like(mine) for _ in range(world)]
+    dist.all_gather(gathered, mine)
+    g = np.stack([x.numpy() for x in gathered])
+    got = _prefill_merge(g[:, :, :2048].reshape(world, T, 8, 256), g[:, :, 2048:2056], g[:, :, 2056:2064])
+    if rank == 0:
+        O1, _, _ = _prefill_partial(q, k, v, 0, T)
+        result.put(float(np.max(np.abs(got - O1))))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,T", [(2, 40), (3, 37)])
+def test_prefill_lse_exchange_gloo(world, T):
+    """The context-parallel prefill's exchange with real collectives (gloo):
+    each rank's outputs over its key shard with (m, l), all-gathered and
+    merged as merge_prefill_partials does, equal attention over all keys."""
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_gloo_prefill_worker, args=(r, world, port, T, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(120)
+        assert p.exitcode == 0
+    assert q.get(timeout=5) < 1e-9
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("R,kv", [(2, 1), (3, 0), (4, 1)])
+def test_prefill_split_emulated_one_gpu(R, kv):
+    """Prefill into a context-parallel global layer, R ranks as R contexts on
+    one GPU: a 1,500-token prompt then a 700-token chunk, each rank's partial
+    through gemma3_cuda_attn_prefill_partial_dev, merged by
+    gemma3_cuda_merge_prefill_partials_dev, against the unsplit context and
+    against the reference's own attention (oracle/_ref); every rank's cache
+    holds exactly its positions' rows."""
+    import torch
+    import gemma3_cuda as gc
+    from oracles import best_oracle, exact_attention
+    layer, ctxlen, T0, T1 = 5, 4096, 1500, 700
+    T = T0 + T1
+    Q, K, V = synth.normal(50, (T, 2048)), synth.normal(51, (T, 1024)), synth.normal(52, (T, 1024))
+    qn, kn = synth.qk_norm_gains(53)
+    rope_l, rope_g = gc.rope_table(ctxlen, 1e4), gc.rope_table(ctxlen, 1e6)
+
+    def make(**kw):
+        c = gc.Context(max_context=ctxlen, max_batch=1, kv_dtype=kv, max_prefill=T0, num_layers=6, **kw)
+        c.upload_rope(rope_l, rope_g)
+        c.set_qk_norm(layer, qn, kn)
+        return c
+
+    ref = make()
+    want = np.concatenate([ref.attn_prefill(layer, 0, Q[:T0], K[:T0], V[:T0], 0),
+                           ref.attn_prefill(layer, 0, Q[T0:], K[T0:], V[T0:], T0)])
+    kref, vref = ref.export_cache(layer, 0)
+    ref.close()
+    oracle = best_oracle()
+    c0 = oracle.new_cache(True, ctxlen)
+    exact = oracle.attn_core_tokens(c0, Q, K, V, qn, kn, oracle.rope_table(ctxlen, 1e6), 0)
+    oracle.free_cache(c0)
+    if kv == gc.KV_BF16:  # the reference's semantics on the rows a BF16 cache holds
+        Qn, Kn = oracle.last_qk
+        exact = exact_attention(Qn, Kn, V, 0, True, "bf16")
+
+    q, k, v = (torch.from_numpy(a).cuda() for a in (Q, K, V))
+    ctxs = [make(kv_rank=r, kv_ranks=R) for r in range(R)]
+    got = []
+    for t0, n in ((0, T0), (T0, T1)):
+        outs = torch.empty(R, n, 2048, device="cuda")
+        mls = torch.empty(R, n, 8, 2, device="cuda")
+        for r, c in enumerate(ctxs):
+            c.attn_prefill_partial_dev(layer, 0, q[t0:].data_ptr(), k[t0:].data_ptr(), v[t0:].data_ptr(), n, t0,
+                                       outs[r].data_ptr(), mls[r].data_ptr())
+            c.synchronize()
+        out = torch.empty(n, 2048, device="cuda")
+        ctxs[0].merge_prefill_partials_dev(R, n, outs.data_ptr(), mls.data_ptr(), out.data_ptr())
+        ctxs[0].synchronize()
+        got.append(out.cpu().numpy())
+    got = np.concatenate(got)
+    assert np.isfinite(got).all()
+    assert rel_err(got, want) <= 2e-3, rel_err(got, want)
+    assert rel_err(got, exact) <= 1e-2, rel_err(got, exact)
+    S = -(-ctxlen // R)
+    for r, c in enumerate(ctxs):
+        lo, hi = min(ctxlen, r * S), min(T, r * S + S)
+        kd, vd = c.export_cache(layer, 0)
+        if hi > lo:
+            assert np.array_equal(vd[:hi - lo], vref[lo:hi]), r
+            assert np.array_equal(kd[:hi - lo], kref[lo:hi]), r
+        c.close()
+
+
+NCCL_PREFILL_CHILD = r'''
+import os, sys, json
+sys.path[:0] = [os.path.join(sys.argv[1], "gemma3.c_b200"), os.path.join(sys.argv[1], "oracle")]
+import numpy as np, torch, torch.distributed as dist
+import gemma3_cuda as gc, synth
+rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+torch.cuda.set_device(rank)
+dist.init_process_group("gloo")
+layer, ctxlen, T = 5, 4096, 3000
+Q, K, V = synth.normal(60, (T, 2048)), synth.normal(61, (T, 1024)), synth.normal(62, (T, 1024))
+qn, kn = synth.qk_norm_gains(63)
+def make(**kw):
+    c = gc.Context(max_context=ctxlen, max_batch=1, kv_dtype=gc.KV_BF16, max_prefill=T, num_layers=6, **kw)
+    c.upload_rope(gc.rope_table(ctxlen, 1e4), gc.rope_table(ctxlen, 1e6)); c.set_qk_norm(layer, qn, kn)
+    return c
+uid = [gc.Context.comm_unique_id() if rank == 0 else None]
+dist.broadcast_object_list(uid, src=0)
+c = make(device=rank, kv_rank=rank, kv_ranks=world)
+c.comm_init(uid[0])
+q, k, v = (torch.from_numpy(a).cuda() for a in (Q, K, V))
+out = torch.empty(T, 2048, device="cuda")
+c.attn_prefill_dev(layer, 0, q.data_ptr(), k.data_ptr(), v.data_ptr(), T, 0, out.data_ptr())
+c.synchronize()
+got = out.cpu().numpy()
+if rank == 0:
+    ref = make(device=0)
+    want = ref.attn_prefill(layer, 0, Q, K, V, 0)
+    print(json.dumps({"err": float(np.max(np.abs(got - want)) / np.sqrt(np.mean(want ** 2)))}))
+    ref.close()
+c.close()
+dist.destroy_process_group()
+'''
+
+
+@pytest.mark.gpu
+def test_prefill_split_nccl_2gpu(tmp_path):
+    """gemma3_cuda_attn_prefill_dev on a context-parallel global layer over
+    two GPUs (partial, NCCL all-gather, merge inside the call) against the
+    unsplit prefill."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    script = tmp_path / "child.py"
+    script.write_text(NCCL_PREFILL_CHILD)
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+                        "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), str(script), ROOT],
+                       capture_output=True, text=True, timeout=300, env=env)
+    assert r.returncode == 0, r.stderr[-3000:]
+    import json
+    res = json.loads([l for l in r.stdout.splitlines() if l.startswith("{")][-1])
+    assert res["err"] <= 2e-3
