@@ -75,9 +75,18 @@ __device__ __forceinline__ void load_head_row(const float *x, int lane, HeadRow 
 }
 
 // RMSNorm with the (1+w) gain when w != null (gemma3_kernels.c:289-304),
-// then RoPE from the table row (gemma3_kernels.c:470-484).
+// then RoPE from the table row (gemma3_kernels.c:470-484).  The gain and
+// table loads are issued first, so their latency overlaps the sum of squares
+// and its warp reduction.
 __device__ __forceinline__ void norm_rope_row(HeadRow &r, const uint16_t *w, float eps, const float *rope_row,
                                               int lane) {
+    const float4 c0 = *reinterpret_cast<const float4 *>(rope_row + 8 * lane);      // (cos,sin) of i = 4l, 4l+1
+    const float4 c1 = *reinterpret_cast<const float4 *>(rope_row + 8 * lane + 4);  // i = 4l+2, 4l+3
+    uint2 wa = make_uint2(0u, 0u), wb = make_uint2(0u, 0u);
+    if (w) {
+        wa = *reinterpret_cast<const uint2 *>(w + 4 * lane);
+        wb = *reinterpret_cast<const uint2 *>(w + 128 + 4 * lane);
+    }
     if (w) {
         float ss = 0.f;
 #pragma unroll
@@ -85,8 +94,6 @@ __device__ __forceinline__ void norm_rope_row(HeadRow &r, const uint16_t *w, flo
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
         const float rr = 1.0f / sqrtf(ss / (float)kHeadDim + eps);
-        const uint2 wa = *reinterpret_cast<const uint2 *>(w + 4 * lane);
-        const uint2 wb = *reinterpret_cast<const uint2 *>(w + 128 + 4 * lane);
         const uint16_t ga[4] = {(uint16_t)(wa.x & 0xffff), (uint16_t)(wa.x >> 16), (uint16_t)(wa.y & 0xffff),
                                 (uint16_t)(wa.y >> 16)};
         const uint16_t gb[4] = {(uint16_t)(wb.x & 0xffff), (uint16_t)(wb.x >> 16), (uint16_t)(wb.y & 0xffff),
@@ -97,8 +104,6 @@ __device__ __forceinline__ void norm_rope_row(HeadRow &r, const uint16_t *w, flo
             r.b[j] = r.b[j] * rr * (1.0f + bf16_bits_to_f(gb[j]));
         }
     }
-    const float4 c0 = *reinterpret_cast<const float4 *>(rope_row + 8 * lane);      // (cos,sin) of i = 4l, 4l+1
-    const float4 c1 = *reinterpret_cast<const float4 *>(rope_row + 8 * lane + 4);  // i = 4l+2, 4l+3
     const float cs[4] = {c0.x, c0.z, c1.x, c1.z}, sn[4] = {c0.y, c0.w, c1.y, c1.w};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -185,6 +190,11 @@ __global__ void __launch_bounds__(512) prologue_prefill(const float *__restrict_
                                                         int T, int start_pos, int kv_pos0, int kv_end,
                                                         __half *__restrict__ qst, __half *__restrict__ kst,
                                                         __half *__restrict__ vst, int st_rows, unsigned *err) {
+    // dependent launch: reads inputs and writes the staging only after the
+    // previous kernel of the stream (the last layer's attention, which reads
+    // the same staging) has completed
+    pdl_launch_dependents();
+    pdl_wait();
     const int t = blockIdx.x, y = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int pos = start_pos + t;
     const float *rope_row = L.rope + (size_t)pos * kHeadDim;
@@ -1154,6 +1164,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // dependent launch: the set-up above overlaps the prologue's tail; global
+    // memory (staging, outputs, tickets) is touched only after it completed
+    pdl_launch_dependents();
+    pdl_wait();
 
     if (warp == kPfWarpTma) {
         // ------------------------------------------------ TMA producer

@@ -607,9 +607,8 @@ static int prefill_impl(gemma3_cuda_ctx *ctx, int layer, int seq, const float *Q
                                                                           ctx->st_rows, ctx->err);
         if (int r = check_launch(ctx, 1)) return r;
     }
-    g3::prologue_prefill<KVT><<<T, 512, 0, ctx->stream>>>(Q, K, V, L, ctx->cfg.rmsnorm_eps, seq, T,
-                                                                     start_pos, kv_pos0, kv_end, ctx->qst, ctx->kst,
-                                                                     ctx->vst, ctx->st_rows, ctx->err);
+    launch_pdl(g3::prologue_prefill<KVT>, dim3(T), dim3(512), 0, ctx->stream, Q, K, V, L, ctx->cfg.rmsnorm_eps, seq,
+               T, start_pos, kv_pos0, kv_end, ctx->qst, ctx->kst, ctx->vst, ctx->st_rows, ctx->err);
     if (int r = check_launch(ctx, 1)) return r;
     if (Tq == 0) return 0;
 
@@ -669,7 +668,7 @@ static int prefill_impl(gemma3_cuda_ctx *ctx, int layer, int seq, const float *Q
     }
     size_t e0;
     prof_begin(ctx, &e0);
-    g3::prefill_fa_sm100<<<grid, g3::kPfThreads, g3::kPfSmem, ctx->stream>>>(tq, tk, tv, p);
+    launch_pdl(g3::prefill_fa_sm100, dim3(grid), dim3(g3::kPfThreads), g3::kPfSmem, ctx->stream, tq, tk, tv, p);
     if (ctx->prof) {
         // algorithmic FLOPs: 2 (QK) + 2 (PV) x 256 x 8 heads per attended key
         double keys = 0;
