@@ -845,6 +845,10 @@ static void plan_decode(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_i
         c = (c + TK - 1) / TK * TK;
         const long long ns = (maxrows + c - 1) / c;
         if (ns > kMaxSplit) continue;
+        // short ranges run the fused form, whose last split merges every
+        // partial of its (sequence, head) alone: 64 partials measured slower
+        // than 32 twice as long (B=1 x 8192 rows: 22.9 vs 18.9 us)
+        if (kTc && c < 2048 && ns > 32) continue;
         const long long last = maxrows - (ns - 1) * c;
         const long long big = (long long)units * (ns - (ns > 1 && 4 * last < c ? 1 : 0));
         const long long waves = std::max<long long>(1, (big + slots - 1) / slots);
