@@ -1512,6 +1512,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             const int ukc = uk++;
             const int qpos = p.start_pos + u.t0 + tr;
             const int lo_ok = p.is_global ? INT_MIN : qpos - (kWindow - 1);
+            const int hi_ok = min(qpos, p.kv_end - 1);   // last key of the row: causal, and staged here
+            const int hi_unit = min(u.qlo, p.kv_end - 1);  // tiles past it hold some masked key
             float m = -INFINITY;  // reference max of the row, log2 domain
             float l = 0.f;        // this half's share of the row sum
             for (int i = 0; i < u.ntiles; ++i, ++gi) {
@@ -1529,15 +1531,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 tc_fence_before();
                 mbar_arrive(s_free);
                 const int tb = p.kv_pos0 + (u.j0 + i) * 64;  // position of the tile's first key
-                const bool edge = (tb + 63 > u.qlo) || (!p.is_global && tb < u.qhi - (kWindow - 1)) ||
-                                  (tb + 63 >= p.kv_end);
+                const bool edge = (tb + 63 > hi_unit) || (!p.is_global && tb < u.qhi - (kWindow - 1));
                 float mx = -INFINITY;
                 if (edge) {
                     const int kb = tb + half * 32;
 #pragma unroll
                     for (int k = 0; k < 32; ++k) {
                         const int kp = kb + k;
-                        if (!(kp <= qpos && kp >= lo_ok && kp < p.kv_end)) x[k] = -INFINITY;
+                        if (!(kp <= hi_ok && kp >= lo_ok)) x[k] = -INFINITY;
                         mx = fmaxf(mx, x[k]);
                     }
                 } else {
