@@ -417,3 +417,85 @@ def test_prefill_split_nccl_2gpu(tmp_path):
     import json
     res = json.loads([l for l in r.stdout.splitlines() if l.startswith("{")][-1])
     assert res["err"] <= 2e-3
+
+
+NCCL_SKIP_CHILD = r'''
+import os, sys, json, time
+sys.path[:0] = [os.path.join(sys.argv[1], "gemma3.c_b200"), os.path.join(sys.argv[1], "oracle")]
+import numpy as np, torch, torch.distributed as dist
+import gemma3_cuda as gc, synth
+rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+torch.cuda.set_device(rank)
+dist.init_process_group("gloo")
+layer, ctxlen, B, pos = 5, 4096, 2, [4095, 1500]
+full_k = [synth.normal(10 + s, (ctxlen, 4, 256)) for s in range(B)]
+full_v = [synth.normal(20 + s, (ctxlen, 4, 256)) for s in range(B)]
+Q, K, V = synth.normal(30, (B, 2048)), synth.normal(31, (B, 1024)), synth.normal(32, (B, 1024))
+def setup(c):
+    c.upload_rope(gc.rope_table(ctxlen, 1e4), gc.rope_table(ctxlen, 1e6))
+    qn, kn = synth.qk_norm_gains(4); c.set_qk_norm(layer, qn, kn)
+    S = -(-ctxlen // c.cfg.kv_ranks); lo = min(ctxlen, c.cfg.kv_rank * S); hi = min(ctxlen, lo + S)
+    for s in range(B):
+        c.import_cache(layer, s, full_k[s][lo:hi], full_v[s][lo:hi])
+uid = [gc.Context.comm_unique_id() if rank == 0 else None]
+dist.broadcast_object_list(uid, src=0)
+c = gc.Context(max_context=ctxlen, max_batch=B, kv_dtype=gc.KV_BF16, device=rank, max_prefill=64,
+               kv_rank=rank, kv_ranks=world)
+setup(c)
+c.comm_init(uid[0])
+c.peer_init()
+q, k, v = (torch.from_numpy(a).cuda() for a in (Q, K, V))
+out = torch.empty(B, 2048, device="cuda")
+def step():
+    c.attn_decode_dev(layer, [0, 1], pos, q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr())
+    c.synchronize()
+    return out.cpu().numpy()
+first = step()
+dist.barrier()
+# rank 1 skips one exchange: rank 0's bounded wait for its flag gives up
+res = {}
+if rank == 0:
+    t0 = time.time()
+    try:
+        step()
+        res["skipped_rc"] = 0
+    except gc.Gemma3CudaError as e:
+        res["skipped_rc"] = e.code
+        res["msg"] = str(e)
+    res["wait_s"] = time.time() - t0
+dist.barrier()
+# recovery: every rank resets (caches, exchange epochs and flags), then the caches are rebuilt
+c.reset()
+setup(c)
+dist.barrier()
+again = step()
+if rank == 0:
+    res["recovered_err"] = float(np.max(np.abs(again - first)) / np.sqrt(np.mean(first ** 2)))
+    print(json.dumps(res))
+c.close()
+dist.destroy_process_group()
+'''
+
+
+@pytest.mark.gpu
+def test_peer_exchange_skipped_rank_recovers_2gpu(tmp_path):
+    """A rank that skips one peer-memory exchange: the other rank's bounded
+    flag wait gives up (GENERATION_FAILED, about 2 s, no trap), both ranks
+    call gemma3_cuda_reset, and the next exchange is correct again."""
+    import torch
+    import gemma3_cuda as gc
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    script = tmp_path / "child.py"
+    script.write_text(NCCL_SKIP_CHILD)
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
+                        "--master-addr", "127.0.0.1", "--master-port", str(_free_port()), str(script), ROOT],
+                       capture_output=True, text=True, timeout=300, env=env)
+    assert r.returncode == 0, r.stderr[-3000:]
+    import json
+    res = json.loads([l for l in r.stdout.splitlines() if l.startswith("{")][-1])
+    assert res["skipped_rc"] == gc.ERR_GENERATION_FAILED, res
+    assert "timed out" in res.get("msg", ""), res
+    assert 1.0 < res["wait_s"] < 30.0, res
+    assert res["recovered_err"] <= 1e-6, res

@@ -378,7 +378,7 @@ def test_prefill_local_balanced_chunked(ropes):
 @pytest.mark.parametrize("layer,B,pos,ctxlen", [
     (0, 64, 1100, 2048),     # local layer, fused kernel, one split per (seq, kv head): in place
     (5, 64, 16384, 16385),   # global layer, long-range form (prologue + split + merge): in place
-    (0, 4, 1100, 2048),      # fused kernel with several splits: inputs staged, output in place
+    (0, 4, 1100, 2048),      # fused kernel with several splits, each reading its q in place
 ])
 def test_decode_pinned_host_buffers(ropes, layer, B, pos, ctxlen):
     """gemma3_cuda_attn_decode with page-locked host buffers (used in place
