@@ -58,7 +58,7 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true", help="skip the configs[1]/[2] figures")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile-case", choices=["decode", "prefill", "proj"],
+    ap.add_argument("--profile-case", choices=["decode", "prefill", "prefill_stack", "proj"],
                     help="tiny workload for ncu captures: 3 launches of the kernel, ~1-2 GB on the device")
     ap.add_argument("--seqs", type=int, default=B_TOTAL,
                     help="override the 64 sequences (small cases for ncu captures only)")
@@ -1060,6 +1060,13 @@ def profile_case(args):
         v = torch.empty(T, 1024, device="cuda")
         for _ in range(2):
             ctx.project_qkv_dev(0, T, x.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr())
+    elif args.profile_case == "prefill_stack":
+        # the configs[2] stack exactly as the bench times it, 2 steps (for a
+        # one-pass launch list: every prologue and attention launch)
+        import types
+        secondary_prefill(types.SimpleNamespace(steps=2, warmup=1), torch, gc, peaks(), 0)
+        print(json.dumps({"profile_case": args.profile_case, "ok": True}))
+        return
     else:
         T = 8192
         ctx = gc.Context(max_context=T, max_batch=1, kv_dtype=gc.KV_BF16, max_prefill=T, num_layers=6)
