@@ -58,7 +58,7 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-secondary", action="store_true", help="skip the configs[1]/[2] figures")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile-case", choices=["decode", "prefill", "prefill_stack", "proj"],
+    ap.add_argument("--profile-case", choices=["decode", "prefill", "prefill_stack", "proj", "model_decode"],
                     help="tiny workload for ncu captures: 3 launches of the kernel, ~1-2 GB on the device")
     ap.add_argument("--seqs", type=int, default=B_TOTAL,
                     help="override the 64 sequences (small cases for ncu captures only)")
@@ -920,6 +920,32 @@ def secondary_model(args, torch, gc, pk, dev):
     return {"workload": "34 Gemma-3-4B blocks on the device (attention, projections, norms, GELU MLP)", **res}
 
 
+def model_decode_case(torch, gc, dev, steps):
+    """`steps` whole-model decode steps (34 blocks, B=64 at 4,096 cached
+    positions, one layer's random BF16 weights on every layer)."""
+    B, CTXD, H, I = 64, 4096, gc.HIDDEN, 10240
+    gen = torch.Generator().manual_seed(11)
+
+    def w(shape, std=0.02):
+        return (torch.randn(*shape, generator=gen) * std).to(torch.bfloat16).view(torch.int16).numpy().view("uint16")
+
+    lw = dict(input_layernorm=w((H,), 0.1), q_proj=w((gc.Q_SIZE, H)), k_proj=w((gc.KV_SIZE, H)),
+              v_proj=w((gc.KV_SIZE, H)), o_proj=w((H, gc.Q_SIZE)), q_norm=w((256,), 0.1), k_norm=w((256,), 0.1),
+              post_attention_layernorm=w((H,), 0.1), gate_proj=w((I, H)), up_proj=w((I, H)), down_proj=w((H, I)),
+              pre_feedforward_layernorm=w((H,), 0.1), post_feedforward_layernorm=w((H,), 0.1))
+    ctx = gc.Context(max_context=CTXD + 1, max_batch=B, kv_dtype=gc.KV_BF16, device=dev, max_prefill=64)
+    ctx.upload_rope(gc.rope_table(CTXD + 1, 10000.0), gc.rope_table(CTXD + 1, 1000000.0))
+    for l in range(N_LAYERS):
+        ctx.set_layer_weights(l, **lw)
+        for s_ in range(B):
+            ctx.fill_cache_random(l, s_, CTXD if gc.is_global_layer(l) else 1024, 1000 + 97 * l + s_)
+    xd = torch.randn(B, H, device=f"cuda:{dev}")
+    for _ in range(steps):
+        ctx.forward_dev(list(range(B)), [CTXD] * B, xd.data_ptr())
+    ctx.synchronize()
+    ctx.close()
+
+
 def secondary_context_parallel(args, dist, torch, gc, pk):
     """B=4 sequences at 131,072 keys, BF16 KV; the 5 global layers'
     KV range is split over the N ranks (partials merged with an NCCL
@@ -1060,6 +1086,12 @@ def profile_case(args):
         v = torch.empty(T, 1024, device="cuda")
         for _ in range(2):
             ctx.project_qkv_dev(0, T, x.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr())
+    elif args.profile_case == "model_decode":
+        # 3 whole-model decode steps (34 blocks, B=64 at 4096 cached positions),
+        # the workload of secondary.model.decode_B64_ctx4096
+        model_decode_case(torch, gc, 0, steps=3)
+        print(json.dumps({"profile_case": args.profile_case, "ok": True}))
+        return
     elif args.profile_case == "prefill_stack":
         # the configs[2] stack exactly as the bench times it, 2 steps (for a
         # one-pass launch list: every prologue and attention launch)
