@@ -935,26 +935,31 @@ __global__ void __launch_bounds__(256) merge_peer_partials(const PeerXchg px, fl
 // Work unit = (block of 64 query tokens, kv head g); the MMA M dimension
 // stacks the two query heads of the group (rows 0-63 head 2g, 64-127 head
 // 2g+1), so each K/V tile feeds both.  One CTA per SM walks the units
-// heaviest first (round-robin over the cost-sorted list), so a unit's Q load
-// and first MMAs overlap the previous unit's last tiles and epilogue.
-// Per key tile of 64 rows:
-//     S[128x64]  = Q[128x256] . K^T   16 MMAs (K=16); A = Q resident in TMEM,
-//                                      B = K tile from shared memory
-//     softmax    warps 0-7: row r is shared by threads r (keys 0-31, O cols
-//                0-127) and r+128 (keys 32-63, O cols 128-255); P goes back
-//                to TMEM as fp16 (two buffers)
-//     O[128x256] += P[128x64] . V     4 MMAs (K=16); A = P from TMEM,
-//                                      B = V tile (MN-major) from shared memory
-// Warp 8 issues the TMA loads, warp 9 the Q copies into TMEM and the S MMAs,
-// warp 10 the PV MMAs (one lane each): each MMA goes to the tensor pipe as
-// soon as its own operands are ready.  Warps 11-14 write each finished unit's
-// O / l out while the softmax warps already work on the next unit.  Operands are fp16 (see
-// prologue_prefill), accumulation fp32.
+// heaviest first (snake rounds over the cost-sorted list).
+// Per key tile of 128 rows:
+//     S[128x128] = Q[128x256] . K^T   16 MMAs (K=16), A = Q and B = K from
+//                                      shared memory into TMEM
+//     softmax    warps 0-7: row r is shared by threads r (keys 0-63, O cols
+//                0-127) and r+128 (keys 64-127, O cols 128-255); S is freed
+//                for the next tile's MMAs as soon as it is in registers; P
+//                goes back to TMEM as fp16 pairs (two buffers), in two chunks
+//     O[128x256] += P[128x128] . V    8 MMAs (K=16); A = P from TMEM, B = V
+//                                      (MN-major) from shared memory
+// A tcgen05.mma of M=128, K=16 costs at least ~64 cycles whatever its N, so
+// S is computed 128 keys at a time (N=128: full rate) rather than 64 (half
+// rate); the PV MMAs (N=256) run at full rate either way.  Warp 8 issues
+// the TMA loads, warp 9 the S MMAs, warp 10 the PV MMAs (one lane each), so
+// each MMA goes to the tensor pipe as soon as its own operands are ready.
+// Warps 11-14 write each finished unit's O / l while the softmax warps work
+// on the next unit.  Operands are fp16 (see prologue_prefill), accumulation
+// fp32.
 //
-// TMEM columns (512): Q 0-127 (fp16 pairs), S 128-191 (fp32), P 192-255
-// (2 x 32, fp16 pairs), O 256-511 (fp32).  (A second S buffer, with P written
-// over its S, was measured: no faster, since S at N=64 and PV already keep the
-// tensor pipe busy for ~1,536 of the ~1,750 cycles of a tile.)
+// TMEM columns (512): S 0-127 (fp32), P 128-191 and 192-255 (fp16 pairs),
+// O 256-511 (fp32).  With P apart from S, S(j+1) runs while the softmax of
+// tile j computes its exponentials; had P been written over S (two S
+// buffers), S(j+2) would wait for PV(j), which waits for the softmax of j,
+// and that chain of S + softmax + PV per two tiles was measured at ~1.2x
+// the period of this layout.
 //
 // Online softmax with a lazily updated reference max: P = 2^(s*c - m) is
 // computed against the row's current reference m, which is only raised
@@ -963,14 +968,18 @@ __global__ void __launch_bounds__(256) merge_peer_partials(const PeerXchg px, fl
 // 256, exact in fp16, and the result is mathematically unchanged.
 //
 // Shared memory (1024-aligned, 128-B swizzle for every MMA operand):
-//     Q staging 64 KB: 4 dim-chunks x [128 rows x 128 B]   (TMA -> tcgen05.cp)
-//     K  3 stages x 32 KB: 4 dim-chunks x [64 keys x 128 B]   (K-major B)
-//     V  2 stages x 32 KB: 4 dim-chunks x [64 keys x 128 B]   (MN-major B)
+//     Q 64 KB: 4 dim-blocks x [128 rows x 128 B], resident for the unit
+//     ring of 5 slots x 32 KB, filled in the order the MMAs consume them:
+//         K half h of a tile: 2 dim-blocks (2h, 2h+1) x [128 keys x 128 B]
+//         V half h of a tile: 4 dim-blocks x [64 keys (64h..) x 128 B]
+//       per unit of n tiles: K0, K1, V0, K2, V1, ..., K(n-1), V(n-2), V(n-1)
+//       (each item two slots), so S(j+1) never waits behind V(j)
 //     barriers, row-max (bf16) / row-sum exchange
-// All barrier phases run on per-CTA counters (tile counter gi, unit counter
-// uk) that continue across units.
+// All mbarrier phases run on per-CTA counters (tile counter gi, unit counter
+// uk, ring position) that continue across units.
 // ------------------------------------------------------------------------
 constexpr int kPfMaxCtas = 160;
+constexpr int kPfTK = 128;  // keys per tile
 struct PrefillParams {
     float *out;       // [T][8][256]
     int T;
@@ -1003,32 +1012,48 @@ struct PrefillParams {
     unsigned *ptickets;  // [kPfMaxCtas], zero between launches
 };
 
+// bar.red.and over `count` threads on named barrier `id`: true iff every
+// participating thread passed pred != 0.
+__device__ __forceinline__ bool named_bar_and(uint32_t id, uint32_t count, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 q, %1, 0;\n\t"
+        "bar.red.and.pred p, %2, %3, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r)
+        : "r"((uint32_t)pred), "r"(id), "r"(count)
+        : "memory");
+    return r != 0;
+}
+
 constexpr int kPfSoftmaxThreads = 256;
 constexpr int kPfThreads = kPfSoftmaxThreads + 96 + 128;  // + producer, two MMA warps, 4 epilogue warps
 constexpr int kPfWarpTma = 8;
-constexpr int kPfWarpMma = 9;  // Q copies + S MMAs; also owns the TMEM allocation
+constexpr int kPfWarpMma = 9;  // S MMAs; also owns the TMEM allocation
 constexpr int kPfWarpPv = 10;  // PV MMAs
 constexpr int kPfWarpEpi = 11; // 11-14: epilogue, one per TMEM lane quadrant
 constexpr float kRescaleLog2 = 8.0f;
 
-
 constexpr uint32_t kPfQBytes = 128 * 256 * 2;
-constexpr uint32_t kPfKVStage = 64 * 256 * 2;
-constexpr int kPfKStages = 3;  // K tiles need ~2 tiles of lead, V tiles get it from the pipeline
-constexpr int kPfVStages = 2;
+constexpr uint32_t kPfSlot = 32768;
+constexpr int kPfSlots = 5;
 constexpr uint32_t kPfOffQ = 0;
-constexpr uint32_t kPfOffK = kPfOffQ + kPfQBytes;
-constexpr uint32_t kPfOffV = kPfOffK + kPfKStages * kPfKVStage;
-constexpr uint32_t kPfOffBar = kPfOffV + kPfVStages * kPfKVStage;
+constexpr uint32_t kPfOffRing = kPfOffQ + kPfQBytes;
+constexpr uint32_t kPfOffBar = kPfOffRing + kPfSlots * kPfSlot;
 constexpr uint32_t kPfOffRed = kPfOffBar + 256;
 // row-max exchange: bf16 [2 parity][2 half][128] (1 KB); row sums fp32 [2 half][128] (1 KB)
 // + the rows' reference maxima for the piece partials, fp32 [128] (512 B)
 constexpr uint32_t kPfSmem = kPfOffRed + 2560;  // 232,192 B: needs a 1024-aligned base (checked)
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemQ = 0;
-constexpr uint32_t kTmemS = 128;
-constexpr uint32_t kTmemP = 192;
+constexpr uint32_t kTmemS = 0;
+constexpr uint32_t kTmemP = 128;  // buffer b at kTmemP + 64 b
 constexpr uint32_t kTmemO = 256;
+
+// Ring item of tile j of a unit of n tiles (items of 2 slots each):
+// K(0) = 0, K(j) = 2j - 1; V(j) = 2j + 2 for j < n - 1, V(n-1) = 2n - 1.
+__device__ __forceinline__ int pf_item_k(int j) { return j == 0 ? 0 : 2 * j - 1; }
+__device__ __forceinline__ int pf_item_v(int j, int n) { return j < n - 1 ? 2 * j + 2 : 2 * n - 1; }
 
 // The unit list: index -> (query block, kv head), costliest blocks first
 // (causal rows grow with the block index; local-layer blocks are equal).
@@ -1056,8 +1081,8 @@ __device__ __forceinline__ PfUnit pf_unit(const PrefillParams &p, int idx) {
     u.qhi = p.start_pos + min(u.t0 + 64, p.T) - 1;
     const int kmin = max(p.kv_pos0, p.is_global ? 0 : u.qlo - (kWindow - 1));
     const int kmax = min(u.qhi, p.kv_end - 1);  // >= kmin: the host launches only queries >= kv_pos0
-    u.j0 = (kmin - p.kv_pos0) / 64;
-    u.ntiles = (kmax - p.kv_pos0) / 64 + 1 - u.j0;
+    u.j0 = (kmin - p.kv_pos0) / kPfTK;
+    u.ntiles = (kmax - p.kv_pos0) / kPfTK + 1 - u.j0;
     u.slot = u.tix = u.first = -1;
     u.nparts = 1;
     return u;
@@ -1095,12 +1120,6 @@ __device__ __forceinline__ bool pf_get(const PrefillParams &p, int nunits, int k
     u.tix = q / p.split;
     return true;
 }
-__device__ __forceinline__ bool pf_next(const PrefillParams &p, int nunits, int k, PfUnit &u) {
-    const int n = pf_count(p, nunits);
-    for (++k; k < n; ++k)
-        if (pf_get(p, nunits, k, u)) return true;
-    return false;
-}
 
 __global__ void __launch_bounds__(kPfThreads, 1)
     prefill_fa_sm100(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -1115,47 +1134,38 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     }
     unsigned char *sm = smem_raw;
     unsigned char *sQ = sm + kPfOffQ;
-    unsigned char *sK = sm + kPfOffK;
-    unsigned char *sV = sm + kPfOffV;
+    unsigned char *sR = sm + kPfOffRing;
     __nv_bfloat16 *redm = reinterpret_cast<__nv_bfloat16 *>(sm + kPfOffRed);  // [2 parity][2 half][128] maxima
     float *reds = reinterpret_cast<float *>(sm + kPfOffRed + 1024);             // [2 half][128] row sums
     float *redmx = reinterpret_cast<float *>(sm + kPfOffRed + 2048);            // [128] row reference maxima
-    volatile int *s_last = reinterpret_cast<volatile int *>(sm + kPfOffBar + 28 * 8);  // epilogue: piece merges
     uint64_t *bars = reinterpret_cast<uint64_t *>(sm + kPfOffBar);
-    uint64_t *q_smem = bars + 0;    // Q tile landed in staging (TMA)
-    uint64_t *k_full = bars + 1;    // [3]
-    uint64_t *k_empty = bars + 4;   // [3]
-    uint64_t *v_full = bars + 7;    // [2]
-    uint64_t *v_empty = bars + 9;   // [2]
-    uint64_t *s_full = bars + 11;
-    uint64_t *s_free = bars + 12;
-    uint64_t *p_full = bars + 13;   // [2], 256 arrivals
-    uint64_t *p_empty = bars + 15;  // [2]
-    uint64_t *mma_done = bars + 17;
-    uint64_t *mma_done_pv = bars + 18;
-    uint64_t *q_tmem = bars + 19;   // Q copied into TMEM; staging free
-    uint64_t *red_bar = bars + 20;  // [2], 256 arrivals
+    uint64_t *q_full = bars + 0;    // Q tile landed (TMA)
+    uint64_t *q_empty = bars + 1;   // the unit's S MMAs have read Q
+    uint64_t *r_full = bars + 2;    // [5] ring slot landed
+    uint64_t *r_empty = bars + 7;   // [5] ring slot read by its MMAs
+    uint64_t *s_full = bars + 12;   // S written
+    uint64_t *s_free = bars + 13;   // 256 arrivals: the softmax has read S
+    uint64_t *p_empty = bars + 14;  // [2] PV done: P buffer read, O updated
+    uint64_t *mma_done = bars + 16;
+    uint64_t *mma_done_pv = bars + 17;
+    uint64_t *p_full = bars + 18;   // [2 buffers][2 chunks], 256 arrivals: P chunk written over S
     uint64_t *fin_bar = bars + 22;  // 256 arrivals, once per unit
     uint64_t *o_free = bars + 23;   // 128 arrivals: the epilogue warps have read O
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 24);
     volatile int *s_abort = reinterpret_cast<volatile int *>(bars + 25);
-    uint64_t *epi_bar = bars + 26;   // 128 arrivals: epilogue-internal steps (3 per unit)
-    uint64_t *epi_done = bars + 27;  // 128 arrivals: epilogue done with the Q staging
+    uint64_t *epi_bar = bars + 26;  // 128 arrivals: epilogue-internal steps
+    volatile int *s_last = reinterpret_cast<volatile int *>(bars + 28);  // epilogue: piece merges
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nunits = p.nqb * kKvHeads;
 
     if (threadIdx.x == 0) {
         for (int i = 0; i < 24; ++i) mbar_init(&bars[i], 1);
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&p_full[b], kPfSoftmaxThreads);
-            mbar_init(&red_bar[b], kPfSoftmaxThreads);
-        }
-        mbar_init(fin_bar, kPfSoftmaxThreads);
+        for (int b = 0; b < 4; ++b) mbar_init(&p_full[b], kPfSoftmaxThreads);
         mbar_init(s_free, kPfSoftmaxThreads);
+        mbar_init(fin_bar, kPfSoftmaxThreads);
         mbar_init(o_free, 128);
         mbar_init(epi_bar, 128);
-        mbar_init(epi_done, 128);
         *s_abort = 0;
         fence_mbar_init();
     }
@@ -1169,103 +1179,105 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     pdl_launch_dependents();
     pdl_wait();
 
+    const int nitems = pf_count(p, nunits);
     if (warp == kPfWarpTma) {
         // ------------------------------------------------ TMA producer
         if (lane == 0) {
             prefetch_tmap(&tmQ);
             prefetch_tmap(&tmK);
             prefetch_tmap(&tmV);
-            // Q of unit uk is loaded one unit ahead: right after the first
-            // tile of unit uk-1 (once that unit's Q has left the staging).
-            auto load_q = [&](const PfUnit &u) {
-                mbar_expect_tx(q_smem, kPfQBytes);
-                for (int c = 0; c < 4; ++c)
-                    for (int hh = 0; hh < 2; ++hh)
-                        tma_load_3d(sQ + c * 16384 + hh * 8192, &tmQ, 64 * c, u.t0, 2 * u.g + hh, q_smem);
-            };
-            int gi = 0, uk = 0;
-            const int nitems = pf_count(p, nunits);
-            {
-                PfUnit f;
-                if (pf_next(p, nunits, -1, f)) load_q(f);
-            }
+            int uk = 0, rb = 0;  // unit counter, ring position of the unit's first slot
+            int last_pos[kPfSlots];  // last ring position issued per slot (for the abort drain)
+            int q_issued = 0;        // Q copies issued
+#pragma unroll
+            for (int s = 0; s < kPfSlots; ++s) last_pos[s] = -1;
             for (int k = 0; k < nitems && !*s_abort; ++k) {
-                PfUnit u, un;
+                PfUnit u;
                 if (!pf_get(p, nunits, k, u)) continue;
                 const int ukc = uk++;
-                const bool has_nxt = pf_next(p, nunits, k, un);
-                bool q_pending = has_nxt;  // the next item's Q is still to be loaded
-                for (int i = 0; i < u.ntiles; ++i, ++gi) {
-                    const int sk = gi % kPfKStages, nk = gi / kPfKStages;
-                    const int sv = gi % kPfVStages, nv = gi / kPfVStages;
-                    const int krow = (u.j0 + i) * 64;
-                    if (nk >= 1 && !mbar_wait(&k_empty[sk], (nk - 1) & 1, p.err)) { *s_abort = 1; break; }
-                    // one 32 KB box per stage: [4 dim-blocks][64 keys][128 B] (a TMA
-                    // instruction has a near-fixed issue cost, so fewer larger boxes
-                    // stream faster than one box per 64-dim block)
-                    mbar_expect_tx(&k_full[sk], kPfKVStage);
-                    tma_load_4d(sK + sk * kPfKVStage, &tmK, 0, krow, 0, u.g, &k_full[sk]);
-                    if (nv >= 1 && !mbar_wait(&v_empty[sv], (nv - 1) & 1, p.err)) { *s_abort = 1; break; }
-                    mbar_expect_tx(&v_full[sv], kPfKVStage);
-                    tma_load_4d(sV + sv * kPfKVStage, &tmV, 0, krow, 0, u.g, &v_full[sv]);
-                    // prefetch the next unit's Q into the staging once this
-                    // unit's Q is in TMEM and the previous unit's epilogue
-                    // has stopped using the staging for its output.  Polled
-                    // from the third tile on, so the K/V stream never waits
-                    // for the epilogue; only the unit's last tile blocks.
-                    if (q_pending && i >= min(2, u.ntiles - 1)) {
-                        if (i == u.ntiles - 1) {
-                            if (!mbar_wait(q_tmem, ukc & 1, p.err)) { *s_abort = 1; break; }
-                            if (ukc >= 1 && !mbar_wait(epi_done, (ukc - 1) & 1, p.err)) { *s_abort = 1; break; }
-                            q_pending = false;
-                        } else {
-                            q_pending = !(mbar_try_wait(q_tmem, ukc & 1) &&
-                                          (ukc < 1 || mbar_try_wait(epi_done, (ukc - 1) & 1)));
-                        }
-                        if (!q_pending) load_q(un);
+                const int n = u.ntiles;
+                bool ok = true;
+                for (int t = 0; ok && t < 2 * n; ++t) {
+                    if (t == 1) {
+                        // Q of this unit (after its first K tile, whose copy then
+                        // overlaps the wait), once the previous unit's S MMAs
+                        // have read theirs
+                        if (ukc >= 1 && !mbar_wait(q_empty, (ukc - 1) & 1, p.err)) { ok = false; break; }
+                        mbar_expect_tx(q_full, kPfQBytes);
+                        for (int c = 0; c < 4; ++c)
+                            for (int hh = 0; hh < 2; ++hh)
+                                tma_load_3d(sQ + c * 16384 + hh * 8192, &tmQ, 64 * c, u.t0, 2 * u.g + hh, q_full);
+                        q_issued = ukc + 1;
+                    }
+                    const bool isv = t == 2 * n - 1 || (t > 0 && !(t & 1));
+                    const int j = t == 2 * n - 1 ? n - 1 : isv ? (t - 2) / 2 : (t + 1) / 2;
+                    const int krow = (u.j0 + j) * kPfTK;
+                    for (int h = 0; h < 2; ++h) {
+                        const int pos = rb + 2 * t + h, s = pos % kPfSlots, ph = pos / kPfSlots;
+                        if (ph >= 1 && !mbar_wait(&r_empty[s], (ph - 1) & 1, p.err)) { ok = false; break; }
+                        mbar_expect_tx(&r_full[s], kPfSlot);
+                        if (isv)
+                            tma_load_4d(sR + s * kPfSlot, &tmV, 0, krow + 64 * h, 0, u.g, &r_full[s]);
+                        else
+                            tma_load_4d(sR + s * kPfSlot, &tmK, 0, krow, 2 * h, u.g, &r_full[s]);
+                        last_pos[s] = pos;
                     }
                 }
+                if (!ok) { *s_abort = 1; break; }
+                rb += 4 * n;
+            }
+            // wait (bounded) for the copies in flight before the CTA exits
+            if (*s_abort) {
+                if (q_issued >= 1) mbar_wait(q_full, (q_issued - 1) & 1, nullptr);
+                for (int s = 0; s < kPfSlots; ++s)
+                    if (last_pos[s] >= 0) mbar_wait(&r_full[s], (last_pos[s] / kPfSlots) & 1, nullptr);
             }
         }
     } else if (warp == kPfWarpMma) {
-        // ------------------------------------------------ Q -> TMEM, S = Q.K^T
+        // ------------------------------------------------ S = Q.K^T
         if (lane == 0) {
-            constexpr uint32_t idS = idesc_f16_f32(128, 64, 0, 0);
+            constexpr uint32_t idS = idesc_f16_f32(128, kPfTK, 0, 0);
             // Descriptors are built once; per MMA only the start-address field
             // (bits 0-13, address >> 4, no carry for addresses < 256 KB)
-            // advances, by compile-time constants.
+            // advances.
             const uint64_t dQ = smem_desc_sw128(smem_u32(sQ), 16, 1024);
-            const uint64_t dK0 = smem_desc_sw128(smem_u32(sK), 16, 1024);
+            const uint64_t dR = smem_desc_sw128(smem_u32(sR), 16, 1024);
             bool ok = true;
-            int gi = 0, uk = 0;
-            const int nitems = pf_count(p, nunits);
+            int gi = 0, uk = 0, rb = 0;
             for (int k = 0; ok && k < nitems; ++k) {
                 PfUnit u;
                 if (!pf_get(p, nunits, k, u)) continue;
                 const int ukc = uk++;
-                if (*s_abort || !mbar_wait(q_smem, ukc & 1, p.err)) { ok = false; break; }
-                tc_fence_after();
-                // Issued after the previous unit's S MMAs: tcgen05 operations
-                // of one thread execute in order, so they have read the old Q.
-#pragma unroll
-                for (int kk = 0; kk < 16; ++kk)
-                    tc_cp_128x256b(tmem + kTmemQ + kk * 8, dQ + (uint64_t)(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4));
-                tc_commit(q_tmem);
-                for (int i = 0; i < u.ntiles; ++i, ++gi) {
+                const int n = u.ntiles;
+                if (*s_abort || !mbar_wait(q_full, ukc & 1, p.err)) { ok = false; break; }
+                for (int i = 0; i < n; ++i, ++gi) {
                     if (*s_abort) { ok = false; break; }
-                    const int s = gi % kPfKStages;
-                    if (!mbar_wait(&k_full[s], (gi / kPfKStages) & 1, p.err)) { ok = false; break; }
-                    // the single S buffer is free once the softmax has read the last one
+                    const int pos0 = rb + 2 * pf_item_k(i);
+                    const int s0 = pos0 % kPfSlots, s1 = (pos0 + 1) % kPfSlots;
+                    if (!mbar_wait(&r_full[s0], (pos0 / kPfSlots) & 1, p.err) ||
+                        !mbar_wait(&r_full[s1], ((pos0 + 1) / kPfSlots) & 1, p.err)) {
+                        ok = false;
+                        break;
+                    }
+                    // S is free once the softmax has loaded the previous one
                     if (gi >= 1 && !mbar_wait(s_free, (gi - 1) & 1, p.err)) { ok = false; break; }
                     tc_fence_after();
-                    const uint64_t dK = dK0 + (uint64_t)((s * kPfKVStage) >> 4);
+                    const uint32_t dS = tmem + kTmemS;
 #pragma unroll
-                    for (int kk = 0; kk < 16; ++kk)
-                        tc_mma_f16_ts(tmem + kTmemS, tmem + kTmemQ + kk * 8,
-                                      dK + (uint64_t)(((kk >> 2) * 8192 + (kk & 3) * 32) >> 4), idS, kk > 0 ? 1u : 0u);
-                    tc_commit(&k_empty[s]);
+                    for (int kk = 0; kk < 16; ++kk) {
+                        const int s = kk < 8 ? s0 : s1;
+                        const uint64_t a = dQ + (uint64_t)(((kk >> 2) * 16384 + (kk & 3) * 32) >> 4);
+                        const uint64_t b =
+                            dR + (uint64_t)((s * kPfSlot + ((kk >> 2) & 1) * 16384 + (kk & 3) * 32) >> 4);
+                        tc_mma_f16(dS, a, b, idS, kk > 0 ? 1u : 0u);
+                    }
+                    tc_commit(&r_empty[s0]);
+                    tc_commit(&r_empty[s1]);
                     tc_commit(s_full);
                 }
+                if (!ok) break;
+                tc_commit(q_empty);
+                rb += 4 * n;
             }
             if (!ok) *s_abort = 1;
             // Drain: every tcgen05 operation this thread issued has completed.
@@ -1276,31 +1288,49 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         // ------------------------------------------------ O += P.V
         if (lane == 0) {
             constexpr uint32_t idO = idesc_f16_f32(128, 256, 0, 1);
-            const uint64_t dV0 = smem_desc_sw128(smem_u32(sV), 8192, 1024);
+            const uint64_t dR = smem_desc_sw128(smem_u32(sR), 8192, 1024);
             bool ok = true;
-            int gi = 0, uk = 0;
-            const int nitems = pf_count(p, nunits);
+            int gi = 0, uk = 0, rb = 0;
             for (int k = 0; ok && k < nitems; ++k) {
                 PfUnit u;
                 if (!pf_get(p, nunits, k, u)) continue;
                 const int ukc = uk++;
-                for (int i = 0; i < u.ntiles; ++i, ++gi) {
+                const int n = u.ntiles;
+                for (int i = 0; i < n; ++i, ++gi) {
                     if (*s_abort) { ok = false; break; }
-                    const int su = gi % kPfVStages, pb = gi & 1;
-                    if (!mbar_wait(&p_full[pb], (gi >> 1) & 1, p.err)) { ok = false; break; }
-                    if (!mbar_wait(&v_full[su], (gi / kPfVStages) & 1, p.err)) { ok = false; break; }
+                    const int b = gi & 1;
+                    const int pos0 = rb + 2 * pf_item_v(i, n);
+                    const int s0 = pos0 % kPfSlots, s1 = (pos0 + 1) % kPfSlots;
+                    if (!mbar_wait(&r_full[s0], (pos0 / kPfSlots) & 1, p.err) ||
+                        !mbar_wait(&r_full[s1], ((pos0 + 1) / kPfSlots) & 1, p.err)) {
+                        ok = false;
+                        break;
+                    }
                     // the first PV of a unit overwrites O: the previous unit's
                     // epilogue must have read it
                     if (i == 0 && ukc >= 1 && !mbar_wait(o_free, (ukc - 1) & 1, p.err)) { ok = false; break; }
-                    tc_fence_after();
-                    const uint64_t dV = dV0 + (uint64_t)((su * kPfKVStage) >> 4);
+                    const uint32_t aP = tmem + kTmemP + b * 64;
+                    // P arrives in two chunks (keys 32c..32c+31 of each half):
+                    // chunk c feeds the MMAs of keys 16kk.. for kk = 2c, 2c+1
+                    // (V half 0) and 4+2c, 5+2c (V half 1)
+                    for (int c = 0; c < 2 && ok; ++c) {
+                        if (!mbar_wait(&p_full[2 * b + c], (gi >> 1) & 1, p.err)) { ok = false; break; }
+                        tc_fence_after();
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        tc_mma_f16_ts(tmem + kTmemO, tmem + kTmemP + pb * 32 + kk * 8, dV + (uint64_t)((kk * 2048) >> 4),
-                                      idO, (i > 0 || kk > 0) ? 1u : 0u);
-                    tc_commit(&v_empty[su]);
-                    tc_commit(&p_empty[pb]);
+                        for (int q = 0; q < 4; ++q) {
+                            const int kk = (q >> 1) * 4 + 2 * c + (q & 1);
+                            const int s = kk < 4 ? s0 : s1;
+                            tc_mma_f16_ts(tmem + kTmemO, aP + kk * 8,
+                                          dR + (uint64_t)((s * kPfSlot + (kk & 3) * 2048) >> 4), idO,
+                                          (i > 0 || c > 0 || q > 0) ? 1u : 0u);
+                        }
+                    }
+                    if (!ok) break;
+                    tc_commit(&r_empty[s0]);
+                    tc_commit(&r_empty[s1]);
+                    tc_commit(&p_empty[b]);
                 }
+                rb += 4 * n;
             }
             if (!ok) *s_abort = 1;
             tc_commit(mma_done_pv);
@@ -1309,17 +1339,17 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     } else if (warp >= kPfWarpEpi) {
         // ------------------------------------------------ epilogue warps
         // O / (l_half0 + l_half1) -> out[t][2g+hh][:], one warp per TMEM lane
-        // quadrant, thread = row.  Columns 0-127 go through the Q staging
-        // buffer (free once the next unit's Q is in TMEM) for coalesced
-        // stores; columns 128-255 go from registers straight to the row's
-        // contiguous 512 bytes, and O is released to the next unit right after
-        // that last TMEM read, before the staged half is stored.  Staging:
-        // [128 rows][32 16-byte chunks], chunk c of row r at slot c ^ (r & 7).
+        // quadrant, thread = row.  Per 32-column chunk, each group of 8
+        // lanes transposes its 8 rows x 8 float4 blocks with three xor-
+        // shuffle stages, so that a store instruction writes 4 rows x 128
+        // contiguous bytes (4 L1 wavefronts) instead of 32 rows x 16 bytes
+        // (32 wavefronts): all CTAs of a local layer finish their units
+        // together, and the scattered form kept the LSU busy for ~8k cycles
+        // per unit, stalling the softmax warps' TMEM loads.  O is released
+        // to the next unit's PV right after the last TMEM read.
         const int quad = warp & 3;
         const int row = quad * 32 + lane;
-        const int et = threadIdx.x - kPfWarpEpi * 32;  // 0..127
         const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16);
-        float4 *stage = reinterpret_cast<float4 *>(sQ);
         bool ok = true;
         int gi = 0, uk = 0, eph = 0;
         auto epi_sync = [&]() {
@@ -1328,23 +1358,18 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             ++eph;
             return __all_sync(0xffffffffu, w);
         };
-        const int nitems = pf_count(p, nunits);
         for (int k = 0; ok && k < nitems; ++k) {
-            PfUnit u, un;
+            PfUnit u;
             if (!pf_get(p, nunits, k, u)) continue;
             const int ukc = uk++;
             gi += u.ntiles;
             const int gl = gi - 1;  // the unit's last tile
-            const bool more = pf_next(p, nunits, k, un);
-            // the staging still holds the next unit's Q until it is in TMEM
             if (!__all_sync(0xffffffffu, !*s_abort && mbar_wait(fin_bar, ukc & 1, p.err) &&
-                                             mbar_wait(&p_empty[gl & 1], (gl >> 1) & 1, p.err) &&
-                                             (!more || mbar_wait(q_tmem, (ukc + 1) & 1, p.err)))) {
+                                             mbar_wait(&p_empty[gl & 1], (gl >> 1) & 1, p.err))) {
                 ok = false;
                 break;
             }
             tc_fence_after();
-            fence_proxy_async_smem();  // the staging was last touched by TMA / tcgen05.cp
             const float lt = reds[row] + reds[128 + row];
             // a piece of a cut unit leaves O unnormalised, with (m, l) beside it
             const bool piece = u.slot >= 0;
@@ -1353,74 +1378,54 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             const int nvalid = min(64, p.T - u.t0);
             if (p.ml_out && !piece && (row & 63) < nvalid)
                 p.ml_out[(size_t)(u.t0 + (row & 63)) * kHeads + 2 * u.g + (row >> 6)] = make_float2(redmx[row], lt);
-            // columns 0-127: TMEM -> shared staging (stored coalesced below);
-            // TMEM loads go out two at a time (64 columns per wait)
+            const int q8 = lane & 7, r8 = quad * 32 + (lane & ~7);  // group's first row
 #pragma unroll 1
-            for (int cc = 0; cc < 4; cc += 2) {
-                float o[2][32];
-                tmem_ld32(lane_base + kTmemO + cc * 32, o[0]);
-                tmem_ld32(lane_base + kTmemO + cc * 32 + 32, o[1]);
+            for (int cc = 0; cc < 8; ++cc) {
+                float o[32];
+                tmem_ld32(lane_base + kTmemO + cc * 32, o);
                 tc_wait_ld();
+                if (cc == 7) {
+                    // all of O read from TMEM: the next unit's PV may overwrite it
+                    tc_fence_before();
+                    mbar_arrive(o_free);
+                }
+                float4 v[8];
 #pragma unroll
-                for (int h = 0; h < 2; ++h)
+                for (int k = 0; k < 8; ++k)
+                    v[k] = make_float4(o[4 * k] * inv, o[4 * k + 1] * inv, o[4 * k + 2] * inv, o[4 * k + 3] * inv);
+                // lane q8 of the group: v[k] = block k of row r8 + q8 -> block q8 of row r8 + k
 #pragma unroll
-                    for (int k4 = 0; k4 < 8; ++k4) {
-                        const int c = (cc + h) * 8 + k4;
-                        stage[row * 32 + (c ^ (row & 7))] = make_float4(o[h][4 * k4] * inv, o[h][4 * k4 + 1] * inv,
-                                                                        o[h][4 * k4 + 2] * inv, o[h][4 * k4 + 3] * inv);
-                    }
-            }
-            // columns 128-255: TMEM -> registers -> this row's 512 contiguous
-            // bytes; O is released to the next unit's PV right after the last
-            // TMEM read, before any store of this unit has to drain
-            {
-                float *rdst = piece ? p.pscratch + ((size_t)u.slot * 128 + row) * kHeadDim
-                                    : p.out + ((size_t)(u.t0 + (row & 63)) * kHeads + 2 * u.g + (row >> 6)) * kHeadDim;
-                const bool rok = piece || (row & 63) < nvalid;
-#pragma unroll 1
-                for (int cc = 0; cc < 4; cc += 2) {
-                    float o[2][32];
-                    tmem_ld32(lane_base + kTmemO + 128 + cc * 32, o[0]);
-                    tmem_ld32(lane_base + kTmemO + 128 + cc * 32 + 32, o[1]);
-                    tc_wait_ld();
-                    if (cc == 2) {
-                        // all of O read from TMEM: the next unit's PV may overwrite it
-                        tc_fence_before();
-                        mbar_arrive(o_free);
-                    }
-                    if (rok) {
-                        float4 *d4 = reinterpret_cast<float4 *>(rdst + 128 + cc * 32);
+                for (int m = 4; m >= 1; m >>= 1) {
+                    const bool up = (q8 & m) != 0;
 #pragma unroll
-                        for (int k4 = 0; k4 < 16; ++k4) {
-                            const float *src = o[k4 >> 3] + 4 * (k4 & 7);
-                            d4[k4] = make_float4(src[0] * inv, src[1] * inv, src[2] * inv, src[3] * inv);
-                        }
+                    for (int k0 = 0; k0 < 8; ++k0) {
+                        if (k0 & m) continue;
+                        float4 &a = v[k0], &b = v[k0 | m];
+                        const float4 snd = up ? a : b;
+                        float4 rcv;
+                        rcv.x = __shfl_xor_sync(0xffffffffu, snd.x, m);
+                        rcv.y = __shfl_xor_sync(0xffffffffu, snd.y, m);
+                        rcv.z = __shfl_xor_sync(0xffffffffu, snd.z, m);
+                        rcv.w = __shfl_xor_sync(0xffffffffu, snd.w, m);
+                        if (up) a = rcv; else b = rcv;
                     }
                 }
-            }
-            if (!epi_sync()) { ok = false; break; }
-            // 128 threads store 128 rows x 512 B of the staging; a warp covers
-            // one row's 512 contiguous bytes
-            for (int f = et; f < 128 * 32; f += 128) {
-                const int r = f >> 5, c = f & 31;
-                if (piece) {
-                    float *dst = p.pscratch + ((size_t)u.slot * 128 + r) * kHeadDim + c * 4;
-                    *reinterpret_cast<float4 *>(dst) = stage[r * 32 + (c ^ (r & 7))];
-                } else if ((r & 63) < nvalid) {
-                    float *dst = p.out + ((size_t)(u.t0 + (r & 63)) * kHeads + 2 * u.g + (r >> 6)) * kHeadDim + c * 4;
-                    *reinterpret_cast<float4 *>(dst) = stage[r * 32 + (c ^ (r & 7))];
+#pragma unroll
+                for (int k = 0; k < 8; ++k) {
+                    const int r = r8 + k;
+                    if (!piece && (r & 63) >= nvalid) continue;
+                    float *rd = piece ? p.pscratch + ((size_t)u.slot * 128 + r) * kHeadDim
+                                      : p.out + ((size_t)(u.t0 + (r & 63)) * kHeads + 2 * u.g + (r >> 6)) * kHeadDim;
+                    *reinterpret_cast<float4 *>(rd + cc * 32 + 4 * q8) = v[k];
                 }
             }
-            if (!ok) break;
-            fence_proxy_async_smem();  // our staging reads before the next Q's TMA write
-            mbar_arrive(epi_done);     // the staging is free for the next Q
             if (piece) {
-                // Both pieces of the cut unit publish; the second to arrive
+                // Every piece of the cut unit publishes; the last to arrive
                 // merges them (the CTA's MMA / softmax warps meanwhile run
-                // the next item).  No waiting on the other CTA.
+                // the next item).  No waiting on the other CTAs.
                 __threadfence();
                 if (!epi_sync()) { ok = false; break; }
-                if (et == 0) {
+                if (threadIdx.x == kPfWarpEpi * 32) {
                     const unsigned old = atomicAdd(&p.ptickets[u.tix], 1u);
                     *s_last = old == (unsigned)(u.nparts - 1) ? 1 : 0;
                     if (*s_last) p.ptickets[u.tix] = 0u;  // ready for the next launch
@@ -1499,13 +1504,19 @@ __global__ void __launch_bounds__(kPfThreads, 1)
         if (!ok) *s_abort = 1;
     } else {
         // ------------------------------------------------ softmax warps 0-7
+        // Warps w and w + 4 share TMEM lanes 32 (w % 4) .. + 31: thread r of
+        // one and thread r of the other hold the two halves of a row, and
+        // exchange the row maximum through shared memory behind a 64-thread
+        // named barrier (id 1 + w % 4).  Every exit from the tile loop goes
+        // through that barrier (bar.red.and of both warps' status), so a
+        // failed wait in one warp never leaves its partner at the barrier.
         const int row = threadIdx.x & 127;  // TMEM lane == S/O row
-        const int half = threadIdx.x >> 7;  // keys [32*half, +32), O cols [128*half, +128)
+        const int half = threadIdx.x >> 7;  // keys [64*half, +64), O cols [128*half, +128)
         const int tr = row & 63;
+        const uint32_t pair_bar = 1 + (warp & 3);
         const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
-        bool ok = true;
+        bool ok = true, fail = false;
         int gi = 0, uk = 0;
-        const int nitems = pf_count(p, nunits);
         for (int k = 0; ok && k < nitems; ++k) {
             PfUnit u;
             if (!pf_get(p, nunits, k, u)) continue;
@@ -1517,79 +1528,70 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             float m = -INFINITY;  // reference max of the row, log2 domain
             float l = 0.f;        // this half's share of the row sum
             for (int i = 0; i < u.ntiles; ++i, ++gi) {
-                const int pb = gi & 1;
+                const int b = gi & 1;
+                const uint32_t pbuf = lane_base + kTmemP + b * 64;
                 // every wait's outcome is made warp-uniform so the warp-collective
                 // tcgen05 and vote instructions below never run diverged
-                if (!__all_sync(0xffffffffu, !*s_abort && mbar_wait(s_full, gi & 1, p.err))) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                float x[32];
-                tmem_ld32(lane_base + kTmemS + half * 32, x);
-                tc_wait_ld();
-                tc_fence_before();
-                mbar_arrive(s_free);
-                const int tb = p.kv_pos0 + (u.j0 + i) * 64;  // position of the tile's first key
-                const bool edge = (tb + 63 > hi_unit) || (!p.is_global && tb < u.qhi - (kWindow - 1));
+                const bool w = !fail && __all_sync(0xffffffffu, !*s_abort && mbar_wait(s_full, gi & 1, p.err));
+                float xa[32], xb[32];  // keys 64*half + 0..31, + 32..63
                 float mx = -INFINITY;
-                if (edge) {
-                    const int kb = tb + half * 32;
+                if (w) {
+                    tc_fence_after();
+                    tmem_ld32(lane_base + kTmemS + half * 64, xa);
+                    tmem_ld32(lane_base + kTmemS + half * 64 + 32, xb);
+                    tc_wait_ld();
+                    tc_fence_before();
+                    mbar_arrive(s_free);  // the next tile's S MMAs may overwrite it
+                    const int tb = p.kv_pos0 + (u.j0 + i) * kPfTK;  // position of the tile's first key
+                    const bool edge = (tb + kPfTK - 1 > hi_unit) || (!p.is_global && tb < u.qhi - (kWindow - 1));
+                    if (edge) {
+                        // valid keys of the row among this half's 64: one bit each
+                        const int kb = tb + half * 64;
+                        const int lo = lo_ok <= kb ? 0 : min(lo_ok - kb, 64);
+                        const int hi = hi_ok >= kb + 63 ? 63 : hi_ok - kb;  // may be < 0
+                        const uint64_t vm = (lo > hi) ? 0ull : ((~0ull >> (63 - hi)) & (~0ull << lo));
+                        const uint32_t ma = (uint32_t)vm, mb = (uint32_t)(vm >> 32);
 #pragma unroll
-                    for (int k = 0; k < 32; ++k) {
-                        const int kp = kb + k;
-                        if (!(kp <= hi_ok && kp >= lo_ok)) x[k] = -INFINITY;
-                        mx = fmaxf(mx, x[k]);
+                        for (int k = 0; k < 32; ++k) {
+                            if (!((ma >> k) & 1u)) xa[k] = -INFINITY;
+                            if (!((mb >> k) & 1u)) xb[k] = -INFINITY;
+                        }
                     }
-                } else {
+                    // four independent chains
+                    float m4[4];
 #pragma unroll
-                    for (int k = 0; k < 32; ++k) mx = fmaxf(mx, x[k]);
+                    for (int c = 0; c < 4; ++c) m4[c] = fmaxf(xa[c], xb[c]);
+#pragma unroll
+                    for (int k = 4; k < 32; ++k) m4[k & 3] = fmaxf(m4[k & 3], fmaxf(xa[k], xb[k]));
+                    mx = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3]));
                 }
                 // exchanged in bf16 rounded up: both halves then use the same
                 // value, not below the true max (P stays <= 2^kRescaleLog2)
                 const __nv_bfloat16 mine = __float2bfloat16_ru(mx * kScaleLog2);
-                redm[(pb * 2 + half) * 128 + row] = mine;
-                mbar_arrive(&red_bar[pb]);
-                if (!__all_sync(0xffffffffu, mbar_wait(&red_bar[pb], (gi >> 1) & 1, p.err))) {
-                    ok = false;
-                    break;
-                }
-                mx = fmaxf(__bfloat162float(mine), __bfloat162float(redm[(pb * 2 + (half ^ 1)) * 128 + row]));
-                const bool raise = mx > m + kRescaleLog2;  // false while the row has no valid key
-                const float m_new = raise ? mx : m;
-                const float alpha = raise ? ex2_approx(m - m_new) : 1.f;
-                float rs = 0.f;
-                uint32_t pk[16];
-                if (m_new == -INFINITY) {
-#pragma unroll
-                    for (int k = 0; k < 16; ++k) pk[k] = 0u;
-                } else {
-                    const float nm = -m_new;
-#pragma unroll
-                    for (int k = 0; k < 16; ++k) {
-                        const float a0 = fmaf(x[2 * k], kScaleLog2, nm), a1 = fmaf(x[2 * k + 1], kScaleLog2, nm);
-                        const float e0 = ex2_approx(a0);
-                        const float e1 = ex2_approx(a1);
-                        rs += e0 + e1;
-                        pk[k] = pack_f16x2(e0, e1);
-                    }
-                }
-                // P buffer pb was last read by PV(gi-2); O is written by PV(gi-1),
-                // so an O rescale waits for that one too (never on a unit's first tile).
-                if (gi >= 2 && !__all_sync(0xffffffffu, mbar_wait(&p_empty[pb], ((gi - 2) >> 1) & 1, p.err))) {
-                    ok = false;
-                    break;
-                }
-                // a row without a valid key so far has O = 0 and l = 0: its
-                // first real maximum needs no rescale (alpha = 0 leaves l exact);
-                // local units' first tile (window edge) leaves many such rows
-                const bool rescale = i >= 1 && __any_sync(0xffffffffu, raise && m != -INFINITY);
-                if (rescale && !__all_sync(0xffffffffu, mbar_wait(&p_empty[pb ^ 1], ((gi - 1) >> 1) & 1, p.err))) {
+                redm[(b * 2 + half) * 128 + row] = mine;
+                tc_fence_before();
+                if (!named_bar_and(pair_bar, 64, w)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
+                mx = fmaxf(__bfloat162float(mine), __bfloat162float(redm[(b * 2 + (half ^ 1)) * 128 + row]));
+                const bool raise = mx > m + kRescaleLog2;  // false while the row has no valid key
+                const float m_new = raise ? mx : m;
+                const float alpha = raise ? ex2_approx(m - m_new) : 1.f;
+                // a row without a valid key so far has O = 0 and l = 0: its
+                // first real maximum needs no rescale (alpha = 0 leaves l exact);
+                // local units' first tile (window edge) leaves many such rows.
+                // O is written by PV(gi-1): a rescale waits for it.
+                const bool rescale = i >= 1 && __any_sync(0xffffffffu, raise && m != -INFINITY);
+                // P buffer b was last read by PV(gi - 2)
+                if ((gi >= 2 && !__all_sync(0xffffffffu, mbar_wait(&p_empty[b], ((gi - 2) >> 1) & 1, p.err))) ||
+                    (rescale && !__all_sync(0xffffffffu, mbar_wait(&p_empty[b ^ 1], ((gi - 1) >> 1) & 1, p.err)))) {
+                    fail = true;  // leaves at the next pair barrier
+                    continue;
+                }
                 if (rescale) {
+                    tc_fence_after();
 #pragma unroll 1
                     for (int cc = 0; cc < 4; ++cc) {
                         float o[32];
@@ -1600,37 +1602,48 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                         for (int k = 0; k < 32; ++k) o[k] *= alpha;
                         tmem_st32(ta, o);
                     }
-                    tc_wait_st();
                 }
-                l = l * alpha + rs;
+                float r4[4] = {0.f, 0.f, 0.f, 0.f};
+                const float nm = -m_new;
+                const bool none = m_new == -INFINITY;
+                // two chunks of 32 keys, each handed to the PV MMAs as soon
+                // as it is in TMEM (the O rescale above is ordered before it)
+#pragma unroll
+                for (int c = 0; c < 2; ++c) {
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) {
+                        const float a0 = fmaf(c ? xb[2 * k] : xa[2 * k], kScaleLog2, nm);
+                        const float a1 = fmaf(c ? xb[2 * k + 1] : xa[2 * k + 1], kScaleLog2, nm);
+                        const float e0 = none ? 0.f : ex2_approx(a0);
+                        const float e1 = none ? 0.f : ex2_approx(a1);
+                        r4[k & 3] += e0 + e1;
+                        pk[k] = pack_f16x2(e0, e1);
+                    }
+                    tmem_st16(pbuf + half * 32 + c * 16, pk);
+                    tc_wait_st();
+                    tc_fence_before();
+                    mbar_arrive(&p_full[2 * b + c]);
+                }
+                l = l * alpha + ((r4[0] + r4[1]) + (r4[2] + r4[3]));
                 m = m_new;
-                tmem_st16(lane_base + kTmemP + pb * 32 + half * 16, pk);
-                tc_wait_st();
-                tc_fence_before();
-                mbar_arrive(&p_full[pb]);
             }
             if (!ok) break;
             // ---- hand the unit to the epilogue warps: this half's row sum.
             // Stay at most one unit ahead of the epilogue: its barriers count
             // phases by parity, and it reads the sums before releasing O.
-            if (ukc >= 1 && !__all_sync(0xffffffffu, mbar_wait(o_free, (ukc - 1) & 1, p.err))) {
-                ok = false;
-                break;
+            if (fail || (ukc >= 1 && !__all_sync(0xffffffffu, mbar_wait(o_free, (ukc - 1) & 1, p.err)))) {
+                fail = true;  // leaves at the next unit's first pair barrier
+                continue;
             }
             reds[half * 128 + row] = l;  // read by the epilogue before it releases O
             if (half == 0) redmx[row] = m;
             mbar_arrive(fin_bar);
         }
+        if (fail) ok = false;
         if (!ok) *s_abort = 1;
     }
     tc_fence_before();
-    __syncthreads();
-    if (warp == kPfWarpTma && lane == 0 && *s_abort) {
-        // Let in-flight TMA copies land before the CTA's shared memory goes.
-        mbar_wait(q_smem, 0, nullptr);
-        for (int s = 0; s < kPfKStages; ++s) mbar_wait(&k_full[s], 0, nullptr);
-        for (int s = 0; s < kPfVStages; ++s) mbar_wait(&v_full[s], 0, nullptr);
-    }
     __syncthreads();
     if (warp == kPfWarpMma) {
         tc_fence_after();

@@ -123,13 +123,14 @@ static int make_map(CUtensorMap *m, const void *base, int rows, size_t plane_str
 }
 
 // The same fp16 planes viewed as 4-D {64 dims, rows, 4 dim-blocks, planes}:
-// one box of {64, box_rows, 4} lands in shared memory as [block][row][64
-// dims], each 128-byte row swizzled - the layout of the kernel's K/V stages.
+// one box of {64, box_rows, box_blocks} lands in shared memory as
+// [block][row][64 dims], each 128-byte row swizzled - the layout of the
+// prefill kernel's ring slots.
 static int make_map4(CUtensorMap *m, const void *base, int rows, size_t plane_stride_elems, int planes,
-                     int box_rows) {
+                     int box_rows, int box_blocks) {
     cuuint64_t dims[4] = {64, (cuuint64_t)rows, (cuuint64_t)(kHeadDim / 64), (cuuint64_t)planes};
     cuuint64_t strides[3] = {(cuuint64_t)kHeadDim * 2, 128, (cuuint64_t)plane_stride_elems * 2};
-    cuuint32_t box[4] = {64, (cuuint32_t)box_rows, (cuuint32_t)(kHeadDim / 64), 1};
+    cuuint32_t box[4] = {64, (cuuint32_t)box_rows, (cuuint32_t)box_blocks, 1};
     cuuint32_t estr[4] = {1, 1, 1, 1};
     CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void *>(base), dims, strides, box, estr,
                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -616,8 +617,9 @@ static int prefill_impl(gemma3_cuda_ctx *ctx, int layer, int seq, const float *Q
     const size_t plane = (size_t)ctx->st_rows * kHeadDim;
     const int q0 = qa - start_pos;  // first query token attended here
     if (int r = make_map(&tq, ctx->qst + (size_t)q0 * kHeadDim, Tq, (size_t)T * kHeadDim, kHeads)) return r;
-    if (int r = make_map4(&tk, ctx->kst, lrows, plane, kKvHeads, 64)) return r;
-    if (int r = make_map4(&tv, ctx->vst, lrows, plane, kKvHeads, 64)) return r;
+    // K: boxes of 128 keys x 2 dim-blocks; V: 64 keys x 4 dim-blocks (32 KB each)
+    if (int r = make_map4(&tk, ctx->kst, lrows, plane, kKvHeads, g3::kPfTK, 2)) return r;
+    if (int r = make_map4(&tv, ctx->vst, lrows, plane, kKvHeads, 64, 4)) return r;
     g3::PrefillParams p;
     p.out = out + (size_t)q0 * kHeads * kHeadDim;
     p.ml_out = ml ? ml + (size_t)q0 * kHeads : nullptr;
