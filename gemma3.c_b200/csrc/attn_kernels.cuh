@@ -1392,7 +1392,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                 float4 v[8];
 #pragma unroll
                 for (int k = 0; k < 8; ++k)
-                    v[k] = make_float4(o[4 * k] * inv, o[4 * k + 1] * inv, o[4 * k + 2] * inv, o[4 * k + 3] * inv);
+                {
+                    const float2 i2 = make_float2(inv, inv);
+                    const float2 lo = fmul2(make_float2(o[4 * k], o[4 * k + 1]), i2);
+                    const float2 hi = fmul2(make_float2(o[4 * k + 2], o[4 * k + 3]), i2);
+                    v[k] = make_float4(lo.x, lo.y, hi.x, hi.y);
+                }
                 // lane q8 of the group: v[k] = block k of row r8 + q8 -> block q8 of row r8 + k
 #pragma unroll
                 for (int m = 4; m >= 1; m >>= 1) {
@@ -1599,12 +1604,17 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                         tmem_ld32(ta, o);
                         tc_wait_ld();
 #pragma unroll
-                        for (int k = 0; k < 32; ++k) o[k] *= alpha;
+                        for (int k = 0; k < 32; k += 2) {
+                            const float2 r = fmul2(make_float2(o[k], o[k + 1]), make_float2(alpha, alpha));
+                            o[k] = r.x;
+                            o[k + 1] = r.y;
+                        }
                         tmem_st32(ta, o);
                     }
                 }
-                float r4[4] = {0.f, 0.f, 0.f, 0.f};
+                float2 r2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
                 const float nm = -m_new;
+                const float2 sc2 = make_float2(kScaleLog2, kScaleLog2), nm2 = make_float2(nm, nm);
                 const bool none = m_new == -INFINITY;
                 // two chunks of 32 keys, each handed to the PV MMAs as soon
                 // as it is in TMEM (the O rescale above is ordered before it)
@@ -1613,11 +1623,12 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     uint32_t pk[16];
 #pragma unroll
                     for (int k = 0; k < 16; ++k) {
-                        const float a0 = fmaf(c ? xb[2 * k] : xa[2 * k], kScaleLog2, nm);
-                        const float a1 = fmaf(c ? xb[2 * k + 1] : xa[2 * k + 1], kScaleLog2, nm);
-                        const float e0 = none ? 0.f : ex2_approx(a0);
-                        const float e1 = none ? 0.f : ex2_approx(a1);
-                        r4[k & 3] += e0 + e1;
+                        const float2 a = ffma2(c ? make_float2(xb[2 * k], xb[2 * k + 1])
+                                                   : make_float2(xa[2 * k], xa[2 * k + 1]),
+                                                 sc2, nm2);
+                        const float e0 = none ? 0.f : ex2_approx(a.x);
+                        const float e1 = none ? 0.f : ex2_approx(a.y);
+                        r2[k & 1] = fadd2(r2[k & 1], make_float2(e0, e1));
                         pk[k] = pack_f16x2(e0, e1);
                     }
                     tmem_st16(pbuf + half * 32 + c * 16, pk);
@@ -1625,7 +1636,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     tc_fence_before();
                     mbar_arrive(&p_full[2 * b + c]);
                 }
-                l = l * alpha + ((r4[0] + r4[1]) + (r4[2] + r4[3]));
+                l = l * alpha + ((r2[0].x + r2[1].x) + (r2[0].y + r2[1].y));
                 m = m_new;
             }
             if (!ok) break;
