@@ -1339,10 +1339,10 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     } else if (warp >= kPfWarpEpi) {
         // ------------------------------------------------ epilogue warps
         // O / (l_half0 + l_half1) -> out[t][2g+hh][:], one warp per TMEM lane
-        // quadrant, thread = row.  Per 32-column chunk, each group of 8
-        // lanes transposes its 8 rows x 8 float4 blocks with three xor-
-        // shuffle stages, so that a store instruction writes 4 rows x 128
-        // contiguous bytes (4 L1 wavefronts) instead of 32 rows x 16 bytes
+        // quadrant, thread = row.  Per 32-column chunk, each group of 4
+        // lanes transposes its 4 rows x 4 blocks of 8 floats with two xor-
+        // shuffle stages, so that a store instruction writes 8 rows x 64
+        // contiguous bytes (8 L1 wavefronts) instead of 32 rows x 16 bytes
         // (32 wavefronts): all CTAs of a local layer finish their units
         // together, and the scattered form kept the LSU busy for ~8k cycles
         // per unit, stalling the softmax warps' TMEM loads.  O is released
@@ -1378,7 +1378,7 @@ __global__ void __launch_bounds__(kPfThreads, 1)
             const int nvalid = min(64, p.T - u.t0);
             if (p.ml_out && !piece && (row & 63) < nvalid)
                 p.ml_out[(size_t)(u.t0 + (row & 63)) * kHeads + 2 * u.g + (row >> 6)] = make_float2(redmx[row], lt);
-            const int q8 = lane & 7, r8 = quad * 32 + (lane & ~7);  // group's first row
+            const int q4 = lane & 3, r4 = quad * 32 + (lane & ~3);  // group's first row
 #pragma unroll 1
             for (int cc = 0; cc < 8; ++cc) {
                 float o[32];
@@ -1398,13 +1398,14 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     const float2 hi = fmul2(make_float2(o[4 * k + 2], o[4 * k + 3]), i2);
                     v[k] = make_float4(lo.x, lo.y, hi.x, hi.y);
                 }
-                // lane q8 of the group: v[k] = block k of row r8 + q8 -> block q8 of row r8 + k
+                // lane q4 of the group: blocks kb = (v[kb], v[kb + 4]) of row r4 + q4
+                // -> block q4 of row r4 + kb (cols 4 q4.. and 16 + 4 q4..)
 #pragma unroll
-                for (int m = 4; m >= 1; m >>= 1) {
-                    const bool up = (q8 & m) != 0;
+                for (int m = 2; m >= 1; m >>= 1) {
+                    const bool up = (q4 & m) != 0;
 #pragma unroll
                     for (int k0 = 0; k0 < 8; ++k0) {
-                        if (k0 & m) continue;
+                        if ((k0 & 3) & m) continue;
                         float4 &a = v[k0], &b = v[k0 | m];
                         const float4 snd = up ? a : b;
                         float4 rcv;
@@ -1416,12 +1417,13 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     }
                 }
 #pragma unroll
-                for (int k = 0; k < 8; ++k) {
-                    const int r = r8 + k;
+                for (int k = 0; k < 4; ++k) {
+                    const int r = r4 + k;
                     if (!piece && (r & 63) >= nvalid) continue;
                     float *rd = piece ? p.pscratch + ((size_t)u.slot * 128 + r) * kHeadDim
                                       : p.out + ((size_t)(u.t0 + (r & 63)) * kHeads + 2 * u.g + (r >> 6)) * kHeadDim;
-                    *reinterpret_cast<float4 *>(rd + cc * 32 + 4 * q8) = v[k];
+                    *reinterpret_cast<float4 *>(rd + cc * 32 + 4 * q4) = v[k];
+                    *reinterpret_cast<float4 *>(rd + cc * 32 + 16 + 4 * q4) = v[k + 4];
                 }
             }
             if (piece) {
