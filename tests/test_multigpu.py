@@ -9,6 +9,9 @@ partials are all-gathered and merged.
   * test_split_emulated_*    - one GPU: R contexts with kv_rank/kv_ranks set,
                                partial + merge through the C-ABI, against an
                                unsplit context;
+  * test_split_configs4_full_size_emulated - the same at configs[4]'s own
+                               size (B=4 x 131,072 keys), also against the
+                               reference;
   * test_split_nccl_2gpu     - two GPUs: NCCL all-gather, then the peer-memory exchange, inside
                                gemma3_cuda_attn_decode_dev (skipped with fewer).
 """
@@ -149,6 +152,82 @@ def test_split_emulated_one_gpu(R, kv):
         assert np.allclose(vd[p - owner * S], V[b].reshape(4, 256), atol=1e-2)
     for c in ctxs:
         c.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("R", [2, 4])
+def test_split_configs4_full_size_emulated(R):
+    """configs[4] at its own size: B=4 sequences, 131,072-key global layer
+    (new token at position 131071), BF16 cache, the KV range split over R
+    contexts on one GPU (partials + merge through the C-ABI).  Checked
+    against the unsplit context on all four sequences (<= 1e-3 x RMS) and
+    against the reference compiled from its own sources
+    (gemma3_transformer.c:294-352 driving gemma3_kernels.c:527-597) on two
+    of them (<= 1e-2 x RMS); the new row lands on the last rank only."""
+    import torch
+    import gemma3_cuda as gc
+    from oracles import best_oracle
+    layer, ctxlen, B = 5, 131072, 4
+    pos = [ctxlen - 1] * B
+    qn, kn = synth.qk_norm_gains(44)
+    ident = np.zeros((ctxlen, 128, 2), dtype=np.float32)
+    ident[..., 0] = 1.0
+    oracle = best_oracle()
+    rope_g = oracle.rope_table(ctxlen, 1e6)
+    Q, K, V = synth.normal(60, (B, 2048)), synth.normal(61, (B, 1024)), synth.normal(62, (B, 1024))
+
+    def setup(c):
+        c.upload_rope(ident, rope_g)
+        c.set_qk_norm(layer, qn, kn)
+
+    full = gc.Context(max_context=ctxlen, max_batch=B, kv_dtype=gc.KV_BF16, max_prefill=64, num_layers=6)
+    setup(full)
+    for s in range(B):
+        full.fill_cache_random(layer, s, ctxlen - 1, 9000 + s)
+    full.synchronize()
+    rows = [full.export_cache(layer, s) for s in range(B)]  # fp32 copies of the BF16 rows
+    want = full.attn_decode(layer, list(range(B)), pos, Q, K, V)
+    full.close()
+
+    q, k, v = (torch.from_numpy(a).cuda() for a in (Q, K, V))
+    parts = torch.empty(R, B, 8, 258, device="cuda")
+    S = -(-ctxlen // R)
+    ctxs = []
+    for r in range(R):
+        c = gc.Context(max_context=ctxlen, max_batch=B, kv_dtype=gc.KV_BF16, max_prefill=64, num_layers=6,
+                       kv_rank=r, kv_ranks=R)
+        setup(c)
+        lo, hi = r * S, min(ctxlen - 1, (r + 1) * S)
+        for s in range(B):
+            c.import_cache(layer, s, rows[s][0][lo:hi], rows[s][1][lo:hi])
+        c.attn_decode_partial_dev(layer, list(range(B)), pos, q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                  parts[r].data_ptr())
+        c.synchronize()
+        ctxs.append(c)
+    out = torch.empty(B, 2048, device="cuda")
+    ctxs[0].merge_partials_dev(R, B, parts.data_ptr(), out.data_ptr())
+    ctxs[0].synchronize()
+    got = out.cpu().numpy()
+    assert np.isfinite(got).all()
+    assert rel_err(got, want) <= 1e-3
+    # the new token's row (position 131071) belongs to the last rank
+    kd, vd = ctxs[R - 1].export_cache(layer, 0)
+    assert np.array_equal(vd[pos[0] - (R - 1) * S], oracle_bf16(V[0]).reshape(4, 256))
+    for c in ctxs:
+        c.close()
+    for s in (0, B - 1):
+        cache = oracle.new_cache(True, ctxlen)
+        kr, vr = oracle.cache_arrays(cache)
+        kr[:ctxlen - 1] = rows[s][0][:ctxlen - 1]
+        vr[:ctxlen - 1] = rows[s][1][:ctxlen - 1]
+        ref = oracle.attn_core_tokens(cache, Q[None, s], K[None, s], V[None, s], qn, kn, rope_g, pos[s])
+        oracle.free_cache(cache)
+        assert rel_err(got[s], ref[0]) <= 1e-2, s
+
+
+def oracle_bf16(x):
+    from oracles import bf16_round
+    return bf16_round(np.asarray(x, dtype=np.float32))
 
 
 NCCL_CHILD = r'''
