@@ -266,6 +266,40 @@ def test_prefill_8192_many_units_per_cta(ropes, layer):
     assert rel_err(got, want) <= TOL, rel_err(got, want)
 
 
+@pytest.mark.parametrize("layer", [0, 5])
+def test_prefill_8192_against_reference(oracle, ropes, layer):
+    """configs[2]'s prompt length on one layer, T=8192 from position 0, the
+    reference's fp32 cache: the whole prompt against the reference compiled
+    from its own sources (its per-token prefill attention,
+    gemma3_transformer.c:641-692 over gemma3_gqa, gemma3_kernels.c:527-597),
+    every output row within TOL x RMS, and the cache rows as the reference
+    stores them."""
+    T = 8192
+    glob = gc.is_global_layer(layer)
+    rope = ropes[1] if glob else ropes[0]
+    qn, kn = synth.qk_norm_gains(700 + layer)
+    Q, K, V = qkv(9100 + layer, T)
+    c = oracle.new_cache(glob, T)
+    want = oracle.attn_core_tokens(c, Q, K, V, qn, kn, rope, 0)
+    ctx = make_ctx(ropes, gc.KV_F32, max_context=T, max_prefill=T)
+    ctx.set_qk_norm(layer, qn, kn)
+    got = ctx.attn_prefill(layer, 0, Q, K, V, 0)
+    assert np.isfinite(got).all()
+    assert rel_err(got, want) <= TOL, rel_err(got, want)
+    kr, vr = oracle.cache_arrays(c)
+    kd, vd = ctx.export_cache(layer, 0)
+    rows = kd.shape[0]
+    if glob:
+        assert np.array_equal(vd[:rows], vr[:rows])
+        assert rel_err(kd[:rows], kr[:rows]) < 1e-5
+    else:
+        # the ring holds the last 1024 positions, at slot pos % 1024, on both sides
+        assert np.array_equal(vd, vr[:rows])
+        assert rel_err(kd, kr[:rows]) < 1e-5
+    oracle.free_cache(c)
+    ctx.close()
+
+
 def test_bounded_wait_times_out_and_context_survives(ropes):
     """A device wait that can never complete gives up after its limit, the
     call reports GENERATION_FAILED with the timeout text, and the same
