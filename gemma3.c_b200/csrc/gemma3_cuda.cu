@@ -1115,8 +1115,11 @@ static int make_map_f16(CUtensorMap *m, const void *base, int rows, int cols, in
 }
 
 // Y[T][N] = X[T][K] . W[N][K]^T, routed by `out`.  xb: fp16 [T][K] (device).
+// deferred: null, or where a caller that sums the split-K partials itself
+// (residual_norm_rows) gets their count: 0 = the output is in `out` (one
+// split), S > 1 = S partial sums [S][T][N] in ctx->pp, no reduce launched.
 static int proj_run(gemma3_cuda_ctx *ctx, const __half *W, int N, int K, const __half *xb, int T,
-                    const g3::ProjOut &out) {
+                    const g3::ProjOut &out, int *deferred = nullptr) {
     const int nt = std::min(256, (T + 31) / 32 * 32);  // the epilogue reads 32 tokens per tcgen05.ld
     const int ntile_tok = (T + nt - 1) / nt;
     const int mtiles = N / 128, kchunks = K / 64;
@@ -1166,7 +1169,8 @@ static int proj_run(gemma3_cuda_ctx *ctx, const __half *W, int N, int K, const _
     prof_begin(ctx, &e0);
     CU_TRY(launch_pdl(g3::proj_gemm_sm100, dim3(grid), dim3(g3::kProjThreads), g3::kProjSmem, ctx->stream, tw, tx, p));
     if (int r = check_launch(ctx, 1)) return r;
-    if (splits > 1) {
+    if (deferred) *deferred = splits > 1 ? splits : 0;
+    if (splits > 1 && !deferred) {
         const size_t n = (size_t)T * N;
         const int blocks = (int)std::min<size_t>((n + 255) / 256, (size_t)ctx->sm_count * 8);
         CU_TRY(launch_pdl(g3::proj_splitk_reduce, dim3(blocks), dim3(256), 0, ctx->stream, (const float *)ctx->pp,
@@ -1387,10 +1391,14 @@ static int forward_layers(gemma3_cuda_ctx *ctx, int T, float *x, AttnFn attn) {
         o.ld[0] = o.ld[1] = o.ld[2] = kHidden;
         o.lo[0] = 0;
         o.lo[1] = o.lo[2] = o.lo[3] = kHidden;
-        if (int r = proj_run(ctx, L.wo, kHidden, kQSize, ctx->ab, T, o)) return r;
+        // the split-K partials of O and down are summed by residual_norm_rows
+        // (in split order, as the reduce kernel would), one launch fewer each
+        int ds = 0;
+        if (int r = proj_run(ctx, L.wo, kHidden, kQSize, ctx->ab, T, o, &ds)) return r;
         // x += post_attn_norm(o_proj); xn = pre_ffn_norm(x)
         CU_TRY(launch_pdl(g3::residual_norm_rows, dim3(T), dim3(g3::kNormThreads), 0, ctx->stream,
-                          (const float *)ctx->delta, ln_of(L, 1), x, ln_of(L, 2), ctx->xb, eps, ctx->err));
+                          (const float *)(ds ? ctx->pp : ctx->delta), ds ? ds : 1, (size_t)T * kHidden, ln_of(L, 1),
+                          x, ln_of(L, 2), ctx->xb, eps, ctx->err));
         if (int r = check_launch(ctx, 1)) return r;
         o.ptr[0] = gate;
         o.ptr[1] = o.ptr[2] = up;
@@ -1411,11 +1419,11 @@ static int forward_layers(gemma3_cuda_ctx *ctx, int T, float *x, AttnFn attn) {
         o.ld[0] = o.ld[1] = o.ld[2] = kHidden;
         o.lo[0] = 0;
         o.lo[1] = o.lo[2] = o.lo[3] = kHidden;
-        if (int r = proj_run(ctx, L.wdown, kHidden, kInter, ctx->hb, T, o)) return r;
+        if (int r = proj_run(ctx, L.wdown, kHidden, kInter, ctx->hb, T, o, &ds)) return r;
         // x += post_ffn_norm(mlp); xn = next layer's pre-attention norm(x)
         const bool last = l + 1 == ctx->cfg.num_layers;
         CU_TRY(launch_pdl(g3::residual_norm_rows, dim3(T), dim3(g3::kNormThreads), 0, ctx->stream,
-                          (const float *)ctx->delta, ln_of(L, 3), x,
+                          (const float *)(ds ? ctx->pp : ctx->delta), ds ? ds : 1, (size_t)T * kHidden, ln_of(L, 3), x,
                           last ? (const uint16_t *)nullptr : ln_of(ctx->layers[l + 1], 0),
                           last ? (__half *)nullptr : ctx->xb, eps, ctx->err));
         if (int r = check_launch(ctx, 1)) return r;

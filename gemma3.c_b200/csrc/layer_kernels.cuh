@@ -69,12 +69,15 @@ __global__ void __launch_bounds__(kNormThreads) rms_norm_rows_f16(const float *_
 }
 
 // One residual step of the block, per row:
+//     delta = sum of the nparts partial sums delta + s * part_stride, in order
+//             (the split-K partials of the projection before it)
 //     d = w_post ? rmsnorm(delta, w_post) : delta;  x += d;
 //     if (xn) xn = (w_pre ? rmsnorm(x, w_pre) : x) in fp16
 // i.e. the post-attention (post-feed-forward) norm, the residual add, and the
 // pre-feed-forward (next layer's pre-attention) norm of
 // gemma3_transformer.c:463-468, :472-478, :491-498 and :436-437.
-__global__ void __launch_bounds__(kNormThreads) residual_norm_rows(const float *__restrict__ delta,
+__global__ void __launch_bounds__(kNormThreads) residual_norm_rows(const float *__restrict__ delta, int nparts,
+                                                                   size_t part_stride,
                                                                    const uint16_t *__restrict__ w_post,
                                                                    float *__restrict__ x,
                                                                    const uint16_t *__restrict__ w_pre,
@@ -86,6 +89,11 @@ __global__ void __launch_bounds__(kNormThreads) residual_norm_rows(const float *
     float d[kNormPer];
 #pragma unroll
     for (int i = 0; i < kNormPer; ++i) d[i] = delta[base + threadIdx.x + i * kNormThreads];
+    for (int s = 1; s < nparts; ++s) {
+        const float *ds = delta + (size_t)s * part_stride;
+#pragma unroll
+        for (int i = 0; i < kNormPer; ++i) d[i] += ds[base + threadIdx.x + i * kNormThreads];
+    }
     if (w_post) rms_apply(d, w_post, eps, red);
 #pragma unroll
     for (int i = 0; i < kNormPer; ++i) {
