@@ -1615,9 +1615,11 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                     }
                 }
                 float2 r2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-                const float nm = -m_new;
+                // a row with no valid key so far (m_new = -inf) gets P = 0: with the
+                // subtracted reference at -inf every exponent is -inf, so no
+                // per-element select is needed
+                const float nm = m_new == -INFINITY ? -INFINITY : -m_new;
                 const float2 sc2 = make_float2(kScaleLog2, kScaleLog2), nm2 = make_float2(nm, nm);
-                const bool none = m_new == -INFINITY;
                 // two chunks of 32 keys, each handed to the PV MMAs as soon
                 // as it is in TMEM (the O rescale above is ordered before it)
 #pragma unroll
@@ -1628,8 +1630,8 @@ __global__ void __launch_bounds__(kPfThreads, 1)
                         const float2 a = ffma2(c ? make_float2(xb[2 * k], xb[2 * k + 1])
                                                    : make_float2(xa[2 * k], xa[2 * k + 1]),
                                                  sc2, nm2);
-                        const float e0 = none ? 0.f : ex2_approx(a.x);
-                        const float e1 = none ? 0.f : ex2_approx(a.y);
+                        const float e0 = ex2_approx(a.x);
+                        const float e1 = ex2_approx(a.y);
                         r2[k & 1] = fadd2(r2[k & 1], make_float2(e0, e1));
                         pk[k] = pack_f16x2(e0, e1);
                     }
