@@ -75,18 +75,54 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi sampler (200 ms) for the GPU this rank uses, during the timed region."""
+    """Clock / throttle-reason sampler for the GPU this rank uses, during the
+    timed region: NVML read every 10 ms from a thread (a timed region of
+    tens of ms then still yields several samples), else nvidia-smi every
+    200 ms.  Reads only; no GPU setting is changed."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits
+    REASON_BITS = (("sw_power_cap", 0x4), ("hw_slowdown", 0x8), ("sw_thermal_slowdown", 0x20),
+                   ("hw_thermal_slowdown", 0x40))
 
     def __init__(self, gpu_index):
         self.idx = gpu_index
-        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.f = None
         self.p = None
+        self.nv = None
+        self.rows = []
+
+    def _nvml_loop(self):
+        nv, h = self.nv, self.h
+        while not self.stop.is_set():
+            try:
+                self.rows.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM),
+                                  nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM),
+                                  nv.nvmlDeviceGetCurrentClocksEventReasons(h)))
+            except Exception:
+                break
+            self.stop.wait(0.01)
 
     def __enter__(self):
+        try:
+            import threading
+            import pynvml
+            pynvml.nvmlInit()
+            # the GPU of this CUDA ordinal, matched by UUID (NVML numbers every
+            # GPU of the box, whatever CUDA_VISIBLE_DEVICES exposes)
+            import torch
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(self.idx).uuid)
+            self.h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            self.nv = pynvml
+            self.stop = threading.Event()
+            self.t = threading.Thread(target=self._nvml_loop, daemon=True)
+            self.t.start()
+            return self
+        except Exception:
+            self.nv = None
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
         try:
             self.p = subprocess.Popen(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
                                        "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.f,
@@ -97,21 +133,28 @@ class Clocks:
         return self
 
     def __exit__(self, *a):
+        if self.nv:
+            self.stop.set()
+            self.t.join()
         if self.p:
             self.p.terminate()
             self.p.wait()
 
     def summary(self):
+        if self.nv:
+            rows = self.rows
+            if not rows:
+                return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["NVML returned no sample"], "samples": 0}
+            reasons = {name for _, _, r in rows for name, bit in self.REASON_BITS if r & bit}
+            return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                    "reasons": sorted(reasons), "samples": len(rows), "source": "NVML, 10 ms"}
         self.f.flush()
         rows = []
         for line in open(self.f.name):
             parts = [x.strip() for x in line.split(",")]
             if len(parts) < 9:
                 continue
-            try:
-                rows.append(parts)
-            except ValueError:
-                pass
+            rows.append(parts)
         os.unlink(self.f.name)
         if not rows:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
@@ -124,7 +167,7 @@ class Clocks:
                 if v.lower() == "active":
                     reasons.add(name)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(rows)}
+                "reasons": sorted(reasons), "samples": len(rows), "source": "nvidia-smi, 200 ms"}
 
 
 class Dist:
