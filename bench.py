@@ -136,6 +136,10 @@ class Clocks:
         if self.nv:
             self.stop.set()
             self.t.join()
+            try:
+                self.nv.nvmlShutdown()
+            except Exception:
+                pass
         if self.p:
             self.p.terminate()
             self.p.wait()

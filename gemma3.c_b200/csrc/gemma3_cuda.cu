@@ -432,6 +432,10 @@ static int ctx_alloc(gemma3_cuda_ctx *c) {
             if (int r = make_map_kv(&L.tm_kv, L.kv, L.rows, k.max_batch * 2 * kKvHeads)) return r;
         CU_TRY(cudaFuncSetAttribute(g3::decode_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, g3::kTcSmem));
         CU_TRY(cudaFuncSetAttribute(g3::decode_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, g3::kTcSmem));
+        CU_TRY(cudaFuncSetAttribute(g3::decode_tc<true, g3::DecodeRowsSmall>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, g3::kTcSmem));
+        CU_TRY(cudaFuncSetAttribute(g3::decode_tc<false, g3::DecodeRowsSmall>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, g3::kTcSmem));
         CU_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&c->dec_ctas_per_sm, g3::decode_tc<false>,
                                                              g3::kTcThreads, g3::kTcSmem));
         if (c->dec_ctas_per_sm < 1)
@@ -902,6 +906,13 @@ static int decode_impl(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_id
     p.partial = ctx->partial;
     p.out = out;
     p.write_partial = (pl.nsplit > 1 || partial_out) ? 1 : 0;
+    {
+        // L2 prefetch before the launch wait only when the call's cache rows
+        // fit L2 with room to spare (B = 1 x 8192 rows: 33.5 MB)
+        double rows = 0;
+        for (int b = 0; b < B; ++b) rows += pl.rows.nrows[b];
+        p.l2_prefetch = fused && rows * kKvHeads * 2.0 * kHeadDim * sizeof(KVT) <= 48e6 ? 1 : 0;
+    }
     p.err = ctx->err;
     const int smem = g3::DecodeCfg<KVT>::NS * 2 * g3::DecodeCfg<KVT>::TK * kHeadDim * sizeof(KVT) +
                      (fused ? g3::kFusedExtra<KVT> : 0);
@@ -911,10 +922,25 @@ static int decode_impl(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_id
     if constexpr (std::is_same<KVT, __nv_bfloat16>::value) {
         // BF16 cache: both contractions on the tensor core
         const CUtensorMap &tm = ctx->layers[layer].tm_kv;
-        if (fused)
+        if (B <= g3::kSmallDecodeBatch) {
+            g3::DecodeRowsSmall rs;
+            rs.B = B;
+            for (int b = 0; b < B; ++b) {
+                rs.seq[b] = pl.rows.seq[b];
+                rs.nrows[b] = pl.rows.nrows[b];
+                rs.pos[b] = pl.rows.pos[b];
+            }
+            if (fused)
+                launch_pdl(g3::decode_tc<true, g3::DecodeRowsSmall>, grid, dim3(g3::kTcThreads), g3::kTcSmem,
+                           ctx->stream, tm, p, rs);
+            else
+                launch_pdl(g3::decode_tc<false, g3::DecodeRowsSmall>, grid, dim3(g3::kTcThreads), g3::kTcSmem,
+                           ctx->stream, tm, p, rs);
+        } else if (fused) {
             launch_pdl(g3::decode_tc<true>, grid, dim3(g3::kTcThreads), g3::kTcSmem, ctx->stream, tm, p, pl.rows);
-        else
+        } else {
             launch_pdl(g3::decode_tc<false>, grid, dim3(g3::kTcThreads), g3::kTcSmem, ctx->stream, tm, p, pl.rows);
+        }
     } else if (fused) {
         launch_pdl(g3::decode_splitkv<KVT, true>, grid, dim3(256), smem, ctx->stream, p, pl.rows);
     } else {
