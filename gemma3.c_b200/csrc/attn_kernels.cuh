@@ -270,8 +270,6 @@ struct DecodeParams {
     float *partial;        // [B][8][nsplit][258] when write_partial
     float *out;            // [B][2048] when !write_partial
     int write_partial;
-    int l2_prefetch;       // decode_tc fused form: prefetch the CTA's rows into L2 before the
-                           //   programmatic-launch wait (set for calls that fit L2 with room)
     unsigned *err;
 };
 template <int kRows>

@@ -97,62 +97,54 @@ __device__ __forceinline__ uint16_t bf16_bits(float x) {
 }
 
 // Log-sum-exp merge of n partials [m, l, O[256]] of the two heads of group
-// g by 128 threads: thread t takes head t / 64, dims 4 (t % 64) .. + 3, read
-// as two 8-byte pairs (the 258-float partial rows are 8-byte aligned).  One
-// online pass over the partials (read through L2: other CTAs wrote them), 16
-// partials of both heads per batch.
+// g by 128 threads: thread t writes dims t and t + 128 of both heads.  One
+// online pass over the partials (read through L2: other CTAs wrote them),
+// 16 partials (48 loads) in flight per thread and head.
 __device__ __forceinline__ void tc_merge_group(const float *base, size_t hstride, int n, float *out_g) {
     constexpr int C = 16;
     const int t = threadIdx.x;
-    const int hh = t >> 6, d = 4 * (t & 63);
-    const float *bh = base + hh * hstride;
-    float Mx = -INFINITY, Lt = 0.f;
-    float4 A = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 1
-    for (int i0 = 0; i0 < n; i0 += C) {
-        float2 ml[C], o0[C], o1[C];
+    for (int hh = 0; hh < 2; ++hh) {
+        const float *bh = base + hh * hstride;
+        float Mx = -INFINITY, Lt = 0.f, At = 0.f, Bt = 0.f;
+#pragma unroll 1
+        for (int i0 = 0; i0 < n; i0 += C) {
+            float2 ml[C];
+            float oa[C], ob[C];
 #pragma unroll
-        for (int j = 0; j < C; ++j) {
-            if (i0 + j < n) {
-                const float *pp = bh + (size_t)(i0 + j) * (kHeadDim + 2);
-                ml[j] = __ldcg(reinterpret_cast<const float2 *>(pp));
-                o0[j] = __ldcg(reinterpret_cast<const float2 *>(pp + 2 + d));
-                o1[j] = __ldcg(reinterpret_cast<const float2 *>(pp + 4 + d));
-            } else {
-                ml[j] = make_float2(-INFINITY, 0.f);
-                o0[j] = o1[j] = make_float2(0.f, 0.f);
+            for (int j = 0; j < C; ++j) {
+                if (i0 + j < n) {
+                    const float *pp = bh + (size_t)(i0 + j) * (kHeadDim + 2);
+                    ml[j] = __ldcg(reinterpret_cast<const float2 *>(pp));
+                    oa[j] = __ldcg(pp + 2 + t);
+                    ob[j] = __ldcg(pp + 2 + 128 + t);
+                } else {
+                    ml[j] = make_float2(-INFINITY, 0.f);
+                    oa[j] = ob[j] = 0.f;
+                }
             }
-        }
-        float cm = Mx;
+            float cm = Mx;
 #pragma unroll
-        for (int j = 0; j < C; ++j) cm = fmaxf(cm, ml[j].x);
-        if (cm == -INFINITY) continue;  // no rows so far
-        const float sc = Mx == -INFINITY ? 0.f : ex2_approx(Mx - cm);
-        Lt *= sc;
-        A.x *= sc;
-        A.y *= sc;
-        A.z *= sc;
-        A.w *= sc;
+            for (int j = 0; j < C; ++j) cm = fmaxf(cm, ml[j].x);
+            if (cm == -INFINITY) continue;  // no rows so far
+            const float sc = Mx == -INFINITY ? 0.f : ex2_approx(Mx - cm);
+            Lt *= sc;
+            At *= sc;
+            Bt *= sc;
 #pragma unroll
-        for (int j = 0; j < C; ++j) {
-            const float f = ml[j].x == -INFINITY ? 0.f : ex2_approx(ml[j].x - cm);
-            Lt += ml[j].y * f;
-            A.x += o0[j].x * f;
-            A.y += o0[j].y * f;
-            A.z += o1[j].x * f;
-            A.w += o1[j].y * f;
+            for (int j = 0; j < C; ++j) {
+                const float f = ml[j].x == -INFINITY ? 0.f : ex2_approx(ml[j].x - cm);
+                Lt += ml[j].y * f;
+                At += oa[j] * f;
+                Bt += ob[j] * f;
+            }
+            Mx = cm;
         }
-        Mx = cm;
+        const float inv = Lt > 0.f ? 1.0f / Lt : 0.f;
+        out_g[hh * kHeadDim + t] = At * inv;
+        out_g[hh * kHeadDim + 128 + t] = Bt * inv;
     }
-    const float inv = Lt > 0.f ? 1.0f / Lt : 0.f;
-    // scalar stores: out may be a caller's page-locked buffer, only 4-byte aligned
-    float *o = out_g + hh * kHeadDim + d;
-    o[0] = A.x * inv;
-    o[1] = A.y * inv;
-    o[2] = A.z * inv;
-    o[3] = A.w * inv;
 }
-
 
 template <bool kFused, typename Rows = DecodeRows>
 __global__ void __launch_bounds__(kTcThreads, 2)
@@ -211,17 +203,6 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         fence_mbar_init();
     }
     if (warp == 5) tmem_alloc(&tmem_slot, kTcTmemCols);
-    // Short-range (fused) calls that fit L2: pull this CTA's K/V rows into L2 before
-    // waiting for the previous kernel of the stream.  Under programmatic
-    // launch the CTAs start while that kernel still runs, and the rows a
-    // call streams are not its outputs; L2 is the coherence point, so a row
-    // an earlier kernel writes afterwards is updated there, never served
-    // stale.  The copies into shared memory start only after the wait.
-    if (kFused && p.l2_prefetch && warp == 4 && lane == 0 && ntiles > 0) {
-        prefetch_tmap(&tmKV);
-        for (int q = 0; q < 8 * ntiles; ++q)
-            tma_prefetch_4d(&tmKV, 0, r0 + (q >> 3) * kTcTK, q & 3, (q & 7) < 4 ? plane_k : plane_v);
-    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();

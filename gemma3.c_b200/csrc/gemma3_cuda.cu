@@ -906,13 +906,6 @@ static int decode_impl(gemma3_cuda_ctx *ctx, int layer, int B, const int *seq_id
     p.partial = ctx->partial;
     p.out = out;
     p.write_partial = (pl.nsplit > 1 || partial_out) ? 1 : 0;
-    {
-        // L2 prefetch before the launch wait only when the call's cache rows
-        // fit L2 with room to spare (B = 1 x 8192 rows: 33.5 MB)
-        double rows = 0;
-        for (int b = 0; b < B; ++b) rows += pl.rows.nrows[b];
-        p.l2_prefetch = fused && rows * kKvHeads * 2.0 * kHeadDim * sizeof(KVT) <= 48e6 ? 1 : 0;
-    }
     p.err = ctx->err;
     const int smem = g3::DecodeCfg<KVT>::NS * 2 * g3::DecodeCfg<KVT>::TK * kHeadDim * sizeof(KVT) +
                      (fused ? g3::kFusedExtra<KVT> : 0);

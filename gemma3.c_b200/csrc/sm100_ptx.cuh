@@ -146,13 +146,6 @@ __device__ __forceinline__ void tma_prefetch_2d(const CUtensorMap *map, int x, i
                  "r"(x), "r"(y)
                  : "memory");
 }
-// Prefetch a 4-D tile into L2 (no shared memory, no completion signal).
-__device__ __forceinline__ void tma_prefetch_4d(const CUtensorMap *map, int x, int y, int z, int w) {
-    asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
-                     reinterpret_cast<uint64_t>(map)),
-                 "r"(x), "r"(y), "r"(z), "r"(w)
-                 : "memory");
-}
 // 4-D tiled tensor load (no multicast); x is 0 here (128-byte aligned).
 __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, int x, int y, int z, int w,
                                             uint64_t *bar) {
